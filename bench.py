@@ -1,0 +1,343 @@
+"""Benchmark of the cuda_kda hot path: chunkwise KDA forward + VJP, B8 H12 T1568 d64 bf16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one kda_fwd (saving the per-chunk states) + one kda_bwd over one batch of seeded
+synthetic inputs with BASELINE config 2's shapes and distributions (q, k L2-normalised
+N(0,1); v N(0,1); beta sigmoid(N(0,1)); g -softplus(N(0,1)) float32; S0 N(0, 0.1^2);
+dO N(0,1) bf16; dS_T N(0,1)).  Scaling is weak: each rank owns its own (b, h) shard of a
+global batch of 8*N sequences x 12 heads, so per-GPU work is fixed; nothing crosses GPUs
+inside the op.  ``value`` = tokens (B*T over all ranks) / max-over-ranks device time.
+
+``--impl reference`` times the CPU restatement of the reference's ``compiled`` path
+(the oracle port: MLX cannot run here) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, H, T, D, CHUNK = 8, 12, 1568, 64, 64
+METRIC = "KDA fwd+bwd tokens/sec/GPU (B8 H12 T1568 d64 bf16) and % of roofline"
+UNIT = "tokens/s"
+# algorithmic (compulsory) HBM bytes per call, SURVEY §8(d) accounting
+FWD_BYTES = 119_052_288
+BWD_BYTES = 217_264_128
+FLOPS_FWD_PER_TOKHEAD = 40_960
+FLOPS_FWDBWD_PER_TOKHEAD = 139_264
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------
+# CPU reference arm (oracle port of the reference's `compiled` path + its step backward)
+# ---------------------------------------------------------------------------------------
+def _cpu_pair(args):
+    seed, pair = args
+    import numpy as np
+    from mlx_vit_b200.synthetic import make_inputs
+    from oracle import kda_oracle as O
+    inp = make_inputs(1, T, 1, D, seed=seed * 1000 + pair, state_std=0.1)
+    for k in ("q", "k", "v", "beta", "do"):  # bf16-rounded operands, as the GPU sees them
+        a = inp[k].astype(np.float32)
+        inp[k] = (a.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+    O.compiled_forward(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], inp["state"])
+    O.step_backward(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], inp["state"],
+                    inp["do"], inp["dst"])
+    return pair
+
+
+def cpu_reference(steps: int, warmup: int):
+    """Times the oracle on (b, h) sequences of the config, one sequence per worker process
+    (single-threaded BLAS each), all host cores.  Returns (tokens/s, cores, sample, secs)."""
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    workers = max(1, min(cores, B * H))
+    pairs = B * H if workers >= 16 else min(B * H, 2 * workers)
+    env_keys = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
+    old = {k: os.environ.get(k) for k in env_keys}
+    for k in env_keys:
+        os.environ[k] = "1"
+    try:
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(workers) as pool:
+            for i in range(warmup):
+                pool.map(_cpu_pair, [(i, p) for p in range(min(pairs, workers))])
+            times = []
+            for s in range(steps):
+                t0 = time.perf_counter()
+                pool.map(_cpu_pair, [(100 + s, p) for p in range(pairs)])
+                times.append(time.perf_counter() - t0)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    tok = pairs * T / H  # tokens (each token covers H heads)
+    tsec = statistics.median(times)
+    sample = (f"{pairs} of the {B * H} (b,h) sequences of B8 H12 T1568 d64 (bf16-rounded "
+              f"inputs, fp32 numpy), fwd (compiled-path restatement) + step-backward VJP, "
+              f"{workers} worker processes x 1 BLAS thread, median of {steps}")
+    return tok / tsec, workers, sample, tsec
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampler
+# ---------------------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc or not self.f:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from mlx_vit_b200 import _lib, cuda_kda, kda_forward, kda_backward
+    from mlx_vit_b200.synthetic import make_inputs_torch
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    dt = torch.bfloat16
+    inp = make_inputs_torch(B, T, H, D, seed=1234 + rank, device=dev, dtype=dt, state_std=0.1)
+    q, k, v, g, beta, S0, do, dst = (inp[n] for n in ("q", "k", "v", "g", "beta", "state", "do", "dst"))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    def step():
+        o, S_T, cs = kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=True)
+        ev_mid.record()
+        kda_backward(q, k, v, g, beta, S0, cs, do, dst, CHUNK)
+
+    for _ in range(args.warmup):
+        ev_mid = torch.cuda.Event(enable_timing=True)
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n0 = L.kda_launch_counter()
+    fwd_ms, bwd_ms = [], []
+    with Clocks(local_rank) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev_mid = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            step()
+            ev1.record()
+            ev1.synchronize()
+            fwd_ms.append(ev0.elapsed_time(ev_mid))
+            bwd_ms.append(ev_mid.elapsed_time(ev1))
+        torch.cuda.synchronize()
+    launches = L.kda_launch_counter() - n0
+    total_ms = sum(fwd_ms) + sum(bwd_ms)
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    tokens = B * T * world * args.steps
+    value = tokens / (total_ms / 1e3)
+
+    # ---- e2e through the public API with host buffers (pinned), copies inside timing ----
+    host = {n: x.cpu().pin_memory() for n, x in inp.items()}
+    h2d = sum(x.numel() * x.element_size() for x in host.values())
+    outs_host = None
+
+    def e2e_step():
+        nonlocal outs_host
+        d = {n: x.to(dev, non_blocking=True) for n, x in host.items()}
+        leaves = {n: d[n].requires_grad_(True) for n in ("q", "k", "v", "g", "beta", "state")}
+        o, S_T = cuda_kda(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"],
+                          leaves["state"], chunk_size=CHUNK)
+        torch.autograd.backward([o, S_T], [d["do"], d["dst"]])
+        res = [o, S_T] + [leaves[n].grad for n in ("q", "k", "v", "g", "beta", "state")]
+        if outs_host is None:
+            outs_host = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for hdst, r in zip(outs_host, res):
+            hdst.copy_(r.detach(), non_blocking=True)
+        return sum(r.numel() * r.element_size() for r in res)
+
+    for _ in range(max(1, args.warmup)):
+        d2h = e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = tokens / (float(te.item()) / 1e3)
+
+    if rank != 0:
+        return None
+    hbm, tfl, src = peaks()
+    fwd_avg, bwd_avg = statistics.mean(fwd_ms), statistics.mean(bwd_ms)
+    # dominant kernel: the longer of the two calls (each call is one kernel launch today)
+    if bwd_avg >= fwd_avg:
+        dom, dom_ms, dom_bytes = "kda_bwd", bwd_avg, BWD_BYTES
+    else:
+        dom, dom_ms, dom_bytes = "kda_fwd", fwd_avg, FWD_BYTES
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    whole = (FWD_BYTES + BWD_BYTES) / (ms_per_step / 1e3) / 1e9
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config-2 distributions)",
+        "config": {"workload": "cfg2: chunkwise KDA fwd+VJP, B8 H12 T1568 dk=dv=64 chunk64, bf16 "
+                               "I/O, fp32 g/state, per GPU", "B_per_gpu": B, "global_batch": B * world,
+                   "H": H, "T": T, "D": D, "chunk": CHUNK, "parallelism": f"bxh-shard x{world}",
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "per_gpu_tokens_per_s": round(value / world, 1),
+        "fwd_ms": round(fwd_avg, 4), "bwd_ms": round(bwd_avg, 4),
+        "hbm_frac_whole_step": round(whole / hbm, 4),
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "algorithmic_bytes_per_launch": dom_bytes,
+                     "traffic": None},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "path": "mlx_vit_b200.cuda_kda autograd fwd+bwd from pinned host buffers, all "
+                        "outputs and gradients copied back"},
+    }
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        try:
+            with open(tf) as f:
+                line["roofline"]["traffic"] = json.load(f).get(dom)
+        except Exception:
+            pass
+    if world == 1 and not args.no_cpu_baseline:
+        v, cores, sample, _ = cpu_reference(steps=1, warmup=0)
+        line["cpu_baseline"] = {"value": round(v, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": sample}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        v, cores, sample, tsec = cpu_reference(args.steps, args.warmup)
+        line = {"metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tsec * 1e3, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (seeded; BASELINE config-2 distributions)",
+                "impl": "reference",
+                "config": {"workload": "cfg2: chunkwise KDA fwd+VJP, B8 H12 T1568 dk=dv=64 "
+                                       "chunk64 (CPU sample)", "B": B, "H": H, "T": T, "D": D},
+                "cpu_baseline": {"value": round(v, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0},
+                "note": "MLX (the reference's runtime) is not installable here; the reference's "
+                        "compiled path is timed as its numpy restatement (oracle/kda_oracle.py)"}
+        print(json.dumps(line))
+        return 0
+
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

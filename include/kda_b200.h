@@ -1,0 +1,119 @@
+/*
+ * kda_b200.h -- C ABI of libkda_b200.so, the B200 (sm_100a) chunkwise KDA recurrence.
+ *
+ * KDA (Kimi Delta Attention) is Gated DeltaNet with a per-channel log-decay g <= 0.  Per
+ * (batch b, head h) with state S in R^{Dv x Dk} (rows = value dim, decay acts on columns):
+ *     S_t = (S_{t-1} diag(exp g_t)) (I - beta_t k_t k_t^T) + beta_t v_t k_t^T,   o_t = S_t q_t
+ * computed chunkwise (WY/UT form).  There is no scale inside the op (the caller pre-scales q).
+ *
+ * These entry points replace the reference's per-path compute methods and the MSL kernels
+ * they launch through mx.fast.metal_kernel (HananKibria/MLX_VIT, nope_gdn_mlx.py):
+ *   kda_fwd  <- GatedDeltaLayer._chunkwise_kda_forward (nope_gdn_mlx.py:2318-2456) and
+ *               _chunkwise_kda_with_traj (:2484-2571): one call does the whole layer
+ *               recurrence (preamble :549-582, M/M_oq kernel :1301-1469, IA build :585-597,
+ *               per-chunk solve+finalize kernels :1519-2055); with chunk_states != NULL it
+ *               also saves the per-chunk states the backward needs (the S_traj of :2567).
+ *   kda_bwd  <- the vjp of _get_chunkwise_kda_recurrence_fn (:2746-2809) and
+ *               _chunkwise_kda_backward (:2579-2720), including the triangular-solve and
+ *               M-backward kernels (:1209-1286, :2080-2295).
+ * Semantics (outputs, final state, all gradients) follow the reference's `compiled` path
+ * _loop_compiled_kda (:890-917) and MLX autograd through it.
+ *
+ * Conventions
+ *   - All pointers are device pointers; buffers are owned by the caller; the library keeps no
+ *     allocation of its own and writes only the listed outputs (and the caller's workspace).
+ *   - Layouts are dense row-major:  q, k, g, dO, dq, dk, dg: [B, T, H, Dk];  v, o, dv: [B, T,
+ *     H, Dv];  beta, dbeta: [B, T, H];  state0, stateT, dstateT, dstate0: [B, H, Dv, Dk]
+ *     float32;  chunk_states: [B, H, ceil(T/chunk), Dv, Dk] float32 (state entering chunk c).
+ *   - dtype_qkv applies to q, k, v, o, dO, dq, dk, dv;  dtype_beta to beta and dbeta;
+ *     g, dg and every state are float32 (nope_gdn_mlx.py:804, :906).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are asynchronous.
+ *   - Every function returns 0 on success or a negative KDA_ERR_* status; kda_strerror()
+ *     names it.  No exception crosses the ABI and no CPU fallback exists.
+ */
+#ifndef KDA_B200_H
+#define KDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define KDA_API
+#else
+#define KDA_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_ABI_VERSION 1
+
+enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
+
+enum kda_status {
+  KDA_OK = 0,
+  KDA_ERR_INVALID_ARG = -1,   /* null pointer, non-positive size, bad descriptor   */
+  KDA_ERR_UNSUPPORTED = -2,   /* shape/chunk combination no kernel here implements */
+  KDA_ERR_DTYPE = -3,         /* dtype code not accepted for that operand          */
+  KDA_ERR_MISALIGNED = -4,    /* pointer not aligned to 16 bytes                   */
+  KDA_ERR_WORKSPACE = -5,     /* workspace missing or smaller than required        */
+  KDA_ERR_CUDA = -6,          /* a CUDA launch or runtime call failed              */
+  KDA_ERR_TIMEOUT = -7        /* a bounded device-side wait gave up                */
+};
+
+/* Flags for KdaDesc.flags */
+#define KDA_FLAG_FORCE_GENERIC 0x1  /* use the fp32 SIMT kernels even where a tensor-core
+                                       kernel exists (testing / fp32-exact arithmetic) */
+
+typedef struct KdaDesc {
+  int64_t B, T, H;     /* batch, sequence length, heads                          */
+  int64_t Dk, Dv;      /* key/query dim and value dim (the reference has Dk==Dv) */
+  int64_t chunk;       /* chunk size C (GatedDeltaLayer.chunk_size)              */
+  int32_t dtype_qkv;   /* enum kda_dtype                                         */
+  int32_t dtype_beta;  /* enum kda_dtype                                         */
+  int32_t flags;       /* KDA_FLAG_*                                             */
+  int32_t reserved;
+} KdaDesc;
+
+/* ABI version of the loaded library (KDA_ABI_VERSION it was built with). */
+KDA_API int kda_abi_version(void);
+
+/* Static string for a status code. */
+KDA_API const char *kda_strerror(int status);
+
+/* Validate a descriptor without touching memory: 0 if some kernel implements it. */
+KDA_API int kda_check_desc(const KdaDesc *desc, int backward);
+
+/* Workspace bytes kda_fwd (backward = 0) or kda_bwd (backward = 1) needs; 0 means the
+ * call needs none and ws may be NULL.  Returns 0 on an invalid descriptor as well. */
+KDA_API size_t kda_workspace_bytes(const KdaDesc *desc, int backward);
+
+/* Number of kernels this library has launched in this process (instrumentation; used by
+ * benchmarks to count device launches inside a timed region).  No reference counterpart. */
+KDA_API uint64_t kda_launch_counter(void);
+
+/* Forward.  state0 may be NULL (zero initial state).  chunk_states may be NULL (inference);
+ * training passes it and hands the same buffer to kda_bwd.
+ * Replaces: GatedDeltaLayer._chunkwise_kda_forward / _chunkwise_kda_with_traj
+ * (nope_gdn_mlx.py:2318-2456, :2484-2571); semantics of _loop_compiled_kda (:890-917). */
+KDA_API int kda_fwd(const KdaDesc *desc, const void *q, const void *k, const void *v,
+            const float *g, const void *beta, const float *state0,
+            void *o, float *stateT, float *chunk_states,
+            void *ws, size_t ws_bytes, void *stream);
+
+/* Backward (VJP).  state0 may be NULL (zero); dstateT may be NULL (zero cotangent);
+ * dstate0 may be NULL (not wanted).  chunk_states is the buffer kda_fwd filled.
+ * Replaces: the vjp of _get_chunkwise_kda_recurrence_fn and _chunkwise_kda_backward
+ * (nope_gdn_mlx.py:2746-2809, :2579-2720). */
+KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const void *v,
+            const float *g, const void *beta, const float *state0,
+            const float *chunk_states, const void *dO, const float *dstateT,
+            void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
+            void *ws, size_t ws_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_B200_H */

@@ -1,0 +1,128 @@
+// C-ABI entry points of libkda_b200.so: descriptor validation and kernel dispatch.
+// Declarations and the reference interface each entry point replaces: include/kda_b200.h.
+#include <stdio.h>
+
+#include <atomic>
+
+#include "kda_common.cuh"
+
+namespace kda {
+int generic_fwd(const Params &p, int dq, int db, cudaStream_t st);
+int generic_bwd(const Params &p, int dq, int db, cudaStream_t st);
+int generic_fwd_split(int D, int C);
+size_t generic_bwd_smem(int D, int C);
+bool tc_supported(const KdaDesc *d, int backward);
+size_t tc_workspace_bytes(const KdaDesc *d, int backward);
+int tc_fwd(const Params &p, void *ws, size_t ws_bytes, cudaStream_t st);
+int tc_bwd(const Params &p, void *ws, size_t ws_bytes, cudaStream_t st);
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace kda
+
+using kda::Params;
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int dtype_ok(int dt) { return dt == KDA_F32 || dt == KDA_BF16 || dt == KDA_F16; }
+
+static int check_desc_shape(const KdaDesc *d) {
+  if (!d) return KDA_ERR_INVALID_ARG;
+  if (d->B <= 0 || d->T <= 0 || d->H <= 0 || d->Dk <= 0 || d->Dv <= 0 || d->chunk <= 0)
+    return KDA_ERR_INVALID_ARG;
+  if (!dtype_ok(d->dtype_qkv) || !dtype_ok(d->dtype_beta)) return KDA_ERR_DTYPE;
+  if (d->B * d->H > (1ll << 30) || d->T > (1ll << 30) || d->B * d->T * d->H * d->Dk > (1ll << 40))
+    return KDA_ERR_UNSUPPORTED;
+  if (d->Dk != d->Dv) return KDA_ERR_UNSUPPORTED;  // the reference state is D x D
+  if (d->chunk > 64 || d->Dk > 128) return KDA_ERR_UNSUPPORTED;
+  return KDA_OK;
+}
+
+static bool use_tc(const KdaDesc *d, int backward) {
+  if (d->flags & KDA_FLAG_FORCE_GENERIC) return false;
+  return kda::tc_supported(d, backward);
+}
+
+extern "C" {
+
+int kda_abi_version(void) { return KDA_ABI_VERSION; }
+
+uint64_t kda_launch_counter(void) { return kda::g_launches.load(std::memory_order_relaxed); }
+
+const char *kda_strerror(int s) {
+  switch (s) {
+    case KDA_OK: return "ok";
+    case KDA_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or bad descriptor)";
+    case KDA_ERR_UNSUPPORTED: return "unsupported shape: needs Dk == Dv, chunk <= 64, D <= 128 (forward) / D <= 64 (backward)";
+    case KDA_ERR_DTYPE: return "unsupported dtype code";
+    case KDA_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+    case KDA_ERR_WORKSPACE: return "workspace missing or too small (see kda_workspace_bytes)";
+    case KDA_ERR_CUDA: return "CUDA launch or runtime error";
+    case KDA_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int kda_check_desc(const KdaDesc *d, int backward) {
+  int s = check_desc_shape(d);
+  if (s) return s;
+  if (use_tc(d, backward)) return KDA_OK;
+  if (!backward) return kda::generic_fwd_split((int)d->Dk, (int)d->chunk) ? KDA_OK : KDA_ERR_UNSUPPORTED;
+  return kda::generic_bwd_smem((int)d->Dk, (int)d->chunk) <= 227 * 1024 ? KDA_OK : KDA_ERR_UNSUPPORTED;
+}
+
+size_t kda_workspace_bytes(const KdaDesc *d, int backward) {
+  if (kda_check_desc(d, backward)) return 0;
+  return use_tc(d, backward) ? kda::tc_workspace_bytes(d, backward) : 0;
+}
+
+static Params make_params(const KdaDesc *d) {
+  Params p = {};
+  p.B = (int)d->B; p.T = (int)d->T; p.H = (int)d->H; p.D = (int)d->Dk; p.C = (int)d->chunk;
+  p.nc = (int)((d->T + d->chunk - 1) / d->chunk);
+  return p;
+}
+
+int kda_fwd(const KdaDesc *d, const void *q, const void *k, const void *v, const float *g,
+            const void *beta, const float *state0, void *o, float *stateT, float *chunk_states,
+            void *ws, size_t ws_bytes, void *stream) {
+  int s = kda_check_desc(d, 0);
+  if (s) return s;
+  if (!q || !k || !v || !g || !beta || !o || !stateT) return KDA_ERR_INVALID_ARG;
+  const void *ptrs[] = {q, k, v, g, o, stateT};
+  for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
+  if ((state0 && !aligned16(state0)) || (chunk_states && !aligned16(chunk_states))) return KDA_ERR_MISALIGNED;
+  size_t need = kda_workspace_bytes(d, 0);
+  if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
+  Params p = make_params(d);
+  p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
+  p.o = o; p.stateT = stateT; p.chunk_states = chunk_states;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (use_tc(d, 0)) return kda::tc_fwd(p, ws, ws_bytes, st);
+  return kda::generic_fwd(p, d->dtype_qkv, d->dtype_beta, st);
+}
+
+int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const float *g,
+            const void *beta, const float *state0, const float *chunk_states, const void *dO,
+            const float *dstateT, void *dq, void *dk, void *dv, float *dg, void *dbeta,
+            float *dstate0, void *ws, size_t ws_bytes, void *stream) {
+  int s = kda_check_desc(d, 1);
+  if (s) return s;
+  if (!q || !k || !v || !g || !beta || !chunk_states || !dO || !dq || !dk || !dv || !dg || !dbeta)
+    return KDA_ERR_INVALID_ARG;
+  const void *ptrs[] = {q, k, v, g, chunk_states, dO, dq, dk, dv, dg};
+  for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
+  if ((state0 && !aligned16(state0)) || (dstateT && !aligned16(dstateT)) ||
+      (dstate0 && !aligned16(dstate0)))
+    return KDA_ERR_MISALIGNED;
+  size_t need = kda_workspace_bytes(d, 1);
+  if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
+  Params p = make_params(d);
+  p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
+  p.chunk_states_in = chunk_states; p.dO = dO; p.dstateT = dstateT;
+  p.dq = dq; p.dk = dk; p.dv = dv; p.dg = dg; p.dbeta = dbeta; p.dstate0 = dstate0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (use_tc(d, 1)) return kda::tc_bwd(p, ws, ws_bytes, st);
+  return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,43 @@
+// Shared device helpers for the KDA kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/kda_b200.h"
+
+namespace kda {
+
+// Kernel launch counter behind kda_launch_counter(); every launch site bumps it.
+void count_launch();
+
+// Kernel parameter block shared by every KDA kernel.  Element strides are those of the dense
+// [B, T, H, D] / [B, T, H] / [B, H, Dv, Dk] layouts of the C ABI.
+struct Params {
+  int B, T, H, D, C, nc;       // D = Dk = Dv, C = chunk, nc = ceil(T / C)
+  const void *q, *k, *v, *beta;
+  const float *g, *state0, *chunk_states_in, *dstateT;
+  const void *dO;
+  void *o, *dq, *dk, *dv, *dbeta;
+  float *stateT, *chunk_states, *dg, *dstate0;
+  int *err;                    // optional device error word
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// Offset of element (b, t, h, d) in a dense [B, T, H, D] tensor.
+__device__ __forceinline__ int64_t off_bthd(int b, int t, int h, int d, int T, int H, int D) {
+  return (((int64_t)b * T + t) * H + h) * D + d;
+}
+
+}  // namespace kda

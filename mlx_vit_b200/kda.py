@@ -1,0 +1,189 @@
+"""``cuda_kda``: the reference KDA operator's drop-in, backed by libkda_b200.so.
+
+Host-side mirror of the reference's compute-path interface (HananKibria/MLX_VIT,
+nope_gdn_mlx.py):
+
+* ``cuda_kda(q, k, v, g, beta, state=None, chunk_size=64) -> (output, new_state)`` has the
+  signature and dtype contract of the ``GatedDeltaLayer`` path methods (e.g.
+  ``_chunkwise_kda_vjp_path`` :2829-2865, ``_loop_compiled_kda`` :890-917): q, k, v, g are
+  (B, L, H, D), beta (B, L, H), state (B, H, D, D) float32 or None (zeros); the output is in
+  q's dtype and the new state float32.  g is used as float32 (nope_gdn_mlx.py:804).
+* Its VJP returns one gradient per primal, like the ``mx.custom_function`` vjp at
+  :2746-2809: dq, dk, dv in the primal dtype, dg float32, dbeta in beta's dtype, dstate
+  float32 (None when no state was passed).  The final-state cotangent may be absent.
+* ``validate_compute_path`` mirrors the constructor checks at :693-735 with ``"cuda_kda"``
+  added (channel-wise KDA only).
+
+Arrays cross the boundary as raw device pointers (any DLPack-capable CUDA array is accepted
+and viewed without a copy through ``torch.from_dlpack``); all launches go on the current torch
+CUDA stream.  There is no CPU or eager fallback: a missing library, a CPU tensor or an
+unsupported shape raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.KDA_F32, torch.bfloat16: _lib.KDA_BF16, torch.float16: _lib.KDA_F16}
+
+KDA_COMPUTE_PATHS = ("metal_vjp", "chunkwise_kda_vjp", "chunkwise_kda", "metal_sg", "metal",
+                     "compiled", "naive", "cuda_kda")
+
+
+def validate_compute_path(compute_path: str, channel_wise_decay: bool = True) -> str:
+    """Constructor-time check of a GDN compute path (nope_gdn_mlx.py:693-735) extended with
+    ``"cuda_kda"``, which exists for channel-wise KDA only."""
+    if compute_path == "cuda_kda" and not channel_wise_decay:
+        raise ValueError("cuda_kda is only valid for channel-wise KDA (channel_wise_decay=True). "
+                         "For scalar-alpha use 'chunkwise_wy'.")
+    if compute_path not in KDA_COMPUTE_PATHS + ("chunkwise_wy",):
+        raise ValueError(f"Unknown compute_path: {compute_path}")
+    return compute_path
+
+
+def _as_torch(x, name):
+    if x is None:
+        return None
+    if not isinstance(x, torch.Tensor):
+        if hasattr(x, "__dlpack__"):
+            x = torch.from_dlpack(x)
+        else:
+            raise TypeError(f"{name}: expected a CUDA array (torch tensor or DLPack), got {type(x)}")
+    if not x.is_cuda:
+        raise ValueError(f"{name}: cuda_kda needs device arrays (got a {x.device} tensor); "
+                         "there is no CPU path")
+    return x
+
+
+def _ptr(x):
+    return ctypes.c_void_p(x.data_ptr()) if x is not None else ctypes.c_void_p(0)
+
+
+def _desc(q, beta, chunk_size, flags):
+    B, T, H, D = q.shape
+    if q.dtype not in _DT or beta.dtype not in _DT:
+        raise ValueError(f"unsupported dtypes q={q.dtype} beta={beta.dtype}")
+    return _lib.KdaDesc(B, T, H, D, D, int(chunk_size), _DT[q.dtype], _DT[beta.dtype], flags, 0)
+
+
+def _check_shapes(q, k, v, g, beta, state):
+    if q.dim() != 4:
+        raise ValueError(f"q must be (B, L, H, D), got {tuple(q.shape)}")
+    B, T, H, D = q.shape
+    for n, x in (("k", k), ("v", v), ("g", g)):
+        if tuple(x.shape) != (B, T, H, D):
+            raise ValueError(f"{n} shape {tuple(x.shape)} != q shape {(B, T, H, D)}")
+    if tuple(beta.shape) != (B, T, H):
+        raise ValueError(f"beta shape {tuple(beta.shape)} != {(B, T, H)}")
+    if state is not None and tuple(state.shape) != (B, H, D, D):
+        raise ValueError(f"state shape {tuple(state.shape)} != {(B, H, D, D)}")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    devs = {x.device for x in (q, k, v, g, beta) + ((state,) if state is not None else ())}
+    if len(devs) != 1:
+        raise ValueError(f"all operands must be on one device, got {devs}")
+
+
+def _workspace(desc, backward, device):
+    n = _lib.lib().kda_workspace_bytes(ctypes.byref(desc), backward)
+    if n == 0:
+        return None, 0
+    return torch.empty(n, dtype=torch.uint8, device=device), n
+
+
+def num_chunks(T: int, chunk_size: int) -> int:
+    return (T + chunk_size - 1) // chunk_size
+
+
+def kda_forward(q, k, v, g, beta, state=None, chunk_size=64, save_states=False, flags=0):
+    """One ``kda_fwd`` call.  Returns (o, S_T, chunk_states | None)."""
+    L = _lib.lib()
+    B, T, H, D = q.shape
+    desc = _desc(q, beta, chunk_size, flags)
+    o = torch.empty_like(q)
+    S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
+    cs = (torch.empty((B, H, num_chunks(T, chunk_size), D, D), dtype=torch.float32, device=q.device)
+          if save_states else None)
+    ws, nws = _workspace(desc, 0, q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream().cuda_stream
+        st = L.kda_fwd(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                       _ptr(state), _ptr(o), _ptr(S_T), _ptr(cs), _ptr(ws), nws,
+                       ctypes.c_void_p(stream))
+    _lib.check(st, "kda_fwd")
+    return o, S_T, cs
+
+
+def kda_backward(q, k, v, g, beta, state, chunk_states, do, dstate=None, chunk_size=64,
+                 flags=0, want_dstate0=True):
+    """One ``kda_bwd`` call.  Returns (dq, dk, dv, dg, dbeta, dstate0 | None)."""
+    L = _lib.lib()
+    B, T, H, D = q.shape
+    desc = _desc(q, beta, chunk_size, flags)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dg = torch.empty((B, T, H, D), dtype=torch.float32, device=q.device)
+    db = torch.empty_like(beta)
+    ds0 = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device) if want_dstate0 else None
+    ws, nws = _workspace(desc, 1, q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream().cuda_stream
+        st = L.kda_bwd(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                       _ptr(state), _ptr(chunk_states), _ptr(do), _ptr(dstate), _ptr(dq),
+                       _ptr(dk), _ptr(dv), _ptr(dg), _ptr(db), _ptr(ds0), _ptr(ws), nws,
+                       ctypes.c_void_p(stream))
+    _lib.check(st, "kda_bwd")
+    return dq, dk, dv, dg, db, ds0
+
+
+class CudaKdaFunction(torch.autograd.Function):
+    """Autograd wiring of the forward/VJP pair (the torch counterpart of the reference's
+    ``mx.custom_function`` + ``.vjp`` at nope_gdn_mlx.py:2734-2809).  The forward saves only
+    the per-chunk entry states (B, H, nc, D, D) float32; the backward recomputes every
+    intra-chunk quantity from them."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, state, chunk_size, flags):
+        o, S_T, cs = kda_forward(q, k, v, g, beta, state, chunk_size, save_states=True, flags=flags)
+        ctx.save_for_backward(q, k, v, g, beta, state, cs)
+        ctx.chunk_size, ctx.flags = chunk_size, flags
+        ctx.has_state = state is not None
+        return o, S_T
+
+    @staticmethod
+    def backward(ctx, do, dS_T):
+        q, k, v, g, beta, state, cs = ctx.saved_tensors
+        do = torch.zeros_like(q) if do is None else do.to(q.dtype).contiguous()
+        dS_T = None if dS_T is None else dS_T.float().contiguous()
+        dq, dk, dv, dg, db, ds0 = kda_backward(q, k, v, g, beta, state, cs, do, dS_T,
+                                               ctx.chunk_size, ctx.flags,
+                                               want_dstate0=ctx.has_state)
+        return dq, dk, dv, dg, db, ds0, None, None
+
+
+def cuda_kda(q, k, v, g, beta, state: Optional[torch.Tensor] = None, chunk_size: int = 64,
+             *, force_generic: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Chunkwise KDA on the GPU: returns (output in q.dtype, final state float32).
+
+    ``force_generic`` selects the fp32 SIMT kernels even where a tensor-core kernel exists.
+    fp32 inputs always run on the fp32 kernels.
+    """
+    q, k, v, g, beta, state = (_as_torch(x, n) for x, n in
+                               ((q, "q"), (k, "k"), (v, "v"), (g, "g"), (beta, "beta"),
+                                (state, "state")))
+    _check_shapes(q, k, v, g, beta, state)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    g = g.to(torch.float32).contiguous()
+    beta = beta.contiguous()
+    if state is not None:
+        state = state.to(torch.float32).contiguous()
+    flags = _lib.KDA_FLAG_FORCE_GENERIC if force_generic else 0
+    need_grad = torch.is_grad_enabled() and any(
+        x is not None and x.requires_grad for x in (q, k, v, g, beta, state))
+    if need_grad:
+        return CudaKdaFunction.apply(q, k, v, g, beta, state, chunk_size, flags)
+    o, S_T, _ = kda_forward(q, k, v, g, beta, state, chunk_size, save_states=False, flags=flags)
+    return o, S_T

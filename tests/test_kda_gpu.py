@@ -1,0 +1,129 @@
+"""GPU parity: the CUDA path (through the C ABI) against the reference golden vectors and the
+CPU oracle.  Tolerances are the north-star ones: max|delta|/max|ref| <= 1e-4 for fp32 I/O
+and <= 2e-2 for bf16 I/O (the oracle then runs in float64 on the same bf16-rounded inputs)."""
+import numpy as np
+import pytest
+import torch
+
+from kda_testutil import manifest, golden, rel_err, OUT_KEYS, TOL_FP32, TOL_BF16
+from mlx_vit_b200 import cuda_kda, kda_forward, kda_backward
+from mlx_vit_b200.synthetic import make_inputs
+from oracle import kda_oracle as O
+
+pytestmark = pytest.mark.gpu
+CASES = manifest()["cases"]
+GRAD_KEYS = ("q", "k", "v", "g", "beta", "state")
+
+
+def to_dev(inp, dev, dtype):
+    t = {}
+    for k in ("q", "k", "v", "beta", "do"):
+        t[k] = torch.from_numpy(inp[k]).to(dev).to(dtype)
+    for k in ("g", "state", "dst"):
+        t[k] = torch.from_numpy(inp[k]).to(dev)
+    return t
+
+
+def run_fwd_bwd(t, chunk, force_generic=False, with_state=True):
+    leaves = {k: t[k].clone().requires_grad_(True) for k in GRAD_KEYS}
+    st = leaves["state"] if with_state else None
+    o, S = cuda_kda(leaves["q"], leaves["k"], leaves["v"], leaves["g"], leaves["beta"], st,
+                    chunk_size=chunk, force_generic=force_generic)
+    loss = (o.float() * t["do"].float()).sum() + (S * t["dst"]).sum()
+    loss.backward()
+    out = dict(o=o, S_T=S, dq=leaves["q"].grad, dk=leaves["k"].grad, dv=leaves["v"].grad,
+               dg=leaves["g"].grad, dbeta=leaves["beta"].grad, dstate0=leaves["state"].grad)
+    return {k: (v.detach().float().cpu().numpy() if v is not None else None) for k, v in out.items()}
+
+
+def rounded_inputs(inp, dtype):
+    """The inputs as the kernel sees them after the cast to ``dtype`` (float32 numpy)."""
+    r = dict(inp)
+    for k in ("q", "k", "v", "beta", "do"):
+        r[k] = torch.from_numpy(inp[k]).to(dtype).float().numpy()
+    return r
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_fp32_matches_reference_golden(cuda, name):
+    c = CASES[name]
+    inp = make_inputs(c["B"], c["T"], c["H"], c["D"], seed=c["seed"], state_std=c["state_std"])
+    gold = golden(name)
+    got = run_fwd_bwd(to_dev(inp, cuda, torch.float32), c["chunk"])
+    for k in OUT_KEYS:
+        assert rel_err(got[k], gold[k]) <= TOL_FP32, (name, k, rel_err(got[k], gold[k]))
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+@pytest.mark.parametrize("force_generic", [False, True])
+def test_bf16_matches_oracle(cuda, name, force_generic):
+    c = CASES[name]
+    inp = make_inputs(c["B"], c["T"], c["H"], c["D"], seed=c["seed"], state_std=c["state_std"])
+    ref = O.fwd_bwd(rounded_inputs(inp, torch.bfloat16), dtype=np.float64)
+    got = run_fwd_bwd(to_dev(inp, cuda, torch.bfloat16), c["chunk"], force_generic=force_generic)
+    for k in OUT_KEYS:
+        assert rel_err(got[k], ref[k]) <= TOL_BF16, (name, k, rel_err(got[k], ref[k]))
+
+
+@pytest.mark.parametrize("chunk", [8, 16, 32, 64])
+@pytest.mark.parametrize("T", [1, 7, 64, 130])
+def test_chunk_sizes_and_ragged_lengths_fp32(cuda, chunk, T):
+    inp = make_inputs(2, T, 3, 32, seed=T * 100 + chunk, state_std=0.1)
+    ref = O.fwd_bwd(inp, dtype=np.float64)
+    got = run_fwd_bwd(to_dev(inp, cuda, torch.float32), chunk)
+    for k in OUT_KEYS:
+        assert rel_err(got[k], ref[k]) <= TOL_FP32, (k, rel_err(got[k], ref[k]))
+
+
+def test_zero_state_none_equals_explicit_zero(cuda):
+    inp = make_inputs(1, 70, 2, 64, seed=11, state_std=0.0)
+    t = to_dev(inp, cuda, torch.bfloat16)
+    with torch.no_grad():
+        o1, s1 = cuda_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], None)
+        o2, s2 = cuda_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], t["state"])
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    assert o1.dtype == torch.bfloat16 and s1.dtype == torch.float32
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_segmented_state_carry_equals_one_pass(cuda, dtype):
+    """Streaming use (config 4's pattern): running T as segments with the state carried gives
+    the one-pass result."""
+    inp = make_inputs(1, 4 * 96, 2, 64, seed=21, state_std=0.1)
+    t = to_dev(inp, cuda, dtype)
+    with torch.no_grad():
+        o_full, s_full = cuda_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], t["state"])
+        st, outs = t["state"], []
+        for i in range(4):
+            sl = slice(i * 96, (i + 1) * 96)
+            o, st = cuda_kda(t["q"][:, sl], t["k"][:, sl], t["v"][:, sl], t["g"][:, sl],
+                             t["beta"][:, sl], st)
+            outs.append(o)
+    tol = TOL_FP32 if dtype == torch.float32 else TOL_BF16
+    assert rel_err(torch.cat(outs, 1).float().cpu(), o_full.float().cpu()) <= tol
+    assert rel_err(st.cpu(), s_full.cpu()) <= tol
+
+
+def test_no_grad_path_and_dstate_none(cuda):
+    inp = make_inputs(1, 50, 2, 32, seed=3, state_std=0.1)
+    t = to_dev(inp, cuda, torch.float32)
+    o, S, cs = kda_forward(t["q"], t["k"], t["v"], t["g"], t["beta"], t["state"], 16, save_states=True)
+    dq, dk, dv, dg, db, ds0 = kda_backward(t["q"], t["k"], t["v"], t["g"], t["beta"], t["state"],
+                                           cs, t["do"], None, 16)
+    z = dict(inp)
+    z["dst"] = np.zeros_like(inp["dst"])
+    ref = O.fwd_bwd(z, dtype=np.float64)
+    for k, x in zip(("dq", "dk", "dv", "dg", "dbeta", "dstate0"), (dq, dk, dv, dg, db, ds0)):
+        assert rel_err(x.cpu().numpy(), ref[k]) <= TOL_FP32, k
+    # chunk_states[:, :, 0] is the initial state
+    assert torch.equal(cs[:, :, 0], t["state"])
+
+
+def test_strong_decay_stays_finite(cuda):
+    inp = make_inputs(1, 200, 2, 64, seed=8, state_std=0.1)
+    inp["g"] = (inp["g"] * 12.0).astype(np.float32)   # per-step decays down to ~e^-60
+    ref = O.fwd_bwd(rounded_inputs(inp, torch.bfloat16), dtype=np.float64)
+    got = run_fwd_bwd(to_dev(inp, cuda, torch.bfloat16), 64)
+    for k in OUT_KEYS:
+        assert np.isfinite(got[k]).all(), k
+        assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))
