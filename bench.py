@@ -294,6 +294,24 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+def kernel_only(args):
+    """Launches only the library calls on the benchmark workload (a driver for ncu)."""
+    import torch
+    from mlx_vit_b200 import kda_forward, kda_backward
+    from mlx_vit_b200.synthetic import make_inputs_torch
+    dev = torch.device("cuda", 0)
+    inp = make_inputs_torch(B, T, H, D, seed=1234, device=dev, dtype=torch.bfloat16, state_std=0.1)
+    q, k, v, g, beta, S0, do, dst = (inp[n] for n in ("q", "k", "v", "g", "beta", "state", "do", "dst"))
+    _, _, cs = kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=True)
+    for _ in range(args.warmup + args.steps):
+        if args.kernel_only in ("fwd", "both"):
+            kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=args.kernel_only == "both")
+        if args.kernel_only in ("bwd", "both"):
+            kda_backward(q, k, v, g, beta, S0, cs, do, dst, CHUNK)
+    torch.cuda.synchronize()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -301,6 +319,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both"), default=None,
+                    help="profiling driver: run only the kda_fwd/kda_bwd launches (steps+warmup "
+                         "times), no timing, no e2e, no JSON line")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -327,6 +348,8 @@ def main():
         return 0
 
     import torch
+    if args.kernel_only:
+        return kernel_only(args)
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))

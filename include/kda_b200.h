@@ -11,8 +11,8 @@
  *   kda_fwd  <- GatedDeltaLayer._chunkwise_kda_forward (nope_gdn_mlx.py:2318-2456) and
  *               _chunkwise_kda_with_traj (:2484-2571): one call does the whole layer
  *               recurrence (preamble :549-582, M/M_oq kernel :1301-1469, IA build :585-597,
- *               per-chunk solve+finalize kernels :1519-2055); with chunk_states != NULL it
- *               also saves the per-chunk states the backward needs (the S_traj of :2567).
+ *               per-chunk solve+finalize kernels :1519-2055); with saved != NULL it also
+ *               saves what the backward needs per chunk (the U_traj / S_traj of :2565-2567).
  *   kda_bwd  <- the vjp of _get_chunkwise_kda_recurrence_fn (:2746-2809) and
  *               _chunkwise_kda_backward (:2579-2720), including the triangular-solve and
  *               M-backward kernels (:1209-1286, :2080-2295).
@@ -24,7 +24,9 @@
  *     allocation of its own and writes only the listed outputs (and the caller's workspace).
  *   - Layouts are dense row-major:  q, k, g, dO, dq, dk, dg: [B, T, H, Dk];  v, o, dv: [B, T,
  *     H, Dv];  beta, dbeta: [B, T, H];  state0, stateT, dstateT, dstate0: [B, H, Dv, Dk]
- *     float32;  chunk_states: [B, H, ceil(T/chunk), Dv, Dk] float32 (state entering chunk c).
+ *     float32.  `saved` is an opaque device buffer of kda_saved_bytes() bytes that kda_fwd fills
+ *     and kda_bwd reads (per-chunk entry states and WY values); pass it between the two calls
+ *     with the same descriptor.
  *   - dtype_qkv applies to q, k, v, o, dO, dq, dk, dv;  dtype_beta to beta and dbeta;
  *     g, dg and every state are float32 (nope_gdn_mlx.py:804, :906).
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls are asynchronous.
@@ -89,26 +91,31 @@ KDA_API int kda_check_desc(const KdaDesc *desc, int backward);
  * call needs none and ws may be NULL.  Returns 0 on an invalid descriptor as well. */
 KDA_API size_t kda_workspace_bytes(const KdaDesc *desc, int backward);
 
+/* Bytes of the `saved` buffer kda_fwd fills for kda_bwd (the reference keeps the same data
+ * as the U_traj / S_traj outputs of _chunkwise_kda_with_traj, nope_gdn_mlx.py:2484-2571).
+ * Returns 0 on an invalid descriptor. */
+KDA_API size_t kda_saved_bytes(const KdaDesc *desc);
+
 /* Number of kernels this library has launched in this process (instrumentation; used by
  * benchmarks to count device launches inside a timed region).  No reference counterpart. */
 KDA_API uint64_t kda_launch_counter(void);
 
-/* Forward.  state0 may be NULL (zero initial state).  chunk_states may be NULL (inference);
- * training passes it and hands the same buffer to kda_bwd.
+/* Forward.  state0 may be NULL (zero initial state).  saved may be NULL (inference);
+ * training passes a kda_saved_bytes() buffer and hands it to kda_bwd.
  * Replaces: GatedDeltaLayer._chunkwise_kda_forward / _chunkwise_kda_with_traj
  * (nope_gdn_mlx.py:2318-2456, :2484-2571); semantics of _loop_compiled_kda (:890-917). */
 KDA_API int kda_fwd(const KdaDesc *desc, const void *q, const void *k, const void *v,
             const float *g, const void *beta, const float *state0,
-            void *o, float *stateT, float *chunk_states,
+            void *o, float *stateT, void *saved,
             void *ws, size_t ws_bytes, void *stream);
 
 /* Backward (VJP).  state0 may be NULL (zero); dstateT may be NULL (zero cotangent);
- * dstate0 may be NULL (not wanted).  chunk_states is the buffer kda_fwd filled.
+ * dstate0 may be NULL (not wanted).  saved is the buffer kda_fwd filled.
  * Replaces: the vjp of _get_chunkwise_kda_recurrence_fn and _chunkwise_kda_backward
  * (nope_gdn_mlx.py:2746-2809, :2579-2720). */
 KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const void *v,
             const float *g, const void *beta, const float *state0,
-            const float *chunk_states, const void *dO, const float *dstateT,
+            const void *saved, const void *dO, const float *dstateT,
             void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
             void *ws, size_t ws_bytes, void *stream);
 

@@ -23,7 +23,7 @@ STATUS = {
 
 # every symbol include/kda_b200.h declares
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
-           "kda_launch_counter", "kda_fwd", "kda_bwd")
+           "kda_saved_bytes", "kda_launch_counter", "kda_fwd", "kda_bwd")
 
 
 class KdaDesc(ctypes.Structure):
@@ -54,6 +54,8 @@ def _declare(L):
     L.kda_check_desc.argtypes = [D, I]
     L.kda_workspace_bytes.restype = S
     L.kda_workspace_bytes.argtypes = [D, I]
+    L.kda_saved_bytes.restype = S
+    L.kda_saved_bytes.argtypes = [D]
     L.kda_launch_counter.restype = ctypes.c_uint64
     L.kda_launch_counter.argtypes = []
     L.kda_fwd.restype = I

@@ -13,8 +13,9 @@ int generic_fwd_split(int D, int C);
 size_t generic_bwd_smem(int D, int C);
 bool tc_supported(const KdaDesc *d, int backward);
 size_t tc_workspace_bytes(const KdaDesc *d, int backward);
-int tc_fwd(const Params &p, void *ws, size_t ws_bytes, cudaStream_t st);
-int tc_bwd(const Params &p, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t tc_saved_bytes(const KdaDesc *d);
+int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st);
+int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st);
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 }  // namespace kda
@@ -75,6 +76,15 @@ size_t kda_workspace_bytes(const KdaDesc *d, int backward) {
   return use_tc(d, backward) ? kda::tc_workspace_bytes(d, backward) : 0;
 }
 
+// The saved record's layout belongs to the backward that reads it: a forward that saves
+// for the backward uses the tensor-core forward only where the tensor-core backward runs too.
+size_t kda_saved_bytes(const KdaDesc *d) {
+  if (kda_check_desc(d, 0)) return 0;
+  if (use_tc(d, 1)) return kda::tc_saved_bytes(d);
+  const int64_t nc = (d->T + d->chunk - 1) / d->chunk;
+  return (size_t)(d->B * d->H * nc * d->Dk * d->Dv) * sizeof(float);
+}
+
 static Params make_params(const KdaDesc *d) {
   Params p = {};
   p.B = (int)d->B; p.T = (int)d->T; p.H = (int)d->H; p.D = (int)d->Dk; p.C = (int)d->chunk;
@@ -83,33 +93,33 @@ static Params make_params(const KdaDesc *d) {
 }
 
 int kda_fwd(const KdaDesc *d, const void *q, const void *k, const void *v, const float *g,
-            const void *beta, const float *state0, void *o, float *stateT, float *chunk_states,
+            const void *beta, const float *state0, void *o, float *stateT, void *saved,
             void *ws, size_t ws_bytes, void *stream) {
   int s = kda_check_desc(d, 0);
   if (s) return s;
   if (!q || !k || !v || !g || !beta || !o || !stateT) return KDA_ERR_INVALID_ARG;
   const void *ptrs[] = {q, k, v, g, o, stateT};
   for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
-  if ((state0 && !aligned16(state0)) || (chunk_states && !aligned16(chunk_states))) return KDA_ERR_MISALIGNED;
+  if ((state0 && !aligned16(state0)) || (saved && !aligned16(saved))) return KDA_ERR_MISALIGNED;
   size_t need = kda_workspace_bytes(d, 0);
   if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
   Params p = make_params(d);
   p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
-  p.o = o; p.stateT = stateT; p.chunk_states = chunk_states;
+  p.o = o; p.stateT = stateT; p.saved = saved; p.ws = ws;
   cudaStream_t st = (cudaStream_t)stream;
-  if (use_tc(d, 0)) return kda::tc_fwd(p, ws, ws_bytes, st);
+  if (use_tc(d, 0) && (!saved || use_tc(d, 1))) return kda::tc_fwd(p, d->dtype_beta, st);
   return kda::generic_fwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 
 int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const float *g,
-            const void *beta, const float *state0, const float *chunk_states, const void *dO,
+            const void *beta, const float *state0, const void *saved, const void *dO,
             const float *dstateT, void *dq, void *dk, void *dv, float *dg, void *dbeta,
             float *dstate0, void *ws, size_t ws_bytes, void *stream) {
   int s = kda_check_desc(d, 1);
   if (s) return s;
-  if (!q || !k || !v || !g || !beta || !chunk_states || !dO || !dq || !dk || !dv || !dg || !dbeta)
+  if (!q || !k || !v || !g || !beta || !saved || !dO || !dq || !dk || !dv || !dg || !dbeta)
     return KDA_ERR_INVALID_ARG;
-  const void *ptrs[] = {q, k, v, g, chunk_states, dO, dq, dk, dv, dg};
+  const void *ptrs[] = {q, k, v, g, saved, dO, dq, dk, dv, dg};
   for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
   if ((state0 && !aligned16(state0)) || (dstateT && !aligned16(dstateT)) ||
       (dstate0 && !aligned16(dstate0)))
@@ -118,10 +128,10 @@ int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
   Params p = make_params(d);
   p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
-  p.chunk_states_in = chunk_states; p.dO = dO; p.dstateT = dstateT;
+  p.saved_in = saved; p.dO = dO; p.dstateT = dstateT; p.ws = ws;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dg = dg; p.dbeta = dbeta; p.dstate0 = dstate0;
   cudaStream_t st = (cudaStream_t)stream;
-  if (use_tc(d, 1)) return kda::tc_bwd(p, ws, ws_bytes, st);
+  if (use_tc(d, 1)) return kda::tc_bwd(p, d->dtype_beta, st);
   return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 

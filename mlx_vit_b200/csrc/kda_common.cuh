@@ -18,12 +18,21 @@ void count_launch();
 struct Params {
   int B, T, H, D, C, nc;       // D = Dk = Dv, C = chunk, nc = ceil(T / C)
   const void *q, *k, *v, *beta;
-  const float *g, *state0, *chunk_states_in, *dstateT;
+  const float *g, *state0, *dstateT;
+  const void *saved_in;        // backward: what the forward saved
+  void *ws;                    // workspace (caller-provided)
   const void *dO;
   void *o, *dq, *dk, *dv, *dbeta;
-  float *stateT, *chunk_states, *dg, *dstate0;
+  float *stateT, *dg, *dstate0;
+  void *saved;                 // forward: per-chunk record for the backward (may be null)
   int *err;                    // optional device error word
 };
+
+// Per-chunk record the tensor-core forward saves for the tensor-core backward (D = C = 64):
+// S0 = chunk-entry state [j][d], Unew^T [j][t], Mneg = -W^T Kb [d'][d], Qt = Qd - P W [t][d]
+// (all bf16, row-major) and e^{gamma_C} [d] (fp32).
+constexpr int kSavedS0 = 0, kSavedUnT = 8192, kSavedM = 16384, kSavedQt = 24576, kSavedEG = 32768;
+constexpr int kSavedChunk = 32768 + 256;
 
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }

@@ -47,8 +47,8 @@ kda_fwd_generic_kernel(Params p, int DVS) {
 
   for (int c = 0; c < p.nc; ++c) {
     const int t0 = c * C;
-    if (p.chunk_states) {
-      float *cs = p.chunk_states + ((int64_t)bh * p.nc + c) * D * D;
+    if (p.saved) {  // generic saved layout: fp32 chunk-entry state [bh][c][Dv][Dk]
+      float *cs = (float *)p.saved + ((int64_t)bh * p.nc + c) * D * D;
       for (int i = tid; i < DVS * D; i += nt) cs[(int64_t)(j0 + i / D) * D + (i % D)] = S[i];
     }
     for (int i = tid; i < C * D; i += nt) {
@@ -157,7 +157,7 @@ kda_bwd_generic_kernel(Params p) {
 
   for (int c = p.nc - 1; c >= 0; --c) {
     const int t0 = c * C;
-    const float *cs = p.chunk_states_in + ((int64_t)bh * p.nc + c) * D * D;
+    const float *cs = (const float *)p.saved_in + ((int64_t)bh * p.nc + c) * D * D;
     for (int i = tid; i < D * D; i += nt) S0[i] = cs[i];
     for (int i = tid; i < C * D; i += nt) {
       int t = i / D, d = i % D, tt = t0 + t;

@@ -1,0 +1,94 @@
+// Warp-level tensor-core and shared-memory helpers for the KDA tensor-core kernels.
+//
+// Tiles of 64 bf16 columns (128-byte rows) live in shared memory with the 128-byte XOR
+// swizzle: 16-byte chunk c of row r is stored at chunk (c ^ (r & 7)).  That keeps ldmatrix /
+// stmatrix conflict-free and is the same layout tcgen05 descriptors call SWIZZLE_128B.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace kda {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// byte offset of element (row, col) in a 64-column swizzled bf16 tile
+__device__ __forceinline__ uint32_t sw64(int row, int col) {
+  return (uint32_t)(row * 128 + ((((col >> 3) ^ row) & 7) << 4) + ((col & 7) << 1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+__device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
+  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&u);
+  return __bfloat1622float2(v);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t (&r)[2]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+__device__ __forceinline__ void stsm_x4_t(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};\n"
+               :: "r"(addr), "r"(r0), "r"(r1), "r"(r2), "r"(r3));
+}
+
+// D += A(16x16, row) * B(16x8, col), bf16 in, fp32 accumulate
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Lane address helpers for ldmatrix/stmatrix x4 on 64-column swizzled tiles.
+//  A fragment of the 16x16 block at (r0, k0):
+__device__ __forceinline__ uint32_t a_frag_addr(uint32_t base, int r0, int k0, int lane) {
+  return base + sw64(r0 + (lane & 15), k0 + ((lane >> 4) << 3));
+}
+//  B fragments (two n8 tiles n0, n0+8; k16 at k0) from a tile stored [n][k] (non-trans):
+__device__ __forceinline__ uint32_t bnk_frag_addr(uint32_t base, int n0, int k0, int lane) {
+  return base + sw64(n0 + (lane & 7) + ((lane >> 4) << 3), k0 + (((lane >> 3) & 1) << 3));
+}
+//  B fragments from a tile stored [k][n] (use with ldsm_x4_t):
+__device__ __forceinline__ uint32_t bkn_frag_addr(uint32_t base, int k0, int n0, int lane) {
+  return base + sw64(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), n0 + ((lane >> 4) << 3));
+}
+//  Transposed access of a tile stored [t][j] (with ldsm_x4_t / stsm_x4_t):
+//   - C fragments (rows j0..j0+15, columns t0..t0+15) of X^T, registers ordered
+//     (n-tile t0: c0c1, c2c3; n-tile t0+8: c0c1, c2c3);
+//   - equally the A fragment of X^T for rows j0..j0+15 and k = t0..t0+15.
+__device__ __forceinline__ uint32_t ct_frag_addr(uint32_t base, int t0, int j0, int lane) {
+  return base + sw64(t0 + (lane & 7) + ((lane >> 4) << 3), j0 + (((lane >> 3) & 1) << 3));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" :: "r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+__device__ __forceinline__ void bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;\n" :: "r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;\n" :: "r"(id), "r"(n) : "memory");
+}
+
+}  // namespace kda

@@ -100,14 +100,19 @@ def num_chunks(T: int, chunk_size: int) -> int:
 
 
 def kda_forward(q, k, v, g, beta, state=None, chunk_size=64, save_states=False, flags=0):
-    """One ``kda_fwd`` call.  Returns (o, S_T, chunk_states | None)."""
+    """One ``kda_fwd`` call.  Returns (o, S_T, saved | None); ``saved`` is the opaque
+    per-chunk record (uint8 device tensor) that ``kda_backward`` consumes."""
     L = _lib.lib()
     B, T, H, D = q.shape
     desc = _desc(q, beta, chunk_size, flags)
     o = torch.empty_like(q)
     S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
-    cs = (torch.empty((B, H, num_chunks(T, chunk_size), D, D), dtype=torch.float32, device=q.device)
-          if save_states else None)
+    cs = None
+    if save_states:
+        n = L.kda_saved_bytes(ctypes.byref(desc))
+        if n == 0:
+            _lib.check(L.kda_check_desc(ctypes.byref(desc), 0) or -1, "kda_saved_bytes")
+        cs = torch.empty(n, dtype=torch.uint8, device=q.device)
     ws, nws = _workspace(desc, 0, q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream().cuda_stream
@@ -118,7 +123,7 @@ def kda_forward(q, k, v, g, beta, state=None, chunk_size=64, save_states=False, 
     return o, S_T, cs
 
 
-def kda_backward(q, k, v, g, beta, state, chunk_states, do, dstate=None, chunk_size=64,
+def kda_backward(q, k, v, g, beta, state, saved, do, dstate=None, chunk_size=64,
                  flags=0, want_dstate0=True):
     """One ``kda_bwd`` call.  Returns (dq, dk, dv, dg, dbeta, dstate0 | None)."""
     L = _lib.lib()
@@ -132,7 +137,7 @@ def kda_backward(q, k, v, g, beta, state, chunk_states, do, dstate=None, chunk_s
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream().cuda_stream
         st = L.kda_bwd(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
-                       _ptr(state), _ptr(chunk_states), _ptr(do), _ptr(dstate), _ptr(dq),
+                       _ptr(state), _ptr(saved), _ptr(do), _ptr(dstate), _ptr(dq),
                        _ptr(dk), _ptr(dv), _ptr(dg), _ptr(db), _ptr(ds0), _ptr(ws), nws,
                        ctypes.c_void_p(stream))
     _lib.check(st, "kda_bwd")
@@ -141,9 +146,9 @@ def kda_backward(q, k, v, g, beta, state, chunk_states, do, dstate=None, chunk_s
 
 class CudaKdaFunction(torch.autograd.Function):
     """Autograd wiring of the forward/VJP pair (the torch counterpart of the reference's
-    ``mx.custom_function`` + ``.vjp`` at nope_gdn_mlx.py:2734-2809).  The forward saves only
-    the per-chunk entry states (B, H, nc, D, D) float32; the backward recomputes every
-    intra-chunk quantity from them."""
+    ``mx.custom_function`` + ``.vjp`` at nope_gdn_mlx.py:2734-2809).  The forward saves one
+    record per chunk (the chunk-entry state and solved WY values, as the reference's U_traj /
+    S_traj); the backward recomputes every other intra-chunk quantity from the inputs."""
 
     @staticmethod
     def forward(ctx, q, k, v, g, beta, state, chunk_size, flags):
