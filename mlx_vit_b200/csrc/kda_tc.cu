@@ -4,17 +4,17 @@
 namespace kda {
 
 // set once the tensor-core backward is in place: the saved-record layout follows it
-static constexpr bool kTcBackward = false;
+static constexpr bool kTcBackward = true;
 
 bool tc_supported(const KdaDesc *d, int backward) {
   if (backward && !kTcBackward) return false;
   return d->Dk == 64 && d->Dv == 64 && d->chunk == 64 && d->dtype_qkv == KDA_BF16 &&
          (d->dtype_beta == KDA_BF16 || d->dtype_beta == KDA_F32);
 }
-size_t tc_workspace_bytes(const KdaDesc *, int) { return 0; }
+size_t tc_bwd_workspace_bytes(const KdaDesc *d);
+size_t tc_workspace_bytes(const KdaDesc *d, int backward) { return backward ? tc_bwd_workspace_bytes(d) : 0; }
 size_t tc_saved_bytes(const KdaDesc *d) {
   const int64_t nc = (d->T + d->chunk - 1) / d->chunk;
   return (size_t)(d->B * d->H * nc) * kSavedChunk;
 }
-int tc_bwd(const Params &, int, cudaStream_t) { return KDA_ERR_UNSUPPORTED; }
 }  // namespace kda

@@ -1,0 +1,657 @@
+// Tensor-core KDA backward for D = 64, chunk = 64, bf16 q/k/v (mma.sync, fp32 accumulate).
+//
+// Per chunk (gamma = cumsum(g) in the chunk, T_ = (I + A)^{-1}, W = T_ beta Kd, Unew the solved
+// WY values of the forward, S0 the chunk-entry state, dS1 the cotangent of the chunk-exit state):
+//   dU  = P^T dO + Kb dS1^T          dR = T_^T dU               dv = beta dR
+//   dS0 = dS1 diag(e^{gamma_C}) - dS1 Kb^T W + dO^T (Qd - P W)
+//   dq  = (dO S0) e^gamma + decayed(dP, k)            dP  = dO Unew^T (s <= t)
+//   dk  = -beta (dR S0) e^gamma + decayed(dKK, k)     dKK = -beta_t dR Unew^T (s < t)
+//         + (Unew dS1) e^{gamma_C - gamma} + decayed^T(dKK, k) + decayed^T(dP, q)
+//   dbeta = dR.V - (dR S0).Kd + sum_s dA M;  dgamma = q dq + k (dk_row - dk_col), + dGamma_C on
+//   the last row;  dg = reverse cumsum of dgamma.
+// (decayed(X, k)_t = sum_s X[t,s] k_s e^{gamma_t - gamma_s}; decayed^T the same over t >= s.)
+// These are the VJPs of the forward's chunk algebra (the quantities of the reference's
+// _chunkwise_kda_backward, nope_gdn_mlx.py:2579-2720, derived independently).
+//
+// Two kernels:
+//   kda_bwd_state_scan  one CTA per (b, h) walks the chunks backwards carrying dS in mma
+//                       registers, using the forward's saved Mneg = -Kb^T W and Qt = Qd - P W;
+//                       it writes every chunk's exit cotangent dS1 (bf16) to the workspace.
+//   kda_bwd_chunks      one CTA per (b, h, chunk), independent of each other: recomputes the
+//                       chunk's decay-weighted M and P, T_ii and dR, and produces all gradients.
+// Chunks whose decay is too strong for the factored form are flagged and redone by the exact
+// fp32 per-chunk kernel (kda_bwd_flagged_chunks_kernel).
+#include <type_traits>
+
+#include "kda_common.cuh"
+#include "kda_mma.cuh"
+
+namespace kda {
+
+int bwd_flagged_chunks(const Params &p, int dtype_beta, const int *flags,
+                       const __nv_bfloat16 *ds_exit, cudaStream_t st);
+
+namespace tcbwd {
+
+constexpr int C = 64, D = 64;
+constexpr float kSpanMax = 60.f;
+
+// workspace: exit cotangent per chunk (bf16 [j][d]) then one flag per chunk
+__host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (size_t)nchunks * 8192; }
+
+// ---------------------------------------------------------------------------------------
+// state-cotangent scan
+// ---------------------------------------------------------------------------------------
+constexpr int SC_NT = 128;
+constexpr int SC_DO = 0, SC_MN = 8192, SC_QT = 16384, SC_EG = 24576, SC_BUF = 24576 + 256;
+constexpr int SC_SMEM = 2 * SC_BUF;
+
+__global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g4 = lane >> 2, c4 = lane & 3, jb = warp * 16;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int T = p.T, H = p.H, nc = p.nc;
+  const uint32_t s_base = smem_u32(sm);
+  const int64_t row_stride = (int64_t)H * D;
+  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
+  const __nv_bfloat16 *dOg = (const __nv_bfloat16 *)p.dO;
+  __nv_bfloat16 *ds_exit = (__nv_bfloat16 *)p.ws;
+
+  auto issue = [&](int c, int buf) {
+    const uint32_t base = s_base + buf * SC_BUF;
+    const uint8_t *rec = (const uint8_t *)p.saved_in + ((int64_t)bh * nc + c) * kSavedChunk;
+    for (int u = tid; u < 512; u += SC_NT) {
+      const int r = u >> 3, ch = u & 7, t = c * C + r;
+      const bool in = t < T;
+      cp_async16(base + SC_DO + sw64(r, ch * 8), dOg + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
+      cp_async16(base + SC_MN + sw64(r, ch * 8), rec + kSavedM + r * 128 + ch * 16, 16);
+      cp_async16(base + SC_QT + sw64(r, ch * 8), rec + kSavedQt + r * 128 + ch * 16, 16);
+    }
+    if (tid < 16) cp_async16(base + SC_EG + tid * 16, rec + kSavedEG + tid * 16, 16);
+    cp_async_commit();
+  };
+
+  float dS[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float2 v = make_float2(0.f, 0.f);
+      if (p.dstateT)
+        v = *reinterpret_cast<const float2 *>(p.dstateT + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4);
+      dS[nt][2 * hh] = v.x;
+      dS[nt][2 * hh + 1] = v.y;
+    }
+  issue(nc - 1, 0);
+  for (int i = 0; i < nc; ++i) {
+    const int c = nc - 1 - i, buf = i & 1;
+    cp_async_wait_all();
+    __syncthreads();
+    if (i + 1 < nc) issue(c - 1, buf ^ 1);
+    const uint32_t base = s_base + buf * SC_BUF;
+    const float *eG = reinterpret_cast<const float *>(sm + buf * SC_BUF + SC_EG);
+    uint32_t da[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      da[kk][0] = pack_bf16(dS[2 * kk][0], dS[2 * kk][1]);
+      da[kk][1] = pack_bf16(dS[2 * kk][2], dS[2 * kk][3]);
+      da[kk][2] = pack_bf16(dS[2 * kk + 1][0], dS[2 * kk + 1][1]);
+      da[kk][3] = pack_bf16(dS[2 * kk + 1][2], dS[2 * kk + 1][3]);
+    }
+    __nv_bfloat16 *dst = ds_exit + ((int64_t)bh * nc + c) * D * D;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
+        *reinterpret_cast<uint32_t *>(dst + row * 64 + col) = da[kk][x];
+      }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float e0 = eG[nt * 8 + 2 * c4], e1 = eG[nt * 8 + 2 * c4 + 1];
+      dS[nt][0] *= e0; dS[nt][1] *= e1; dS[nt][2] *= e0; dS[nt][3] *= e1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t ao[4];
+      ldsm_x4_t(ct_frag_addr(base + SC_DO, 16 * kk, jb, lane), ao);  // dO^T rows j, k = t
+#pragma unroll
+      for (int nd = 0; nd < 4; ++nd) {
+        uint32_t bm[4], bq[4];
+        ldsm_x4_t(bkn_frag_addr(base + SC_MN, 16 * kk, 16 * nd, lane), bm);
+        ldsm_x4_t(bkn_frag_addr(base + SC_QT, 16 * kk, 16 * nd, lane), bq);
+        mma16816(dS[2 * nd], da[kk], bm[0], bm[1]);
+        mma16816(dS[2 * nd + 1], da[kk], bm[2], bm[3]);
+        mma16816(dS[2 * nd], ao, bq[0], bq[1]);
+        mma16816(dS[2 * nd + 1], ao, bq[2], bq[3]);
+      }
+    }
+  }
+  if (p.dstate0) {
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        *reinterpret_cast<float2 *>(p.dstate0 + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4) =
+            make_float2(dS[nt][2 * hh], dS[nt][2 * hh + 1]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// chunk-parallel gradients
+// ---------------------------------------------------------------------------------------
+constexpr int CK_NT = 256;
+constexpr int O_QS = 0, O_KS = 8192, O_VS = 16384, O_DO = 24576;   // raw bf16 tiles [t][d]
+constexpr int O_GS = 32768;                                         // g -> gamma -> dgamma fp32
+constexpr int O_S0 = 49152, O_UN = 57344, O_DS = 65536;             // S0 [j][d], Unew^T [j][t], dS1 [j][d]
+constexpr int O_KD = 73728, O_QD = 81920, O_KF = 90112, O_KB = 98304;
+constexpr int O_AB = 106496, O_AD = 114688, O_TI = 118784;          // bf16 A off-diag, fp32 A diag, T_ii
+constexpr int O_MK = 120832, O_PB = 129024, O_DR = 137216, O_DP = 145408, O_DK = 153600;
+constexpr int O_RS = 161792;                                        // 8 warps x 256 B staging
+constexpr int O_VEC = O_RS + 8 * 256;
+constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088,
+              V_EG = 2112, V_DB = 2176, V_DGM = 2240, V_FLAG = 2304;
+constexpr int CK_SMEM = O_VEC + (V_FLAG + 4) * 4;
+
+template <typename Tb>
+__global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g4 = lane >> 2, c4 = lane & 3;
+  const int nc = p.nc, idx = blockIdx.x, bh = idx / nc, c = idx % nc;
+  const int b = bh / p.H, h = bh % p.H, T = p.T, H = p.H, t0 = c * C;
+  const uint32_t s_base = smem_u32(sm);
+  const int64_t row_stride = (int64_t)H * D;
+  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
+  float *GS = reinterpret_cast<float *>(sm + O_GS);
+  float *AD = reinterpret_cast<float *>(sm + O_AD);
+  float *vec = reinterpret_cast<float *>(sm + O_VEC);
+  float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
+  float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *dbacc = vec + V_DB, *dgacc = vec + V_DGM;
+  const Tb *betag = (const Tb *)p.beta;
+  int *flags = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc));
+  const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
+  const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
+
+  // ---- P0: loads ----
+  {
+    const __nv_bfloat16 *src[4] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
+                                   (const __nv_bfloat16 *)p.v, (const __nv_bfloat16 *)p.dO};
+    for (int u = tid; u < 4 * 512; u += CK_NT) {
+      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
+      const bool in = t < T;
+      cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
+                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
+    }
+    for (int u = tid; u < 1024; u += CK_NT) {
+      const int r = u >> 4, ch = u & 15, t = t0 + r;
+      const bool in = t < T;
+      cp_async16(s_base + O_GS + r * 256 + ch * 16, p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
+    }
+    for (int u = tid; u < 512; u += CK_NT) {
+      const int r = u >> 3, ch = u & 7;
+      cp_async16(s_base + O_S0 + sw64(r, ch * 8), rec + kSavedS0 + r * 128 + ch * 16, 16);
+      cp_async16(s_base + O_UN + sw64(r, ch * 8), rec + kSavedUnT + r * 128 + ch * 16, 16);
+      cp_async16(s_base + O_DS + sw64(r, ch * 8), ds_exit + r * 64 + ch * 8, 16);
+    }
+    cp_async_commit();
+    if (tid < C) {
+      bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
+      dbacc[tid] = 0.f;
+      dgacc[tid] = 0.f;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+  }
+  // ---- P1: gamma = cumsum(g), guard, per-block vectors ----
+  {
+    const int d = tid & 63, seg = tid >> 6;
+    float acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc += GS[(seg * 16 + r) * 64 + d];
+    part[seg * 64 + d] = acc;
+    __syncthreads();
+    float off = 0.f;
+    for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      off += GS[(seg * 16 + r) * 64 + d];
+      GS[(seg * 16 + r) * 64 + d] = off;
+    }
+    __syncthreads();
+  }
+  int bigloc = 0;
+  if (tid < 64) {
+    float span = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      span = fmaxf(span, GS[(i * 16) * 64 + tid] - GS[(i * 16 + 8) * 64 + tid]);
+      span = fmaxf(span, GS[(i * 16 + 8) * 64 + tid] - GS[(i * 16 + 15) * 64 + tid]);
+    }
+    bigloc = !(span <= kSpanMax);
+  }
+  const int big = __syncthreads_or(bigloc);
+  if (tid == 0) flags[idx] = big;
+  if (big) return;  // redone exactly by the flagged-chunk kernel
+  if (tid < 64) {
+    const int d = tid;
+    const float gC = GS[63 * 64 + d];
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = GS[(i * 16 + 8) * 64 + d];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      refs[i * 64 + d] = r[i];
+      erb[i * 64 + d] = __expf(r[i]);
+      egr[i * 64 + d] = __expf(gC - r[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j <= i ? __expf(r[i] - r[j]) : 0.f;
+    }
+    eG[d] = __expf(gC);
+  }
+  __syncthreads();
+
+  // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma} ----
+  for (int u = tid; u < 512; u += CK_NT) {
+    const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
+    const uint32_t off = sw64(t, d0);
+    const uint4 kq = *reinterpret_cast<const uint4 *>(sm + O_KS + off);
+    const uint4 qq = *reinterpret_cast<const uint4 *>(sm + O_QS + off);
+    const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+    uint32_t okd[4], oqd[4], okf[4], okb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
+      const int d = d0 + 2 * e;
+      const float F0 = __expf(GS[t * 64 + d] - refs[blk * 64 + d]);
+      const float F1 = __expf(GS[t * 64 + d + 1] - refs[blk * 64 + d + 1]);
+      const float i0 = __fdividef(1.f, F0), i1 = __fdividef(1.f, F1);
+      okd[e] = pack_bf16(kf.x * F0, kf.y * F1);
+      oqd[e] = pack_bf16(qf.x * F0, qf.y * F1);
+      okf[e] = pack_bf16(kf.x * i0, kf.y * i1);
+      okb[e] = pack_bf16(kf.x * i0 * egr[blk * 64 + d], kf.y * i1 * egr[blk * 64 + d + 1]);
+    }
+    *reinterpret_cast<uint4 *>(sm + O_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
+    *reinterpret_cast<uint4 *>(sm + O_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
+    *reinterpret_cast<uint4 *>(sm + O_KF + off) = make_uint4(okf[0], okf[1], okf[2], okf[3]);
+    *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
+  }
+  // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
+  {
+    const int d = tid & 63, jq = tid >> 6;
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int row = jq * 16 + j;
+      a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(row, d))) *
+           __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
+    }
+    atomicAdd(&dgacc[d], a * eG[d]);
+  }
+  __syncthreads();
+
+  // ---- P3: M = KD G KF^T (strict lower) and P = QD G KF^T (lower incl.) ----
+  {
+    const int i = warp >> 1, mat = warp & 1;
+    uint32_t af0[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) ldsm_x4(a_frag_addr(s_base + (mat ? O_QD : O_KD), 16 * i, 16 * kk, lane), af0[kk]);
+    for (int j = 0; j <= i; ++j) {
+      float acc[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t af[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) af[x] = af0[kk][x];
+        if (j < i) {  // scale the k = d columns by e^{r_i - r_j}
+          const float *G = gij + (i * 4 + j) * 64;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int d = 16 * kk + (x >> 1) * 8 + 2 * c4;
+            const float2 v = unpack_bf16(af[x]);
+            af[x] = pack_bf16(v.x * G[d], v.y * G[d + 1]);
+          }
+        }
+        uint32_t bf[4];
+        ldsm_x4(bnk_frag_addr(s_base + O_KF, 16 * j, 16 * kk, lane), bf);
+        mma16816(acc[0], af, bf[0], bf[1]);
+        mma16816(acc[1], af, bf[2], bf[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int tl = g4 + 8 * hh, t = 16 * i + tl;
+          const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
+          float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
+          if (mat == 0) {
+            v0 = s < t ? v0 : 0.f;
+            v1 = s + 1 < t ? v1 : 0.f;
+            *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, s)) = pack_bf16(v0, v1);
+            if (j == i) {
+              AD[i * 256 + tl * 16 + sl] = bet[t] * v0;
+              AD[i * 256 + tl * 16 + sl + 1] = bet[t] * v1;
+            } else {
+              *reinterpret_cast<uint32_t *>(sm + O_AB + sw64(t, s)) = pack_bf16(bet[t] * v0, bet[t] * v1);
+            }
+          } else {
+            v0 = s <= t ? v0 : 0.f;
+            v1 = s + 1 <= t ? v1 : 0.f;
+            *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, s)) = pack_bf16(v0, v1);
+          }
+        }
+    }
+  }
+  __syncthreads();
+  // ---- P4: T_ii = (I + A_ii)^{-1} ----
+  if (tid < 64) {
+    const int i = tid >> 4, u = tid & 15;
+    const float *A = AD + i * 256;
+    float x[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float v = t == u ? 1.f : 0.f;
+#pragma unroll
+      for (int s = 0; s < t; ++s) v = fmaf(-A[t * 16 + s], x[s], v);
+      x[t] = v;
+    }
+    __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + O_TI + i * 512);
+#pragma unroll
+    for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
+  }
+  __syncthreads();
+
+  // ---- P5: dU = P^T dO + Kb dS1^T and dR = (I + A)^{-T} dU, 8 value columns per warp ----
+  {
+    const int n0 = warp * 8, l15 = lane & 15;
+    float du[4][4] = {};
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (kk >= mt) {
+          uint32_t af[4], bf[2];
+          ldsm_x4_t(ct_frag_addr(s_base + O_PB, 16 * kk, 16 * mt, lane), af);  // P^T
+          ldsm_x2_t(s_base + O_DO + sw64(16 * kk + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
+          mma16816(du[mt], af, bf[0], bf[1]);
+        }
+        uint32_t af[4], bf[2];
+        ldsm_x4(a_frag_addr(s_base + O_KB, 16 * mt, 16 * kk, lane), af);
+        ldsm_x2(s_base + O_DS + sw64(n0 + (l15 & 7), 16 * kk + ((l15 >> 3) << 3)), bf);
+        mma16816(du[mt], af, bf[0], bf[1]);
+      }
+    }
+    uint8_t *Rm = sm + O_RS + warp * 256;
+    const uint32_t Rs = s_base + O_RS + warp * 256;
+    __nv_bfloat16 *dvg = (__nv_bfloat16 *)p.dv;
+    for (int i = 3; i >= 0; --i) {
+      float z[4] = {du[i][0], du[i][1], du[i][2], du[i][3]};
+      for (int j = i + 1; j < 4; ++j) {
+        uint32_t af[4], bf[2];
+        ldsm_x4_t(ct_frag_addr(s_base + O_AB, 16 * j, 16 * i, lane), af);  // A_ji^T
+        ldsm_x2_t(s_base + O_DR + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
+        float tmp[4] = {};
+        mma16816(tmp, af, bf[0], bf[1]);
+#pragma unroll
+        for (int x = 0; x < 4; ++x) z[x] -= tmp[x];
+      }
+      *reinterpret_cast<uint32_t *>(Rm + g4 * 16 + c4 * 4) = pack_bf16(z[0], z[1]);
+      *reinterpret_cast<uint32_t *>(Rm + (g4 + 8) * 16 + c4 * 4) = pack_bf16(z[2], z[3]);
+      __syncwarp();
+      uint32_t af[4], bf[2];
+      ldsm_x4_t(s_base + O_TI + i * 512 + ((lane & 7) + (lane >> 4) * 8) * 32 + ((lane >> 3) & 1) * 16, af);
+      ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
+      float y[4] = {};
+      mma16816(y, af, bf[0], bf[1]);
+      float dbv[2] = {0.f, 0.f};
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
+        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(t, col)) = pack_bf16(y[2 * hh], y[2 * hh + 1]);
+        const float2 vv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_VS + sw64(t, col)));
+        dbv[hh] = y[2 * hh] * vv.x + y[2 * hh + 1] * vv.y;
+        if (t0 + t < T)
+          *reinterpret_cast<uint32_t *>(dvg + base_bh + (int64_t)(t0 + t) * row_stride + col) =
+              pack_bf16(bet[t] * y[2 * hh], bet[t] * y[2 * hh + 1]);
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float v = dbv[hh];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c4 == 0) atomicAdd(&dbacc[16 * i + g4 + 8 * hh], v);
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+
+  // ---- P6..P8: per warp 16 rows (block mt) x 32 columns (half nh) of dq, dk ----
+  const int mt = warp >> 1, nh = warp & 1;
+  float DQ[4][4], DKp[4][4], DKm[4][4], Fv[4][4];
+  {
+    float dRS[4][4] = {}, dOS[4][4] = {}, dKb[4][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t aR[4], aO[4], aU[4];
+      ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
+      ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
+      ldsm_x4_t(ct_frag_addr(s_base + O_UN, 16 * kk, 16 * mt, lane), aU);  // Unew rows t, k = j
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t bS[4], bD[4];
+        ldsm_x4_t(bkn_frag_addr(s_base + O_S0, 16 * kk, 32 * nh + 16 * np, lane), bS);
+        ldsm_x4_t(bkn_frag_addr(s_base + O_DS, 16 * kk, 32 * nh + 16 * np, lane), bD);
+        mma16816(dRS[2 * np], aR, bS[0], bS[1]);
+        mma16816(dRS[2 * np + 1], aR, bS[2], bS[3]);
+        mma16816(dOS[2 * np], aO, bS[0], bS[1]);
+        mma16816(dOS[2 * np + 1], aO, bS[2], bS[3]);
+        mma16816(dKb[2 * np], aU, bD[0], bD[1]);
+        mma16816(dKb[2 * np + 1], aU, bD[2], bD[3]);
+      }
+    }
+    float dbr[2] = {0.f, 0.f}, dgc[4][2] = {};
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const int t = 16 * mt + g4 + 8 * hh, d = 32 * nh + 8 * nt + 2 * c4 + x, e = 2 * hh + x;
+          const float F = __expf(GS[t * 64 + d] - refs[mt * 64 + d]);
+          const float eg = F * erb[mt * 64 + d], eb = __fdividef(egr[mt * 64 + d], F);
+          const float kv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_KS + sw64(t, d)));
+          Fv[nt][e] = F;
+          DQ[nt][e] = dOS[nt][e] * eg;
+          DKp[nt][e] = -bet[t] * dRS[nt][e] * eg;
+          DKm[nt][e] = dKb[nt][e] * eb;
+          dbr[hh] -= dRS[nt][e] * kv * eg;
+          dgc[nt][x] += kv * DKm[nt][e];
+        }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float v = dbr[hh];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float v = dgc[nt][x];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if (g4 == 0) atomicAdd(&dgacc[32 * nh + 8 * nt + 2 * c4 + x], v);
+      }
+  }
+  // ---- P7: dP = dO Unew^T (s <= t), dKK = -beta dR Unew^T (s < t), dbeta += dA . M ----
+  {
+    float dbr[2] = {0.f, 0.f};
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {
+      const int sb = 2 * nh + np;
+      if (sb > mt) continue;
+      float aP[2][4] = {}, aA[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t aO[4], aR[4], bU[4];
+        ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
+        ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
+        ldsm_x4_t(bkn_frag_addr(s_base + O_UN, 16 * kk, 16 * sb, lane), bU);
+        mma16816(aP[0], aO, bU[0], bU[1]);
+        mma16816(aP[1], aO, bU[2], bU[3]);
+        mma16816(aA[0], aR, bU[0], bU[1]);
+        mma16816(aA[1], aR, bU[2], bU[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int t = 16 * mt + g4 + 8 * hh, s = 16 * sb + 8 * nt + 2 * c4;
+          const float p0 = s <= t ? aP[nt][2 * hh] : 0.f, p1 = s + 1 <= t ? aP[nt][2 * hh + 1] : 0.f;
+          const float a0 = s < t ? -aA[nt][2 * hh] : 0.f, a1 = s + 1 < t ? -aA[nt][2 * hh + 1] : 0.f;
+          *reinterpret_cast<uint32_t *>(sm + O_DP + sw64(t, s)) = pack_bf16(p0, p1);
+          *reinterpret_cast<uint32_t *>(sm + O_DK + sw64(t, s)) = pack_bf16(bet[t] * a0, bet[t] * a1);
+          const float2 m = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_MK + sw64(t, s)));
+          dbr[hh] += a0 * m.x + a1 * m.y;
+        }
+    }
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float v = dbr[hh];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
+    }
+  }
+  __syncthreads();
+  // ---- P8: decayed products ----
+  {
+    float Q2[4][4] = {}, K2[4][4] = {}, M2[4][4] = {};
+    for (int j = 0; j <= mt; ++j) {  // rows t in block mt, columns s in block j
+      float T1[4][4] = {}, T2[4][4] = {};
+      uint32_t aP[4], aK[4];
+      ldsm_x4(a_frag_addr(s_base + O_DP, 16 * mt, 16 * j, lane), aP);
+      ldsm_x4(a_frag_addr(s_base + O_DK, 16 * mt, 16 * j, lane), aK);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t bK[4];
+        ldsm_x4_t(bkn_frag_addr(s_base + O_KF, 16 * j, 32 * nh + 16 * np, lane), bK);
+        mma16816(T1[2 * np], aP, bK[0], bK[1]);
+        mma16816(T1[2 * np + 1], aP, bK[2], bK[3]);
+        mma16816(T2[2 * np], aK, bK[0], bK[1]);
+        mma16816(T2[2 * np + 1], aK, bK[2], bK[3]);
+      }
+      const float *G = gij + (mt * 4 + j) * 64;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float gv = G[32 * nh + 8 * nt + 2 * c4 + (e & 1)];
+          Q2[nt][e] += gv * T1[nt][e];
+          K2[nt][e] += gv * T2[nt][e];
+        }
+    }
+    for (int i = mt; i < 4; ++i) {  // rows s in block mt, sum over t in block i
+      float T3[4][4] = {};
+      uint32_t aKt[4], aPt[4];
+      ldsm_x4_t(ct_frag_addr(s_base + O_DK, 16 * i, 16 * mt, lane), aKt);
+      ldsm_x4_t(ct_frag_addr(s_base + O_DP, 16 * i, 16 * mt, lane), aPt);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t bK[4], bQ[4];
+        ldsm_x4_t(bkn_frag_addr(s_base + O_KD, 16 * i, 32 * nh + 16 * np, lane), bK);
+        ldsm_x4_t(bkn_frag_addr(s_base + O_QD, 16 * i, 32 * nh + 16 * np, lane), bQ);
+        mma16816(T3[2 * np], aKt, bK[0], bK[1]);
+        mma16816(T3[2 * np + 1], aKt, bK[2], bK[3]);
+        mma16816(T3[2 * np], aPt, bQ[0], bQ[1]);
+        mma16816(T3[2 * np + 1], aPt, bQ[2], bQ[3]);
+      }
+      const float *G = gij + (i * 4 + mt) * 64;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) M2[nt][e] += G[32 * nh + 8 * nt + 2 * c4 + (e & 1)] * T3[nt][e];
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        DQ[nt][e] += Fv[nt][e] * Q2[nt][e];
+        DKp[nt][e] += Fv[nt][e] * K2[nt][e];
+        DKm[nt][e] += __fdividef(M2[nt][e], Fv[nt][e]);
+      }
+  }
+  // ---- P9: dgamma, dg = reverse cumsum, outputs ----
+  __syncthreads();  // every warp is done reading gamma, MK and PB
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = 16 * mt + g4 + 8 * hh, d = 32 * nh + 8 * nt + 2 * c4;
+      const float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t, d)));
+      const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
+      const int e = 2 * hh;
+      GS[t * 64 + d] = qv.x * DQ[nt][e] + kv.x * (DKp[nt][e] - DKm[nt][e]);
+      GS[t * 64 + d + 1] = qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]);
+      *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, d)) = pack_bf16(DQ[nt][e], DQ[nt][e + 1]);
+      *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, d)) =
+          pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
+    }
+  __syncthreads();
+  if (tid < 64) {
+    const int d = tid;
+    float acc = dgacc[d];
+    for (int t = C - 1; t >= 0; --t) {
+      acc += GS[t * 64 + d];
+      if (t0 + t < T) p.dg[base_bh + (int64_t)(t0 + t) * row_stride + d] = acc;
+    }
+  } else if (tid < 128) {
+    const int t = tid - 64;
+    if (t0 + t < T) ((Tb *)p.dbeta)[((int64_t)b * T + t0 + t) * H + h] = from_f<Tb>(dbacc[t]);
+  }
+  __nv_bfloat16 *dqg = (__nv_bfloat16 *)p.dq, *dkg = (__nv_bfloat16 *)p.dk;
+  for (int u = tid; u < 512; u += CK_NT) {
+    const int r = u >> 3, ch = u & 7, t = t0 + r;
+    if (t < T) {
+      const int64_t o = base_bh + (int64_t)t * row_stride + ch * 8;
+      *reinterpret_cast<uint4 *>(dqg + o) = *reinterpret_cast<const uint4 *>(sm + O_MK + sw64(r, ch * 8));
+      *reinterpret_cast<uint4 *>(dkg + o) = *reinterpret_cast<const uint4 *>(sm + O_PB + sw64(r, ch * 8));
+    }
+  }
+}
+
+template <typename Tb>
+int launch(const Params &p, cudaStream_t st) {
+  if (cudaFuncSetAttribute(kda_bwd_state_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM))
+    return KDA_ERR_CUDA;
+  kda_bwd_state_scan_kernel<<<p.B * p.H, SC_NT, SC_SMEM, st>>>(p);
+  count_launch();
+  auto kern = kda_bwd_chunks_kernel<Tb>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_SMEM)) return KDA_ERR_CUDA;
+  const int n = p.B * p.H * p.nc;
+  kern<<<n, CK_NT, CK_SMEM, st>>>(p);
+  count_launch();
+  if (cudaPeekAtLastError() != cudaSuccess) return KDA_ERR_CUDA;
+  const int *flags = reinterpret_cast<const int *>((const uint8_t *)p.ws + ws_flags_offset(n));
+  return bwd_flagged_chunks(p, std::is_same<Tb, float>::value ? KDA_F32 : KDA_BF16, flags,
+                            (const __nv_bfloat16 *)p.ws, st);
+}
+
+}  // namespace tcbwd
+
+size_t tc_bwd_workspace_bytes(const KdaDesc *d) {
+  const int64_t n = d->B * d->H * ((d->T + d->chunk - 1) / d->chunk);
+  return tcbwd::ws_flags_offset(n) + (size_t)n * sizeof(int);
+}
+
+int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st) {
+  if (dtype_beta == KDA_BF16) return tcbwd::launch<__nv_bfloat16>(p, st);
+  if (dtype_beta == KDA_F32) return tcbwd::launch<float>(p, st);
+  return KDA_ERR_DTYPE;
+}
+
+}  // namespace kda

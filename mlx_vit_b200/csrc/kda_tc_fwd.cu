@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(NT, 1) kda_fwd_tc_kernel(Params p) {
         stsm_x4_t(ct_frag_addr(ost, 16 * pp, jb, lane), pack_bf16(O[0][0], O[0][1]), pack_bf16(O[0][2], O[0][3]),
                   pack_bf16(O[1][0], O[1][1]), pack_bf16(O[1][2], O[1][3]));
       }
-      // the per-chunk record for the backward: S0 and Unew^T (bf16), Mneg = (-W)^T Kb,
+      // the per-chunk record for the backward: S0 and Unew^T (bf16), Mneg = -Kb^T W,
       // Qt = Qd + P (-W), e^{gamma_C}
       if (p.saved) {
         uint8_t *sv = (uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk;
@@ -165,16 +165,16 @@ __global__ void __launch_bounds__(NT, 1) kda_fwd_tc_kernel(Params p) {
             *reinterpret_cast<uint32_t *>(sv + kSavedS0 + (row * 64 + col) * 2) = sa[kk][x];
             *reinterpret_cast<uint32_t *>(sv + kSavedUnT + (row * 64 + col) * 2) = ua[kk][x];
           }
-        {  // Mneg rows d' in [jb, jb+16)
+        {  // Mneg = Kb^T (-W), rows d' in [jb, jb+16)
           float M[8][4] = {};
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             uint32_t af[4];
-            ldsm_x4_t(ct_frag_addr(ho + HO_W, 16 * kk, jb, lane), af);
+            ldsm_x4_t(ct_frag_addr(ho + HO_KB, 16 * kk, jb, lane), af);
 #pragma unroll
             for (int nd = 0; nd < 4; ++nd) {
               uint32_t bf[4];
-              ldsm_x4_t(bkn_frag_addr(ho + HO_KB, 16 * kk, 16 * nd, lane), bf);
+              ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
               mma16816(M[2 * nd], af, bf[0], bf[1]);
               mma16816(M[2 * nd + 1], af, bf[2], bf[3]);
             }
