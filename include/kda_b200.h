@@ -61,7 +61,8 @@ enum kda_status {
   KDA_ERR_MISALIGNED = -4,    /* pointer not aligned to 16 bytes                   */
   KDA_ERR_WORKSPACE = -5,     /* workspace missing or smaller than required        */
   KDA_ERR_CUDA = -6,          /* a CUDA launch or runtime call failed              */
-  KDA_ERR_TIMEOUT = -7        /* a bounded device-side wait gave up                */
+  KDA_ERR_TIMEOUT = -7,       /* a bounded device-side wait gave up                */
+  KDA_ERR_SCRATCH_LIMIT = -8  /* kda_bwd_noalloc: problem needs more than its scratch */
 };
 
 /* Flags for KdaDesc.flags */
@@ -118,6 +119,24 @@ KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const voi
             const void *saved, const void *dO, const float *dstateT,
             void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
             void *ws, size_t ws_bytes, void *stream);
+
+/* Size of the static device scratch kda_bwd_noalloc uses (32 MiB; enough for about 4000
+ * chunks of 64 tokens x heads, e.g. B=8 H=12 T=1568 needs 2400). */
+#define KDA_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Backward that allocates nothing and takes no workspace: the same computation and arguments
+ * as kda_bwd minus ws/ws_bytes, for callers that cannot call cudaMalloc (a host that owns all
+ * device memory through its own pool, or one that must not trigger the device
+ * synchronisation an allocation can cause).  Its scratch is a static device array of
+ * KDA_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit; a problem
+ * that needs more returns KDA_ERR_SCRATCH_LIMIT.  The first call on a device looks up the
+ * array's address, so make it before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race on it.  No counterpart in the reference. */
+KDA_API int kda_bwd_noalloc(const KdaDesc *desc, const void *q, const void *k, const void *v,
+                            const float *g, const void *beta, const float *state0,
+                            const void *saved, const void *dO, const float *dstateT,
+                            void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
+                            void *stream);
 
 #ifdef __cplusplus
 }

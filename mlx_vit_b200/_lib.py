@@ -19,11 +19,13 @@ KDA_FLAG_FORCE_GENERIC = 0x1
 STATUS = {
     0: "KDA_OK", -1: "KDA_ERR_INVALID_ARG", -2: "KDA_ERR_UNSUPPORTED", -3: "KDA_ERR_DTYPE",
     -4: "KDA_ERR_MISALIGNED", -5: "KDA_ERR_WORKSPACE", -6: "KDA_ERR_CUDA", -7: "KDA_ERR_TIMEOUT",
+    -8: "KDA_ERR_SCRATCH_LIMIT",
 }
+KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 # every symbol include/kda_b200.h declares
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
-           "kda_saved_bytes", "kda_launch_counter", "kda_fwd", "kda_bwd")
+           "kda_saved_bytes", "kda_launch_counter", "kda_fwd", "kda_bwd", "kda_bwd_noalloc")
 
 
 class KdaDesc(ctypes.Structure):
@@ -62,6 +64,8 @@ def _declare(L):
     L.kda_fwd.argtypes = [D] + [P] * 9 + [P, S, P]
     L.kda_bwd.restype = I
     L.kda_bwd.argtypes = [D] + [P] * 15 + [P, S, P]
+    L.kda_bwd_noalloc.restype = I
+    L.kda_bwd_noalloc.argtypes = [D] + [P] * 15 + [P]
 
 
 def lib(path: str | None = None):

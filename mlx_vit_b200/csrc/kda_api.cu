@@ -59,6 +59,7 @@ const char *kda_strerror(int s) {
     case KDA_ERR_WORKSPACE: return "workspace missing or too small (see kda_workspace_bytes)";
     case KDA_ERR_CUDA: return "CUDA launch or runtime error";
     case KDA_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+    case KDA_ERR_SCRATCH_LIMIT: return "problem needs more workspace than kda_bwd_noalloc's static scratch (KDA_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }

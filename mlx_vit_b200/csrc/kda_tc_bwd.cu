@@ -21,6 +21,7 @@
 //                       chunk's decay-weighted M and P, T_ii and dR, and produces all gradients.
 // Chunks whose decay is too strong for the factored form are flagged and redone by the exact
 // fp32 per-chunk kernel (kda_bwd_flagged_chunks_kernel).
+#include <mutex>
 #include <type_traits>
 
 #include "kda_common.cuh"
@@ -655,3 +656,52 @@ int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st) {
 }
 
 }  // namespace kda
+
+// ---------------------------------------------------------------------------------------
+// kda_bwd_noalloc: kda_bwd with the workspace taken from a static device array.
+//
+// Some callers cannot allocate device memory: a host that owns all GPU memory through its own
+// fixed pool and forbids other allocations, or one calling from a context where a cudaMalloc
+// (which may synchronise the device) is not allowed.  This entry point needs no workspace from
+// them.  Its scratch is the file-scope array below, KDA_NOALLOC_SCRATCH_BYTES bytes that every
+// GPU that loads the library keeps until the process exits.  The first call on a device
+// resolves the array's device address (cudaGetSymbolAddress, with that device current); make
+// that first call before any stream capture.  All calls share the one array: calls whose
+// kernels overlap on the GPU (different streams, or two host threads) race on it.  Nothing in
+// it has to start at zero: each call overwrites every byte it reads back.
+// ---------------------------------------------------------------------------------------
+
+static __device__ __align__(256) uint8_t kda_noalloc_scratch[KDA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int kda_bwd_noalloc(const KdaDesc *d, const void *q, const void *k, const void *v,
+                               const float *g, const void *beta, const float *state0,
+                               const void *saved, const void *dO, const float *dstateT, void *dq,
+                               void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
+                               void *stream) {
+  const int s = kda_check_desc(d, 1);
+  if (s) return s;
+  const size_t need = kda_workspace_bytes(d, 1);
+  if (need > (size_t)KDA_NOALLOC_SCRATCH_BYTES) return KDA_ERR_SCRATCH_LIMIT;
+  void *scratch = nullptr;
+  if (need) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KDA_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void *ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, kda_noalloc_scratch) != cudaSuccess || !ptr) return KDA_ERR_CUDA;
+      g_noalloc_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  return kda_bwd(d, q, k, v, g, beta, state0, saved, dO, dstateT, dq, dk, dv, dg, dbeta, dstate0,
+                 scratch, need ? (size_t)KDA_NOALLOC_SCRATCH_BYTES : 0, stream);
+}
+
+
