@@ -356,20 +356,21 @@ kda_bwd_generic_kernel(Params p) {
 // ---------------------------------------------------------------------------------------
 template <typename Tb>
 __global__ void __launch_bounds__(kGenThreads)
-kda_bwd_flagged_chunks_kernel(Params p, const int *flags, const __nv_bfloat16 *ds_exit) {
-  const int idx = blockIdx.x;
-  if (!flags[idx]) return;
+kda_bwd_flagged_chunks_kernel(Params p, const int *flagged, const __nv_bfloat16 *ds_exit) {
   extern __shared__ float sm[];
-  const int D = p.D, nc = p.nc;
-  const int bh = idx / nc, c = idx % nc;
-  float *S0 = sm, *dS = S0 + D * D;
-  const __nv_bfloat16 *s0 = (const __nv_bfloat16 *)((const uint8_t *)p.saved_in +
-                                                    (int64_t)idx * kSavedChunk + kSavedS0);
-  for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
-    S0[i] = __bfloat162float(s0[i]);
-    dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + i]);
+  const int D = p.D, nc = p.nc, count = flagged[0];
+  for (int f = blockIdx.x; f < count; f += gridDim.x) {
+    const int idx = flagged[1 + f], bh = idx / nc, c = idx % nc;
+    float *S0 = sm, *dS = S0 + D * D;
+    const __nv_bfloat16 *s0 = (const __nv_bfloat16 *)((const uint8_t *)p.saved_in +
+                                                      (int64_t)idx * kSavedChunk + kSavedS0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
+      S0[i] = __bfloat162float(s0[i]);
+      dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + i]);
+    }
+    bwd_chunk_body<__nv_bfloat16, Tb>(p, sm, bh, c, false);
   }
-  bwd_chunk_body<__nv_bfloat16, Tb>(p, sm, bh, c, false);
 }
 
 size_t generic_bwd_smem(int D, int C);
@@ -377,7 +378,8 @@ size_t generic_bwd_smem(int D, int C);
 int bwd_flagged_chunks(const Params &p, int dtype_beta, const int *flags,
                        const __nv_bfloat16 *ds_exit, cudaStream_t st) {
   const size_t smem = generic_bwd_smem(p.D, p.C);
-  const int n = p.B * p.H * p.nc;
+  int n = p.B * p.H * p.nc;  // grid: at most one CTA per chunk, at most two per SM
+  if (n > 296) n = 296;
   if (dtype_beta == KDA_BF16) {
     auto kern = kda_bwd_flagged_chunks_kernel<__nv_bfloat16>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) return KDA_ERR_CUDA;

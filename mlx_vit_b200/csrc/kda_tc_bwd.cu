@@ -37,7 +37,8 @@ namespace tcbwd {
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 
-// workspace: exit cotangent per chunk (bf16 [j][d]) then one flag per chunk
+// workspace: exit cotangent per chunk (bf16 [j][d]), then the count and the list of flagged
+// chunks (ints)
 __host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (size_t)nchunks * 8192; }
 
 // ---------------------------------------------------------------------------------------
@@ -58,6 +59,8 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
   const int64_t base_bh = ((int64_t)b * T * H + h) * D;
   const __nv_bfloat16 *dOg = (const __nv_bfloat16 *)p.dO;
   __nv_bfloat16 *ds_exit = (__nv_bfloat16 *)p.ws;
+  if (bh == 0 && tid == 0)  // the chunk kernel that follows appends flagged chunks to a fresh list
+    *reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc)) = 0;
 
   auto issue = [&](int c, int buf) {
     const uint32_t base = s_base + buf * SC_BUF;
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
   float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *dbacc = vec + V_DB, *dgacc = vec + V_DGM;
   const Tb *betag = (const Tb *)p.beta;
-  int *flags = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc));
+  int *flagged = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc));
   const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
   const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
 
@@ -233,8 +236,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     bigloc = !(span <= kSpanMax);
   }
   const int big = __syncthreads_or(bigloc);
-  if (tid == 0) flags[idx] = big;
-  if (big) return;  // redone exactly by the flagged-chunk kernel
+  if (big) {  // redone exactly by the flagged-chunk kernel
+    if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
+    return;
+  }
   if (tid < 64) {
     const int d = tid;
     const float gC = GS[63 * 64 + d];
@@ -292,57 +297,55 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   }
   __syncthreads();
 
-  // ---- P3: M = KD G KF^T (strict lower) and P = QD G KF^T (lower incl.) ----
-  {
-    const int i = warp >> 1, mat = warp & 1;
-    uint32_t af0[4][4];
+  // ---- P3: M = KD G KF^T (strict lower) and P = QD G KF^T (lower incl.); the 20 (block row i,
+  //      block column j <= i, matrix) tasks are spread evenly over the 8 warps ----
+  for (int task = warp; task < 20; task += 8) {
+    const int mat = task & 1, pr = task >> 1;  // pr enumerates (i, j), j <= i
+    const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
+    const int j = pr - i * (i + 1) / 2;
+    float acc[2][4] = {};
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) ldsm_x4(a_frag_addr(s_base + (mat ? O_QD : O_KD), 16 * i, 16 * kk, lane), af0[kk]);
-    for (int j = 0; j <= i; ++j) {
-      float acc[2][4] = {};
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t af[4];
+      ldsm_x4(a_frag_addr(s_base + (mat ? O_QD : O_KD), 16 * i, 16 * kk, lane), af);
+      if (j < i) {  // scale the k = d columns by e^{r_i - r_j}
+        const float *G = gij + (i * 4 + j) * 64;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t af[4];
-#pragma unroll
-        for (int x = 0; x < 4; ++x) af[x] = af0[kk][x];
-        if (j < i) {  // scale the k = d columns by e^{r_i - r_j}
-          const float *G = gij + (i * 4 + j) * 64;
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int d = 16 * kk + (x >> 1) * 8 + 2 * c4;
-            const float2 v = unpack_bf16(af[x]);
-            af[x] = pack_bf16(v.x * G[d], v.y * G[d + 1]);
-          }
+        for (int x = 0; x < 4; ++x) {
+          const int d = 16 * kk + (x >> 1) * 8 + 2 * c4;
+          const float2 v = unpack_bf16(af[x]);
+          const float2 gg = *reinterpret_cast<const float2 *>(G + d);
+          af[x] = pack_bf16(v.x * gg.x, v.y * gg.y);
         }
-        uint32_t bf[4];
-        ldsm_x4(bnk_frag_addr(s_base + O_KF, 16 * j, 16 * kk, lane), bf);
-        mma16816(acc[0], af, bf[0], bf[1]);
-        mma16816(acc[1], af, bf[2], bf[3]);
       }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int tl = g4 + 8 * hh, t = 16 * i + tl;
-          const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
-          float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
-          if (mat == 0) {
-            v0 = s < t ? v0 : 0.f;
-            v1 = s + 1 < t ? v1 : 0.f;
-            *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, s)) = pack_bf16(v0, v1);
-            if (j == i) {
-              AD[i * 256 + tl * 16 + sl] = bet[t] * v0;
-              AD[i * 256 + tl * 16 + sl + 1] = bet[t] * v1;
-            } else {
-              *reinterpret_cast<uint32_t *>(sm + O_AB + sw64(t, s)) = pack_bf16(bet[t] * v0, bet[t] * v1);
-            }
-          } else {
-            v0 = s <= t ? v0 : 0.f;
-            v1 = s + 1 <= t ? v1 : 0.f;
-            *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, s)) = pack_bf16(v0, v1);
-          }
-        }
+      uint32_t bf[4];
+      ldsm_x4(bnk_frag_addr(s_base + O_KF, 16 * j, 16 * kk, lane), bf);
+      mma16816(acc[0], af, bf[0], bf[1]);
+      mma16816(acc[1], af, bf[2], bf[3]);
     }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int tl = g4 + 8 * hh, t = 16 * i + tl;
+        const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
+        float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
+        if (mat == 0) {
+          v0 = s < t ? v0 : 0.f;
+          v1 = s + 1 < t ? v1 : 0.f;
+          *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, s)) = pack_bf16(v0, v1);
+          if (j == i) {
+            AD[i * 256 + tl * 16 + sl] = bet[t] * v0;
+            AD[i * 256 + tl * 16 + sl + 1] = bet[t] * v1;
+          } else {
+            *reinterpret_cast<uint32_t *>(sm + O_AB + sw64(t, s)) = pack_bf16(bet[t] * v0, bet[t] * v1);
+          }
+        } else {
+          v0 = s <= t ? v0 : 0.f;
+          v1 = s + 1 <= t ? v1 : 0.f;
+          *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, s)) = pack_bf16(v0, v1);
+        }
+      }
   }
   __syncthreads();
   // ---- P4: T_ii = (I + A_ii)^{-1} ----
@@ -603,16 +606,23 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
           pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
     }
   __syncthreads();
-  if (tid < 64) {
-    const int d = tid;
+  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up): 4 segments of 16 rows
+    const int d = tid & 63, seg = tid >> 6;
+    float ssum = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) ssum += GS[(seg * 16 + r) * 64 + d];
+    part[seg * 64 + d] = ssum;
+    __syncthreads();
     float acc = dgacc[d];
-    for (int t = C - 1; t >= 0; --t) {
+    for (int s2 = seg + 1; s2 < 4; ++s2) acc += part[s2 * 64 + d];
+#pragma unroll
+    for (int r = 15; r >= 0; --r) {
+      const int t = seg * 16 + r;
       acc += GS[t * 64 + d];
       if (t0 + t < T) p.dg[base_bh + (int64_t)(t0 + t) * row_stride + d] = acc;
     }
-  } else if (tid < 128) {
-    const int t = tid - 64;
-    if (t0 + t < T) ((Tb *)p.dbeta)[((int64_t)b * T + t0 + t) * H + h] = from_f<Tb>(dbacc[t]);
+    if (tid < 64 && t0 + tid < T)
+      ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(dbacc[tid]);
   }
   __nv_bfloat16 *dqg = (__nv_bfloat16 *)p.dq, *dkg = (__nv_bfloat16 *)p.dk;
   for (int u = tid; u < 512; u += CK_NT) {
@@ -646,7 +656,7 @@ int launch(const Params &p, cudaStream_t st) {
 
 size_t tc_bwd_workspace_bytes(const KdaDesc *d) {
   const int64_t n = d->B * d->H * ((d->T + d->chunk - 1) / d->chunk);
-  return tcbwd::ws_flags_offset(n) + (size_t)n * sizeof(int);
+  return tcbwd::ws_flags_offset(n) + (size_t)(n + 1) * sizeof(int);
 }
 
 int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st) {

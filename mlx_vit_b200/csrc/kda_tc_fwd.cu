@@ -451,47 +451,45 @@ __global__ void __launch_bounds__(NT, 1) kda_fwd_tc_kernel(Params p) {
       }
     }
 
-    // ---- (2) M = Kdec Kinc^T (even producer warps) and P = Qdec Kinc^T (odd) ----
-    {
-      const int i = pwarp >> 1, mat = pwarp & 1;
-      uint32_t af[4][4];
+    // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T: the 20 (block row i, block column j <= i,
+    //      matrix) tasks spread evenly over the 8 producer warps ----
+    for (int task = pwarp; task < 20; task += 8) {
+      const int mat = task & 1, pr = task >> 1;
+      const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
+      const int j = pr - i * (i + 1) / 2;
+      if (big && j == i) continue;  // diagonal block already computed exactly
+      float acc[2][4] = {};
+      const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af[kk]);
-      for (int j = 0; j <= i; ++j) {
-        if (big && j == i) break;  // diagonal block already computed exactly
-        float acc[2][4] = {};
-        const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          uint32_t bf[4];
-          ldsm_x4(bnk_frag_addr(kib, 0, 16 * kk, lane), bf);
-          mma16816(acc[0], af[kk], bf[0], bf[1]);
-          mma16816(acc[1], af[kk], bf[2], bf[3]);
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int tl = g4 + 8 * hh, t = 16 * i + tl;
-            const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
-            float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
-            if (mat == 0) {
-              v0 = s < t ? bet[t] * v0 : 0.f;
-              v1 = s + 1 < t ? bet[t] * v1 : 0.f;
-              if (j == i) {
-                AD[i * 256 + tl * 16 + sl] = v0;
-                AD[i * 256 + tl * 16 + sl + 1] = v1;
-              } else {
-                *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
-              }
-            } else {
-              v0 = s <= t ? v0 : 0.f;
-              v1 = s + 1 <= t ? v1 : 0.f;
-              *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
-            }
-          }
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t af[4], bf[4];
+        ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af);
+        ldsm_x4(bnk_frag_addr(kib, 0, 16 * kk, lane), bf);
+        mma16816(acc[0], af, bf[0], bf[1]);
+        mma16816(acc[1], af, bf[2], bf[3]);
       }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int tl = g4 + 8 * hh, t = 16 * i + tl;
+          const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
+          float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
+          if (mat == 0) {
+            v0 = s < t ? bet[t] * v0 : 0.f;
+            v1 = s + 1 < t ? bet[t] * v1 : 0.f;
+            if (j == i) {
+              AD[i * 256 + tl * 16 + sl] = v0;
+              AD[i * 256 + tl * 16 + sl + 1] = v1;
+            } else {
+              *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
+            }
+          } else {
+            v0 = s <= t ? v0 : 0.f;
+            v1 = s + 1 <= t ? v1 : 0.f;
+            *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
+          }
+        }
     }
     bar_sync(BAR_PROD, NPROD);
 
