@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
 // ---------------------------------------------------------------------------------------
 constexpr int CK_NT = 256;
 constexpr int O_QS = 0, O_KS = 8192, O_VS = 16384, O_DO = 24576;   // raw bf16 tiles [t][d]
-constexpr int O_GS = 32768;                                         // g -> gamma -> dgamma fp32
+constexpr int O_GS = 32768;                                         // g -> gamma -> F -> dgamma fp32
 constexpr int O_S0 = 49152, O_UN = 57344, O_DS = 65536;             // S0 [j][d], Unew^T [j][t], dS1 [j][d]
 constexpr int O_KD = 73728, O_QD = 81920, O_KF = 90112, O_KB = 98304;
 constexpr int O_AB = 106496, O_AD = 114688, O_TI = 118784;          // bf16 A off-diag, fp32 A diag, T_ii
@@ -178,11 +178,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
   const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
 
-  // ---- P0: loads ----
+  // ---- P0: loads in two groups: q, k, g first (for P1-P4), the rest lands behind P1-P4 ----
   {
     const __nv_bfloat16 *src[4] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
                                    (const __nv_bfloat16 *)p.v, (const __nv_bfloat16 *)p.dO};
-    for (int u = tid; u < 4 * 512; u += CK_NT) {
+    for (int u = tid; u < 2 * 512; u += CK_NT) {
       const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
       const bool in = t < T;
       cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
@@ -192,6 +192,13 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       const int r = u >> 4, ch = u & 15, t = t0 + r;
       const bool in = t < T;
       cp_async16(s_base + O_GS + r * 256 + ch * 16, p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
+    }
+    cp_async_commit();
+    for (int u = tid; u < 2 * 512; u += CK_NT) {
+      const int which = 2 + (u >> 9), r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
+      const bool in = t < T;
+      cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
+                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
     }
     for (int u = tid; u < 512; u += CK_NT) {
       const int r = u >> 3, ch = u & 7;
@@ -205,7 +212,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       dbacc[tid] = 0.f;
       dgacc[tid] = 0.f;
     }
-    cp_async_wait_all();
+    cp_async_wait_group<1>();
     __syncthreads();
   }
   // ---- P1: gamma = cumsum(g), guard, per-block vectors ----
@@ -238,6 +245,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const int big = __syncthreads_or(bigloc);
   if (big) {  // redone exactly by the flagged-chunk kernel
     if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
+    cp_async_wait_group<0>();  // leave no copy in flight into this CTA's shared memory
     return;
   }
   if (tid < 64) {
@@ -272,6 +280,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       const int d = d0 + 2 * e;
       const float F0 = __expf(GS[t * 64 + d] - refs[blk * 64 + d]);
       const float F1 = __expf(GS[t * 64 + d + 1] - refs[blk * 64 + d + 1]);
+      GS[t * 64 + d] = F0;  // from here on GS holds F = e^{gamma - r_b(t)}
+      GS[t * 64 + d + 1] = F1;
       const float i0 = __fdividef(1.f, F0), i1 = __fdividef(1.f, F1);
       okd[e] = pack_bf16(kf.x * F0, kf.y * F1);
       oqd[e] = pack_bf16(qf.x * F0, qf.y * F1);
@@ -282,18 +292,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     *reinterpret_cast<uint4 *>(sm + O_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
     *reinterpret_cast<uint4 *>(sm + O_KF + off) = make_uint4(okf[0], okf[1], okf[2], okf[3]);
     *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
-  }
-  // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
-  {
-    const int d = tid & 63, jq = tid >> 6;
-    float a = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int row = jq * 16 + j;
-      a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(row, d))) *
-           __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
-    }
-    atomicAdd(&dgacc[d], a * eG[d]);
   }
   __syncthreads();
 
@@ -366,6 +364,21 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   }
   __syncthreads();
 
+  // ---- the second load group (v, dO, S0, Unew^T, dS1) ----
+  cp_async_wait_group<0>();
+  __syncthreads();
+  // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
+  {
+    const int d = tid & 63, jq = tid >> 6;
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int row = jq * 16 + j;
+      a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(row, d))) *
+           __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
+    }
+    atomicAdd(&dgacc[d], a * eG[d]);
+  }
   // ---- P5: dU = P^T dO + Kb dS1^T and dR = (I + A)^{-T} dU, 8 value columns per warp ----
   {
     const int n0 = warp * 8, l15 = lane & 15;
@@ -463,7 +476,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int t = 16 * mt + g4 + 8 * hh, d = 32 * nh + 8 * nt + 2 * c4 + x, e = 2 * hh + x;
-          const float F = __expf(GS[t * 64 + d] - refs[mt * 64 + d]);
+          const float F = GS[t * 64 + d];
           const float eg = F * erb[mt * 64 + d], eb = __fdividef(egr[mt * 64 + d], F);
           const float kv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_KS + sw64(t, d)));
           Fv[nt][e] = F;
