@@ -181,6 +181,8 @@ def run_ours(args, rank, world, local_rank):
     saved = torch.empty(L.kda_saved_bytes(ctypes.byref(desc)), dtype=torch.uint8, device=dev)
     nws = L.kda_workspace_bytes(ctypes.byref(desc), 1)
     ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+    nwsf = L.kda_workspace_bytes(ctypes.byref(desc), 0)
+    wsf = torch.empty(max(nwsf, 16), dtype=torch.uint8, device=dev)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
     dg = torch.empty_like(g)
     db = torch.empty_like(beta)
@@ -188,7 +190,7 @@ def run_ours(args, rank, world, local_rank):
 
     def fwd_call():
         st = L.kda_fwd(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(S0),
-                       _ptr(o), _ptr(S_T), _ptr(saved), None, 0,
+                       _ptr(o), _ptr(S_T), _ptr(saved), _ptr(wsf), nwsf,
                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _lib.check(st, "kda_fwd")
 

@@ -97,6 +97,12 @@ KDA_API size_t kda_workspace_bytes(const KdaDesc *desc, int backward);
  * Returns 0 on an invalid descriptor. */
 KDA_API size_t kda_saved_bytes(const KdaDesc *desc);
 
+/* Device-side status of the current device: KDA_ERR_TIMEOUT if a bounded wait inside a
+ * kernel gave up since the last reset (the kernel then skipped its remaining work), else 0.
+ * Synchronises the current device; with reset != 0 it also clears the status.
+ * No reference counterpart (the reference has no device-side waits). */
+KDA_API int kda_device_status(int reset);
+
 /* Number of kernels this library has launched in this process (instrumentation; used by
  * benchmarks to count device launches inside a timed region).  No reference counterpart. */
 KDA_API uint64_t kda_launch_counter(void);

@@ -25,7 +25,8 @@ KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 # every symbol include/kda_b200.h declares
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
-           "kda_saved_bytes", "kda_launch_counter", "kda_fwd", "kda_bwd", "kda_bwd_noalloc")
+           "kda_saved_bytes", "kda_launch_counter", "kda_device_status", "kda_fwd", "kda_bwd",
+           "kda_bwd_noalloc")
 
 
 class KdaDesc(ctypes.Structure):
@@ -58,6 +59,8 @@ def _declare(L):
     L.kda_workspace_bytes.argtypes = [D, I]
     L.kda_saved_bytes.restype = S
     L.kda_saved_bytes.argtypes = [D]
+    L.kda_device_status.restype = I
+    L.kda_device_status.argtypes = [I]
     L.kda_launch_counter.restype = ctypes.c_uint64
     L.kda_launch_counter.argtypes = []
     L.kda_fwd.restype = I

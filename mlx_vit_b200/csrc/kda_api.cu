@@ -14,6 +14,8 @@ size_t generic_bwd_smem(int D, int C);
 bool tc_supported(const KdaDesc *d, int backward);
 size_t tc_workspace_bytes(const KdaDesc *d, int backward);
 size_t tc_saved_bytes(const KdaDesc *d);
+int tc_fwd_device_status(bool reset);
+int tc_bwd_device_status(bool reset);
 int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st);
 int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st);
 static std::atomic<uint64_t> g_launches{0};
@@ -46,6 +48,12 @@ static bool use_tc(const KdaDesc *d, int backward) {
 extern "C" {
 
 int kda_abi_version(void) { return KDA_ABI_VERSION; }
+
+int kda_device_status(int reset) {
+  const int f = kda::tc_fwd_device_status(reset != 0);
+  const int b = kda::tc_bwd_device_status(reset != 0);
+  return f ? f : b;
+}
 
 uint64_t kda_launch_counter(void) { return kda::g_launches.load(std::memory_order_relaxed); }
 

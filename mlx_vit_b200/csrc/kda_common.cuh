@@ -30,7 +30,8 @@ struct Params {
 
 // Per-chunk record the tensor-core forward saves for the tensor-core backward (D = C = 64):
 // S0 = chunk-entry state [j][d], Unew^T [j][t], Mneg = -Kb^T W [d'][d], Qt = Qd - P W [t][d]
-// (all bf16, row-major) and e^{gamma_C} [d] (fp32).  With them the state cotangent obeys
+// (all bf16, 64 x 64 with the 128-byte row swizzle of the shared-memory tiles, so that one
+// bulk copy lands them ready for ldmatrix) and e^{gamma_C} [d] (fp32).  With them the state cotangent obeys
 //   dS_entry = dS_exit diag(e^{gamma_C}) + dS_exit Mneg + dO^T Qt.
 constexpr int kSavedS0 = 0, kSavedUnT = 8192, kSavedM = 16384, kSavedQt = 24576, kSavedEG = 32768;
 constexpr int kSavedChunk = 32768 + 256;

@@ -365,9 +365,11 @@ kda_bwd_flagged_chunks_kernel(Params p, const int *flagged, const __nv_bfloat16 
     const __nv_bfloat16 *s0 = (const __nv_bfloat16 *)((const uint8_t *)p.saved_in +
                                                       (int64_t)idx * kSavedChunk + kSavedS0);
     __syncthreads();
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {
-      S0[i] = __bfloat162float(s0[i]);
-      dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + i]);
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {  // records are 128-byte swizzled
+      const int row = i / 64, col = i % 64;
+      const int sw = row * 64 + ((((col >> 3) ^ row) & 7) << 3) + (col & 7);
+      S0[i] = __bfloat162float(s0[sw]);
+      dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + sw]);
     }
     bwd_chunk_body<__nv_bfloat16, Tb>(p, sm, bh, c, false);
   }

@@ -12,7 +12,10 @@ bool tc_supported(const KdaDesc *d, int backward) {
          (d->dtype_beta == KDA_BF16 || d->dtype_beta == KDA_F32);
 }
 size_t tc_bwd_workspace_bytes(const KdaDesc *d);
-size_t tc_workspace_bytes(const KdaDesc *d, int backward) { return backward ? tc_bwd_workspace_bytes(d) : 0; }
+size_t tc_fwd_workspace_bytes(const KdaDesc *d);
+size_t tc_workspace_bytes(const KdaDesc *d, int backward) {
+  return backward ? tc_bwd_workspace_bytes(d) : tc_fwd_workspace_bytes(d);
+}
 size_t tc_saved_bytes(const KdaDesc *d) {
   const int64_t nc = (d->T + d->chunk - 1) / d->chunk;
   return (size_t)(d->B * d->H * nc) * kSavedChunk;

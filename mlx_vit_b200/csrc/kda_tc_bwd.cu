@@ -34,6 +34,9 @@ int bwd_flagged_chunks(const Params &p, int dtype_beta, const int *flags,
 
 namespace tcbwd {
 
+// set to a KDA_ERR_* code by a bounded wait that gave up (read by kda_device_status)
+static __device__ int g_bwd_status;
+
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 
@@ -46,7 +49,8 @@ __host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (siz
 // ---------------------------------------------------------------------------------------
 constexpr int SC_NT = 128;
 constexpr int SC_DO = 0, SC_MN = 8192, SC_QT = 16384, SC_EG = 24576, SC_BUF = 24576 + 256;
-constexpr int SC_SMEM = 2 * SC_BUF;
+constexpr int SC_MBAR = 2 * SC_BUF;
+constexpr int SC_SMEM = SC_MBAR + 16;
 
 __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -62,17 +66,27 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
   if (bh == 0 && tid == 0)  // the chunk kernel that follows appends flagged chunks to a fresh list
     *reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc)) = 0;
 
+  const uint32_t mbar = s_base + SC_MBAR;
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar + 8, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // dO rows (strided in [B, T, H, D]) by cp.async; Mneg, Qt, e^{gamma_C} (one contiguous,
+  // already swizzled span of the saved record) by one bulk copy
   auto issue = [&](int c, int buf) {
     const uint32_t base = s_base + buf * SC_BUF;
     const uint8_t *rec = (const uint8_t *)p.saved_in + ((int64_t)bh * nc + c) * kSavedChunk;
+    if (tid == 0) {
+      mbar_expect_tx(mbar + buf * 8, kSavedChunk - kSavedM);
+      bulk_g2s(base + SC_MN, rec + kSavedM, kSavedChunk - kSavedM, mbar + buf * 8);
+    }
     for (int u = tid; u < 512; u += SC_NT) {
       const int r = u >> 3, ch = u & 7, t = c * C + r;
       const bool in = t < T;
       cp_async16(base + SC_DO + sw64(r, ch * 8), dOg + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
-      cp_async16(base + SC_MN + sw64(r, ch * 8), rec + kSavedM + r * 128 + ch * 16, 16);
-      cp_async16(base + SC_QT + sw64(r, ch * 8), rec + kSavedQt + r * 128 + ch * 16, 16);
     }
-    if (tid < 16) cp_async16(base + SC_EG + tid * 16, rec + kSavedEG + tid * 16, 16);
     cp_async_commit();
   };
 
@@ -91,7 +105,10 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
   for (int i = 0; i < nc; ++i) {
     const int c = nc - 1 - i, buf = i & 1;
     cp_async_wait_all();
-    __syncthreads();
+    if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (i >> 1) & 1))) {
+      if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+      return;
+    }
     if (i + 1 < nc) issue(c - 1, buf ^ 1);
     const uint32_t base = s_base + buf * SC_BUF;
     const float *eG = reinterpret_cast<const float *>(sm + buf * SC_BUF + SC_EG);
@@ -109,7 +126,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
 #pragma unroll
       for (int x = 0; x < 4; ++x) {
         const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
-        *reinterpret_cast<uint32_t *>(dst + row * 64 + col) = da[kk][x];
+        *reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(dst) + sw64(row, col)) = da[kk][x];
       }
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
@@ -156,7 +173,8 @@ constexpr int O_RS = 161792;                                        // 8 warps x
 constexpr int O_VEC = O_RS + 8 * 256;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088,
               V_EG = 2112, V_DB = 2176, V_DGM = 2240, V_FLAG = 2304;
-constexpr int CK_SMEM = O_VEC + (V_FLAG + 4) * 4;
+constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;
+constexpr int CK_SMEM = O_MBAR + 8;
 
 template <typename Tb>
 __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
@@ -200,11 +218,13 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
                  src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
     }
-    for (int u = tid; u < 512; u += CK_NT) {
-      const int r = u >> 3, ch = u & 7;
-      cp_async16(s_base + O_S0 + sw64(r, ch * 8), rec + kSavedS0 + r * 128 + ch * 16, 16);
-      cp_async16(s_base + O_UN + sw64(r, ch * 8), rec + kSavedUnT + r * 128 + ch * 16, 16);
-      cp_async16(s_base + O_DS + sw64(r, ch * 8), ds_exit + r * 64 + ch * 8, 16);
+    if (tid == 0) {  // S0 and Unew^T (adjacent in the saved record) and dS1, already swizzled
+      const uint32_t mbar = s_base + O_MBAR;
+      mbar_init(mbar, 1);
+      mbar_fence_init();
+      mbar_expect_tx(mbar, 3 * 8192);
+      bulk_g2s(s_base + O_S0, rec + kSavedS0, 2 * 8192, mbar);
+      bulk_g2s(s_base + O_DS, ds_exit, 8192, mbar);
     }
     cp_async_commit();
     if (tid < C) {
@@ -246,6 +266,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   if (big) {  // redone exactly by the flagged-chunk kernel
     if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
     cp_async_wait_group<0>();  // leave no copy in flight into this CTA's shared memory
+    mbar_wait(s_base + O_MBAR, 0);
     return;
   }
   if (tid < 64) {
@@ -366,7 +387,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
 
   // ---- the second load group (v, dO, S0, Unew^T, dS1) ----
   cp_async_wait_group<0>();
-  __syncthreads();
+  if (__syncthreads_or(!mbar_wait(s_base + O_MBAR, 0))) {
+    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+    return;
+  }
   // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
   {
     const int d = tid & 63, jq = tid >> 6;
@@ -666,6 +690,16 @@ int launch(const Params &p, cudaStream_t st) {
 }
 
 }  // namespace tcbwd
+
+int tc_bwd_device_status(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tcbwd::g_bwd_status, sizeof(int)) != cudaSuccess) return KDA_ERR_CUDA;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(tcbwd::g_bwd_status, &z, sizeof(int)) != cudaSuccess) return KDA_ERR_CUDA;
+  }
+  return v;
+}
 
 size_t tc_bwd_workspace_bytes(const KdaDesc *d) {
   const int64_t n = d->B * d->H * ((d->T + d->chunk - 1) / d->chunk);

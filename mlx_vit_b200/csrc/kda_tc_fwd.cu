@@ -1,25 +1,25 @@
-// Tensor-core KDA forward for D = 64, chunk = 64, bf16 q/k/v: one CTA per (b, h) walks the
-// chunks of its sequence; inputs are read from HBM exactly once and the state never leaves
-// the SM.
+// Tensor-core KDA forward for D = 64, chunk = 64, bf16 q/k/v, in two kernels.
 //
-// Warp roles (384 threads):
-//   warps 4..11 (producers) build chunk c+1's state-independent operands while
-//   warps 0..3  (scan)      advance the state through chunk c;
-// the two groups hand over double-buffered shared-memory tiles through named barriers.
+//  kda_fwd_chunks  one CTA per (b, h, chunk), all independent (fills all SMs): every
+//                  state-independent quantity of the chunk, written as a per-chunk record
+//                  (-W, U, Qd, Kb, P as bf16 tiles, e^{gamma_C}) to the forward workspace,
+//                  and, for training, the state-independent part of the backward's record
+//                  (Mneg = -Kb^T W, Qt = Qd - P W).
+//  kda_fwd_scan    one CTA of 4 warps per (b, h): streams the chunk records (double-buffered
+//                  cp.async) and advances the fp32 state, which each warp keeps as 16 rows of
+//                  mma accumulator registers:
+//                    Unew^T = U^T - S W^T;  O^T = S Qd^T + Unew^T P^T;  S <- S diag(e^{gamma_C}) + Unew^T Kb
 //
-// Per chunk (gamma = cumsum(g) inside the chunk, rows t, 16-row blocks b(t), r_i = gamma at the
-// middle row of block i):
+// Chunk quantities (gamma = cumsum(g) inside the chunk, rows t, 16-row blocks b(t), r_i = gamma
+// at the middle row of block i):
 //  1. operand build (elementwise): Kdec = k e^{gamma - r_b(t)}, Qdec = q e^{...},
 //     Kinc[i][j] = k_s e^{r_i - gamma_s} (s in block j <= i), beta k e^gamma, beta v,
 //     Qd = q e^gamma, Kb = k e^{gamma_C - gamma}; one exp and one reciprocal per element, the
 //     other factors are products with per-block vectors e^{r_i}, e^{gamma_C - r_i}, e^{r_i - r_j}
-//  2. M = Kdec Kinc^T, P = Qdec Kinc^T per row block (mma.sync): the decay-weighted K K^T and
+//  2. M = Kdec Kinc^T, P = Qdec Kinc^T per block pair (mma.sync): the decay-weighted K K^T and
 //     Q K^T with both factors of e^{gamma_t - gamma_s} bounded; A = beta M (strict lower)
 //  3. T_ii = (I + A_ii)^{-1} for the four 16x16 diagonal blocks (fp32 substitution)
 //  4. block forward substitution W = (I+A)^{-1} beta Kd, U = (I+A)^{-1} beta V (mma.sync)
-//  5. scan (4 warps, each owning 16 rows of the fp32 state S in mma accumulator registers):
-//        Unew^T = U^T - S W^T;  O^T = S Qd^T + Unew^T P^T;  S <- S diag(e^{gamma_C}) + Unew^T Kb
-//     and, for training, the per-chunk record the backward reads (kSaved* layout).
 // This is the chunkwise WY algebra of the reference's chunkwise path (nope_gdn_mlx.py:549-613,
 // 2318-2456) with U = (I+A)^{-1} beta (V - K_proj S^T) split into U - W S^T.
 #include "kda_common.cuh"
@@ -28,21 +28,22 @@
 namespace kda {
 namespace tcfwd {
 
+// set to a KDA_ERR_* code by a bounded wait that gave up (read by kda_device_status)
+static __device__ int g_fwd_status;
+
 constexpr int C = 64, D = 64;
-constexpr int NSCAN = 128, NPROD = 256, NT = NSCAN + NPROD;
 constexpr float kSpanMax = 60.f;
 
-// named barriers (0 is __syncthreads)
-constexpr int BAR_PROD = 1, BAR_SCAN = 2, BAR_FULL = 3 /* +buf */, BAR_EMPTY = 5 /* +buf */;
-
-// ---- shared memory layout (bytes) ----
-// handoff set, double-buffered: -W, U, Qd, Kb, P tiles + e^{gamma_C}
+// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, row-major)
 constexpr int HO_W = 0, HO_U = 8192, HO_QD = 16384, HO_KB = 24576, HO_P = 32768, HO_EG = 40960;
 constexpr int HO_SIZE = 40960 + 256;
-constexpr int OFF_HO = 0;                                // 2 x HO_SIZE
-constexpr int OFF_O = OFF_HO + 2 * HO_SIZE;              // O staging, 2 x 8 KB
-// producer scratch
-constexpr int OFF_QS = OFF_O + 2 * 8192;                 // raw q/k/v tiles (bf16, swizzled)
+
+// ---------------------------------------------------------------------------------------
+// kda_fwd_chunks
+// ---------------------------------------------------------------------------------------
+constexpr int NT1 = 512;  // 16 warps: every phase splits into more independent pieces
+constexpr int OFF_OUT = 0;                               // the record, swizzled tiles
+constexpr int OFF_QS = OFF_OUT + HO_SIZE;                // raw q/k/v tiles (bf16, swizzled)
 constexpr int OFF_KS = OFF_QS + 8192;
 constexpr int OFF_VS = OFF_KS + 8192;
 constexpr int OFF_GS = OFF_VS + 8192;                    // g -> gamma (fp32 [t][d]) 16 KB
@@ -54,530 +55,560 @@ constexpr int OFF_AD = OFF_AB + 8192;                    // A diagonal blocks fp
 constexpr int OFF_TI = OFF_AD + 4096;                    // T_ii bf16 4x16x16
 constexpr int OFF_XK = OFF_TI + 2048;                    // beta Kd
 constexpr int OFF_XV = OFF_XK + 8192;                    // beta V
-constexpr int OFF_RS = OFF_XV + 8192;                    // per-producer-warp 16x16 staging
-constexpr int OFF_VEC = OFF_RS + 8 * 512;
-// vectors (floats): bet[64] refs[4][64] part[4][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
-constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088,
-              V_FLAG = 2112;
-constexpr int SMEM = OFF_VEC + (2112 + 4) * 4;
+constexpr int OFF_RS = OFF_XV + 8192;                    // per-warp 16x16 staging
+constexpr int OFF_VEC = OFF_RS + 16 * 256;
+// vectors (floats): bet[64] refs[4][64] part[8][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
+constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
+              V_FLAG = 2368;
+constexpr int SMEM1 = OFF_VEC + (2368 + 4) * 4;
 
 __device__ __forceinline__ int ki_index(int i, int j) { return i * (i + 1) / 2 + j; }
 
 template <typename Tb>
-__global__ void __launch_bounds__(NT, 1) kda_fwd_tc_kernel(Params p) {
+__global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  const int T = p.T, H = p.H, nc = p.nc;
-  const uint32_t s_base = smem_u32(sm);
   const int g4 = lane >> 2, c4 = lane & 3;
-  const int64_t row_stride = (int64_t)H * D;  // elements between consecutive t
+  const int nc = p.nc, idx = blockIdx.x, bh = idx / nc, c = idx % nc;
+  const int b = bh / p.H, h = bh % p.H, T = p.T, H = p.H, t0 = c * C;
+  const uint32_t s_base = smem_u32(sm);
+  const int64_t row_stride = (int64_t)H * D;
   const int64_t base_bh = ((int64_t)b * T * H + h) * D;
-
-  if (warp < 4) {
-    // =============================== scan group ===============================
-    const int jb = warp * 16;
-    float S[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float2 v = make_float2(0.f, 0.f);
-        if (p.state0)
-          v = *reinterpret_cast<const float2 *>(p.state0 + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4);
-        S[nt][2 * hh] = v.x;
-        S[nt][2 * hh + 1] = v.y;
-      }
-    __nv_bfloat16 *og = (__nv_bfloat16 *)p.o;
-    for (int c = 0; c < nc; ++c) {
-      const int buf = c & 1;
-      const uint32_t ho = s_base + OFF_HO + buf * HO_SIZE;
-      const float *eG = reinterpret_cast<const float *>(sm + OFF_HO + buf * HO_SIZE + HO_EG);
-      const uint32_t ost = s_base + OFF_O + buf * 8192;
-      bar_sync(BAR_FULL + buf, NT);
-
-      uint32_t sa[4][4];  // S as bf16 A fragments (rows j, k = d)
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        sa[kk][0] = pack_bf16(S[2 * kk][0], S[2 * kk][1]);
-        sa[kk][1] = pack_bf16(S[2 * kk][2], S[2 * kk][3]);
-        sa[kk][2] = pack_bf16(S[2 * kk + 1][0], S[2 * kk + 1][1]);
-        sa[kk][3] = pack_bf16(S[2 * kk + 1][2], S[2 * kk + 1][3]);
-      }
-      uint32_t ua[4][4];  // Unew^T as A fragments (rows j, k = t)
-      {
-        float X[8][4];  // Unew^T = U^T + S (-W)^T
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp) {
-          uint32_t r[4];
-          ldsm_x4_t(ct_frag_addr(ho + HO_U, 16 * pp, jb, lane), r);
-          const float2 a = unpack_bf16(r[0]), bq = unpack_bf16(r[1]), cq = unpack_bf16(r[2]), dq = unpack_bf16(r[3]);
-          X[2 * pp][0] = a.x; X[2 * pp][1] = a.y; X[2 * pp][2] = bq.x; X[2 * pp][3] = bq.y;
-          X[2 * pp + 1][0] = cq.x; X[2 * pp + 1][1] = cq.y; X[2 * pp + 1][2] = dq.x; X[2 * pp + 1][3] = dq.y;
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-          for (int pp = 0; pp < 4; ++pp) {
-            uint32_t bf[4];
-            ldsm_x4(bnk_frag_addr(ho + HO_W, 16 * pp, 16 * kk, lane), bf);
-            mma16816(X[2 * pp], sa[kk], bf[0], bf[1]);
-            mma16816(X[2 * pp + 1], sa[kk], bf[2], bf[3]);
-          }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          ua[kk][0] = pack_bf16(X[2 * kk][0], X[2 * kk][1]);
-          ua[kk][1] = pack_bf16(X[2 * kk][2], X[2 * kk][3]);
-          ua[kk][2] = pack_bf16(X[2 * kk + 1][0], X[2 * kk + 1][1]);
-          ua[kk][3] = pack_bf16(X[2 * kk + 1][2], X[2 * kk + 1][3]);
-        }
-      }
-      // O^T = S Qd^T + Unew^T P^T  (16 t-columns at a time)
-#pragma unroll
-      for (int pp = 0; pp < 4; ++pp) {
-        float O[2][4] = {};
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          uint32_t bf[4];
-          ldsm_x4(bnk_frag_addr(ho + HO_QD, 16 * pp, 16 * kk, lane), bf);
-          mma16816(O[0], sa[kk], bf[0], bf[1]);
-          mma16816(O[1], sa[kk], bf[2], bf[3]);
-        }
-#pragma unroll
-        for (int kk = 0; kk <= pp; ++kk) {
-          uint32_t bf[4];
-          ldsm_x4(bnk_frag_addr(ho + HO_P, 16 * pp, 16 * kk, lane), bf);
-          mma16816(O[0], ua[kk], bf[0], bf[1]);
-          mma16816(O[1], ua[kk], bf[2], bf[3]);
-        }
-        stsm_x4_t(ct_frag_addr(ost, 16 * pp, jb, lane), pack_bf16(O[0][0], O[0][1]), pack_bf16(O[0][2], O[0][3]),
-                  pack_bf16(O[1][0], O[1][1]), pack_bf16(O[1][2], O[1][3]));
-      }
-      // the per-chunk record for the backward: S0 and Unew^T (bf16), Mneg = -Kb^T W,
-      // Qt = Qd + P (-W), e^{gamma_C}
-      if (p.saved) {
-        uint8_t *sv = (uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
-            *reinterpret_cast<uint32_t *>(sv + kSavedS0 + (row * 64 + col) * 2) = sa[kk][x];
-            *reinterpret_cast<uint32_t *>(sv + kSavedUnT + (row * 64 + col) * 2) = ua[kk][x];
-          }
-        {  // Mneg = Kb^T (-W), rows d' in [jb, jb+16)
-          float M[8][4] = {};
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            uint32_t af[4];
-            ldsm_x4_t(ct_frag_addr(ho + HO_KB, 16 * kk, jb, lane), af);
-#pragma unroll
-            for (int nd = 0; nd < 4; ++nd) {
-              uint32_t bf[4];
-              ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
-              mma16816(M[2 * nd], af, bf[0], bf[1]);
-              mma16816(M[2 * nd + 1], af, bf[2], bf[3]);
-            }
-          }
-#pragma unroll
-          for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
-              *reinterpret_cast<uint32_t *>(sv + kSavedM + ((jb + g4 + 8 * hh) * 64 + nt * 8 + 2 * c4) * 2) =
-                  pack_bf16(M[nt][2 * hh], M[nt][2 * hh + 1]);
-        }
-        {  // Qt rows t in [jb, jb+16): Qd + P (-W)
-          float Q[8][4];
-#pragma unroll
-          for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const float2 v = unpack_bf16(*reinterpret_cast<const uint32_t *>(
-                  sm + OFF_HO + buf * HO_SIZE + HO_QD + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)));
-              Q[nt][2 * hh] = v.x;
-              Q[nt][2 * hh + 1] = v.y;
-            }
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            if (kk > warp) break;
-            uint32_t af[4];
-            ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);
-#pragma unroll
-            for (int nd = 0; nd < 4; ++nd) {
-              uint32_t bf[4];
-              ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
-              mma16816(Q[2 * nd], af, bf[0], bf[1]);
-              mma16816(Q[2 * nd + 1], af, bf[2], bf[3]);
-            }
-          }
-#pragma unroll
-          for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
-              *reinterpret_cast<uint32_t *>(sv + kSavedQt + ((jb + g4 + 8 * hh) * 64 + nt * 8 + 2 * c4) * 2) =
-                  pack_bf16(Q[nt][2 * hh], Q[nt][2 * hh + 1]);
-        }
-        if (tid < 64) reinterpret_cast<float *>(sv + kSavedEG)[tid] = eG[tid];
-      }
-      // S <- S diag(e^gamma_C) + Unew^T Kb
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const float e0 = eG[nt * 8 + 2 * c4], e1 = eG[nt * 8 + 2 * c4 + 1];
-        S[nt][0] *= e0; S[nt][1] *= e1; S[nt][2] *= e0; S[nt][3] *= e1;
-      }
-#pragma unroll
-      for (int nd = 0; nd < 4; ++nd)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          uint32_t bf[4];
-          ldsm_x4_t(bkn_frag_addr(ho + HO_KB, 16 * kk, 16 * nd, lane), bf);
-          mma16816(S[2 * nd], ua[kk], bf[0], bf[1]);
-          mma16816(S[2 * nd + 1], ua[kk], bf[2], bf[3]);
-        }
-      if (c + 2 < nc) bar_arrive(BAR_EMPTY + buf, NT);  // handoff buffer free again
-      bar_sync(BAR_SCAN, NSCAN);                          // O staging complete
-      const int t0 = c * C;
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int u = tid + it * NSCAN, r = u >> 3, ch = u & 7, t = t0 + r;
-        if (t < T)
-          *reinterpret_cast<uint4 *>(og + base_bh + (int64_t)t * row_stride + ch * 8) =
-              *reinterpret_cast<const uint4 *>(sm + OFF_O + buf * 8192 + sw64(r, ch * 8));
-      }
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        *reinterpret_cast<float2 *>(p.stateT + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4) =
-            make_float2(S[nt][2 * hh], S[nt][2 * hh + 1]);
-    return;
-  }
-
-  // =============================== producer group ===============================
-  const int ptid = tid - NSCAN, pwarp = warp - 4;
   float *GS = reinterpret_cast<float *>(sm + OFF_GS);
   float *AD = reinterpret_cast<float *>(sm + OFF_AD);
   float *vec = reinterpret_cast<float *>(sm + OFF_VEC);
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART;
   float *erb = vec + V_ERB, *egr = vec + V_EGR, *gij = vec + V_G;
   int *flag = reinterpret_cast<int *>(vec + V_FLAG);
-  const __nv_bfloat16 *qg = (const __nv_bfloat16 *)p.q, *kg = (const __nv_bfloat16 *)p.k;
-  const __nv_bfloat16 *vg = (const __nv_bfloat16 *)p.v;
+  uint8_t *hom = sm + OFF_OUT;
+  const uint32_t ho = s_base + OFF_OUT;
+  float *eG = reinterpret_cast<float *>(hom + HO_EG);
   const Tb *betag = (const Tb *)p.beta;
 
-  auto issue_loads = [&](int c) {
-    const int t0 = c * C;
-    for (int u = ptid; u < 3 * 512; u += NPROD) {  // q, k, v: 64 rows x 8 chunks of 16 B
-      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7;
-      const int t = t0 + r;
-      const __nv_bfloat16 *src = which == 0 ? qg : which == 1 ? kg : vg;
+  {  // loads: q, k, v tiles (swizzled), g fp32, beta
+    const __nv_bfloat16 *src[3] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
+                                   (const __nv_bfloat16 *)p.v};
+    for (int u = tid; u < 3 * 512; u += NT1) {
+      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
       const bool in = t < T;
-      const __nv_bfloat16 *gp = src + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8;
-      const uint32_t dst = s_base + (which == 0 ? OFF_QS : which == 1 ? OFF_KS : OFF_VS) + sw64(r, ch * 8);
-      cp_async16(dst, gp, in ? 16 : 0);
+      cp_async16(s_base + OFF_QS + which * 8192 + sw64(r, ch * 8),
+                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
     }
-    for (int u = ptid; u < 1024; u += NPROD) {  // g: 64 rows x 16 chunks of 16 B (fp32)
-      const int r = u >> 4, ch = u & 15;
-      const int t = t0 + r;
+    for (int u = tid; u < 1024; u += NT1) {
+      const int r = u >> 4, ch = u & 15, t = t0 + r;
       const bool in = t < T;
-      const float *gp = p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4;
-      cp_async16(s_base + OFF_GS + r * 256 + ch * 16, gp, in ? 16 : 0);
+      cp_async16(s_base + OFF_GS + r * 256 + ch * 16, p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
     }
     cp_async_commit();
-  };
-
-  issue_loads(0);
-  float beta_next = 0.f;
-  if (ptid < C) beta_next = ptid < T ? to_f(betag[((int64_t)b * T + ptid) * H + h]) : 0.f;
-
-  for (int c = 0; c < nc; ++c) {
-    const int buf = c & 1, t0 = c * C;
-    uint8_t *hom = sm + OFF_HO + buf * HO_SIZE;
-    const uint32_t ho = s_base + OFF_HO + buf * HO_SIZE;
-    float *eG = reinterpret_cast<float *>(hom + HO_EG);
+    if (tid < C) bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
     cp_async_wait_all();
-    if (ptid < C) bet[ptid] = beta_next;
-    bar_sync(BAR_PROD, NPROD);
+    __syncthreads();
+  }
 
-    // ---- (1a) gamma = cumsum(g): 4 segments of 16 rows per channel ----
-    {
-      const int d = ptid & 63, seg = ptid >> 6;
-      float acc = 0.f;
+  // ---- (1a) gamma = cumsum(g): 8 segments of 8 rows per channel ----
+  {
+    const int d = tid & 63, seg = tid >> 6;
+    float acc = 0.f;
 #pragma unroll
-      for (int r = 0; r < 16; ++r) acc += GS[(seg * 16 + r) * 64 + d];
-      part[seg * 64 + d] = acc;
-      bar_sync(BAR_PROD, NPROD);
-      float off = 0.f;
-      for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
+    for (int r = 0; r < 8; ++r) acc += GS[(seg * 8 + r) * 64 + d];
+    part[seg * 64 + d] = acc;
+    __syncthreads();
+    float off = 0.f;
+    for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        off += GS[(seg * 16 + r) * 64 + d];
-        GS[(seg * 16 + r) * 64 + d] = off;
-      }
-      bar_sync(BAR_PROD, NPROD);
+    for (int r = 0; r < 8; ++r) {
+      off += GS[(seg * 8 + r) * 64 + d];
+      GS[(seg * 8 + r) * 64 + d] = off;
     }
-    // guard: factored decay stays within e^{kSpanMax} unless gamma moves more than that across
-    // half a 16-row block; such a "big" chunk uses block-start references (every off-diagonal
-    // factor <= 1) and computes its diagonal blocks exactly.
-    if (ptid < 64) {
-      float span = 0.f;
+    __syncthreads();
+  }
+  // guard: factored decay stays within e^{kSpanMax} unless gamma moves more than that across
+  // half a 16-row block; such a "big" chunk uses block-start references (every off-diagonal
+  // factor <= 1) and computes its diagonal blocks exactly.
+  if (tid < 64) {
+    float span = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      span = fmaxf(span, GS[(i * 16) * 64 + tid] - GS[(i * 16 + 8) * 64 + tid]);
+      span = fmaxf(span, GS[(i * 16 + 8) * 64 + tid] - GS[(i * 16 + 15) * 64 + tid]);
+    }
+    const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
+    if (lane == 0) flag[warp] = any;
+  }
+  __syncthreads();
+  const bool big = flag[0] | flag[1];
+  if (tid < 64) {
+    const int d = tid;
+    const float gC = GS[63 * 64 + d];
+    float r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = GS[(i * 16 + (big ? 0 : 8)) * 64 + d];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      refs[i * 64 + d] = r[i];
+      erb[i * 64 + d] = __expf(r[i]);
+      egr[i * 64 + d] = __expf(gC - r[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j <= i ? __expf(r[i] - r[j]) : 0.f;
+    }
+    eG[d] = __expf(gC);
+  }
+  __syncthreads();
+
+  // ---- (1b) operand build: 512 units of (row t, 8 consecutive channels) ----
+  for (int u = tid; u < 512; u += NT1) {
+    const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
+    const uint32_t off = sw64(t, d0);
+    const uint4 kq = *reinterpret_cast<const uint4 *>(sm + OFF_KS + off);
+    const uint4 qq = *reinterpret_cast<const uint4 *>(sm + OFF_QS + off);
+    const uint4 vq = *reinterpret_cast<const uint4 *>(sm + OFF_VS + off);
+    const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w},
+                   vw[4] = {vq.x, vq.y, vq.z, vq.w};
+    const float bt = bet[t];
+    const float4 ga4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0);
+    const float4 gb4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0 + 4);
+    const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
+    uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[4][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
+      const int d = d0 + 2 * e;
+      float F[2], iF[2], eg[2], eb[2];
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const float gm = gam[2 * e + x];
+        F[x] = __expf(gm - refs[blk * 64 + d + x]);
+        if (!big) {
+          iF[x] = __fdividef(1.f, F[x]);
+          eg[x] = F[x] * erb[blk * 64 + d + x];
+          eb[x] = iF[x] * egr[blk * 64 + d + x];
+        } else {
+          iF[x] = 0.f;
+          eg[x] = __expf(gm);
+          eb[x] = __expf(GS[63 * 64 + d + x] - gm);
+        }
+      }
+      okd[e] = pack_bf16(kf.x * F[0], kf.y * F[1]);
+      oqd[e] = pack_bf16(qf.x * F[0], qf.y * F[1]);
+      oxk[e] = pack_bf16(bt * kf.x * eg[0], bt * kf.y * eg[1]);
+      oqe[e] = pack_bf16(qf.x * eg[0], qf.y * eg[1]);
+      oxv[e] = pack_bf16(bt * vf.x, bt * vf.y);
+      okb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        span = fmaxf(span, GS[(i * 16) * 64 + ptid] - GS[(i * 16 + 8) * 64 + ptid]);
-        span = fmaxf(span, GS[(i * 16 + 8) * 64 + ptid] - GS[(i * 16 + 15) * 64 + ptid]);
-      }
-      const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
-      if (lane == 0) flag[pwarp] = any;
-    }
-    // the scan must be done with this handoff buffer (chunk c-2) before it is rewritten
-    if (c >= 2) bar_sync(BAR_EMPTY + buf, NT);
-    bar_sync(BAR_PROD, NPROD);
-    const bool big = flag[0] | flag[1];
-    if (ptid < 64) {
-      const int d = ptid;
-      const float gC = GS[63 * 64 + d];
-      float r[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) r[i] = GS[(i * 16 + (big ? 0 : 8)) * 64 + d];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        refs[i * 64 + d] = r[i];
-        erb[i * 64 + d] = __expf(r[i]);
-        egr[i * 64 + d] = __expf(gC - r[i]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j <= i ? __expf(r[i] - r[j]) : 0.f;
-      }
-      eG[d] = __expf(gC);
-    }
-    bar_sync(BAR_PROD, NPROD);
-
-    // ---- (1b) operand build: 512 units of (row t, 8 consecutive channels) ----
-    for (int u = ptid; u < 512; u += NPROD) {
-      const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
-      const uint32_t off = sw64(t, d0);
-      const uint4 kq = *reinterpret_cast<const uint4 *>(sm + OFF_KS + off);
-      const uint4 qq = *reinterpret_cast<const uint4 *>(sm + OFF_QS + off);
-      const uint4 vq = *reinterpret_cast<const uint4 *>(sm + OFF_VS + off);
-      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w},
-                     vw[4] = {vq.x, vq.y, vq.z, vq.w};
-      const float bt = bet[t];
-      const float4 ga4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0);
-      const float4 gb4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0 + 4);
-      const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
-      uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[4][4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
-        const int d = d0 + 2 * e;
-        float F[2], iF[2], eg[2], eb[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const float gm = gam[2 * e + x];
-          F[x] = __expf(gm - refs[blk * 64 + d + x]);
+        float s0 = 0.f, s1 = 0.f;
+        if (i >= blk) {
           if (!big) {
-            iF[x] = __fdividef(1.f, F[x]);
-            eg[x] = F[x] * erb[blk * 64 + d + x];
-            eb[x] = iF[x] * egr[blk * 64 + d + x];
+            s0 = iF[0] * gij[(i * 4 + blk) * 64 + d];
+            s1 = iF[1] * gij[(i * 4 + blk) * 64 + d + 1];
           } else {
-            iF[x] = 0.f;
-            eg[x] = __expf(gm);
-            eb[x] = __expf(GS[63 * 64 + d + x] - gm);
+            s0 = __expf(refs[i * 64 + d] - gam[2 * e]);
+            s1 = __expf(refs[i * 64 + d + 1] - gam[2 * e + 1]);
           }
         }
-        okd[e] = pack_bf16(kf.x * F[0], kf.y * F[1]);
-        oqd[e] = pack_bf16(qf.x * F[0], qf.y * F[1]);
-        oxk[e] = pack_bf16(bt * kf.x * eg[0], bt * kf.y * eg[1]);
-        oqe[e] = pack_bf16(qf.x * eg[0], qf.y * eg[1]);
-        oxv[e] = pack_bf16(bt * vf.x, bt * vf.y);
-        okb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
+        oki[i][e] = pack_bf16(kf.x * s0, kf.y * s1);
+      }
+    }
+    *reinterpret_cast<uint4 *>(sm + OFF_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
+    *reinterpret_cast<uint4 *>(sm + OFF_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
+    *reinterpret_cast<uint4 *>(sm + OFF_XK + off) = make_uint4(oxk[0], oxk[1], oxk[2], oxk[3]);
+    *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
+    *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
+    *reinterpret_cast<uint4 *>(hom + HO_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float s0 = 0.f, s1 = 0.f;
-          if (i >= blk) {
-            if (!big) {
-              s0 = iF[0] * gij[(i * 4 + blk) * 64 + d];
-              s1 = iF[1] * gij[(i * 4 + blk) * 64 + d + 1];
-            } else {
-              s0 = __expf(refs[i * 64 + d] - gam[2 * e]);
-              s1 = __expf(refs[i * 64 + d + 1] - gam[2 * e + 1]);
-            }
-          }
-          oki[i][e] = pack_bf16(kf.x * s0, kf.y * s1);
+    for (int i = 0; i < 4; ++i)
+      if (i >= blk)
+        *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(i, blk) * 2048 + sw64(t & 15, d0)) =
+            make_uint4(oki[i][0], oki[i][1], oki[i][2], oki[i][3]);
+  }
+  __syncthreads();
+
+  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors)
+  if (big) {
+    for (int e = tid; e < 1024; e += NT1) {
+      const int i = e >> 8, tl = (e >> 4) & 15, sl = e & 15, t = 16 * i + tl, s = 16 * i + sl;
+      float mk = 0.f, mq = 0.f;
+      if (s <= t) {
+        for (int d = 0; d < 64; d += 2) {
+          const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
+          const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
+          const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
+          const float e0 = __expf(GS[t * 64 + d] - GS[s * 64 + d]);
+          const float e1 = __expf(GS[t * 64 + d + 1] - GS[s * 64 + d + 1]);
+          mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
+          mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
         }
       }
-      *reinterpret_cast<uint4 *>(sm + OFF_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
-      *reinterpret_cast<uint4 *>(sm + OFF_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
-      *reinterpret_cast<uint4 *>(sm + OFF_XK + off) = make_uint4(oxk[0], oxk[1], oxk[2], oxk[3]);
-      *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
-      *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
-      *reinterpret_cast<uint4 *>(hom + HO_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
+      AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
+      *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(s <= t ? mq : 0.f);
+    }
+    __syncthreads();
+  }
+
+  // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T: the 20 (block row i, block column j <= i,
+  //      matrix) tasks spread evenly over the 8 producer warps ----
+  for (int task = warp; task < 20; task += 16) {
+    const int mat = task & 1, pr = task >> 1;
+    const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
+    const int j = pr - i * (i + 1) / 2;
+    if (big && j == i) continue;  // diagonal block already computed exactly
+    float acc[2][4] = {};
+    const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (i >= blk)
-          *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(i, blk) * 2048 + sw64(t & 15, d0)) =
-              make_uint4(oki[i][0], oki[i][1], oki[i][2], oki[i][3]);
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t af[4], bf[4];
+      ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af);
+      ldsm_x4(bnk_frag_addr(kib, 0, 16 * kk, lane), bf);
+      mma16816(acc[0], af, bf[0], bf[1]);
+      mma16816(acc[1], af, bf[2], bf[3]);
     }
-    bar_sync(BAR_PROD, NPROD);
-
-    // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors)
-    if (big) {
-      for (int e = ptid; e < 1024; e += NPROD) {
-        const int i = e >> 8, tl = (e >> 4) & 15, sl = e & 15, t = 16 * i + tl, s = 16 * i + sl;
-        float mk = 0.f, mq = 0.f;
-        if (s <= t) {
-          for (int d = 0; d < 64; d += 2) {
-            const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
-            const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
-            const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
-            const float e0 = __expf(GS[t * 64 + d] - GS[s * 64 + d]);
-            const float e1 = __expf(GS[t * 64 + d + 1] - GS[s * 64 + d + 1]);
-            mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
-            mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int tl = g4 + 8 * hh, t = 16 * i + tl;
+        const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
+        float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
+        if (mat == 0) {
+          v0 = s < t ? bet[t] * v0 : 0.f;
+          v1 = s + 1 < t ? bet[t] * v1 : 0.f;
+          if (j == i) {
+            AD[i * 256 + tl * 16 + sl] = v0;
+            AD[i * 256 + tl * 16 + sl + 1] = v1;
+          } else {
+            *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
           }
+        } else {
+          v0 = s <= t ? v0 : 0.f;
+          v1 = s + 1 <= t ? v1 : 0.f;
+          *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
         }
-        AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
-        *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(s <= t ? mq : 0.f);
       }
-      bar_sync(BAR_PROD, NPROD);
-    }
+  }
+  __syncthreads();
 
-    // the raw input tiles are consumed: prefetch the next chunk behind the tensor-core work
-    if (c + 1 < nc) {
-      issue_loads(c + 1);
-      if (ptid < C) {
-        const int t = t0 + C + ptid;
-        beta_next = t < T ? to_f(betag[((int64_t)b * T + t) * H + h]) : 0.f;
+  // ---- (3) T_ii = (I + A_ii)^{-1}, one column per thread, in registers ----
+  if (tid < 64) {
+    const int i = tid >> 4, u = tid & 15;
+    const float *A = AD + i * 256;
+    float x[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float v = t == u ? 1.f : 0.f;
+#pragma unroll
+      for (int s = 0; s < t; ++s) v = fmaf(-A[t * 16 + s], x[s], v);
+      x[t] = v;
+    }
+    __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TI + i * 512);
+#pragma unroll
+    for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
+  }
+  __syncthreads();
+
+  // ---- (4) W = (I+A)^{-1} beta Kd (stored negated), U = (I+A)^{-1} beta V; 8 columns per
+  //      warp, each warp's substitution independent of the others ----
+  {
+    const bool isW = warp < 8;
+    const int n0 = (warp & 7) * 8, l15 = lane & 15;
+    const uint32_t Yb = ho + (isW ? HO_W : HO_U);
+    uint8_t *Ym = hom + (isW ? HO_W : HO_U);
+    const uint8_t *Xm = sm + (isW ? OFF_XK : OFF_XV);
+    const uint32_t Rs = s_base + OFF_RS + warp * 256;
+    uint8_t *Rm = sm + OFF_RS + warp * 256;
+    const float sg = isW ? 1.f : -1.f, so = isW ? -1.f : 1.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float acc[4] = {};
+#pragma unroll
+      for (int j = 0; j < i; ++j) {
+        uint32_t af[4], bf[2];
+        ldsm_x4(a_frag_addr(s_base + OFF_AB, 16 * i, 16 * j, lane), af);
+        ldsm_x2_t(Yb + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
+        mma16816(acc, af, bf[0], bf[1]);
       }
+      // R = X_i -/+ acc  (the stored Y of the W half is -W) -> bf16 staging [t][col] 16x8
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int tl = g4 + 8 * hh, col = n0 + 2 * c4;
+        const float2 x = unpack_bf16(*reinterpret_cast<const uint32_t *>(Xm + sw64(16 * i + tl, col)));
+        *reinterpret_cast<uint32_t *>(Rm + tl * 16 + c4 * 4) =
+            pack_bf16(x.x + sg * acc[2 * hh], x.y + sg * acc[2 * hh + 1]);
+      }
+      __syncwarp();
+      uint32_t af[4], bf[2];
+      ldsm_x4(s_base + OFF_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
+      ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
+      float y[4] = {};
+      mma16816(y, af, bf[0], bf[1]);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
+        *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(so * y[2 * hh], so * y[2 * hh + 1]);
+      }
+      __syncwarp();
     }
+  }
 
-    // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T: the 20 (block row i, block column j <= i,
-    //      matrix) tasks spread evenly over the 8 producer warps ----
-    for (int task = pwarp; task < 20; task += 8) {
-      const int mat = task & 1, pr = task >> 1;
-      const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
-      const int j = pr - i * (i + 1) / 2;
-      if (big && j == i) continue;  // diagonal block already computed exactly
-      float acc[2][4] = {};
-      const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
+  __syncthreads();
+  // ---- the record for kda_fwd_scan (row-major bf16 tiles + e^{gamma_C}) ----
+  {
+    uint8_t *rec = (uint8_t *)p.ws + (int64_t)idx * HO_SIZE;  // same swizzled layout as smem
+    for (int u = tid; u < HO_SIZE / 16; u += NT1)
+      *reinterpret_cast<uint4 *>(rec + u * 16) = *reinterpret_cast<const uint4 *>(hom + u * 16);
+  }
+  // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-3,
+  //      rows d' in [jb, jb+16)), Qt = Qd + P (-W) (warps 4-7, rows t in [jb, jb+16)) ----
+  if (p.saved) {
+    uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
+    const int jb = (warp & 3) * 16;
+    if (tid < 64) reinterpret_cast<float *>(sv + kSavedEG)[tid] = eG[tid];
+    if (warp < 4) {  // warps 8..15 have no part in this step
+    {  // Mneg = Kb^T (-W), rows d' in [jb, jb+16)
+      float M[8][4] = {};
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        uint32_t af[4], bf[4];
-        ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af);
-        ldsm_x4(bnk_frag_addr(kib, 0, 16 * kk, lane), bf);
-        mma16816(acc[0], af, bf[0], bf[1]);
-        mma16816(acc[1], af, bf[2], bf[3]);
+        uint32_t af[4];
+        ldsm_x4_t(ct_frag_addr(ho + HO_KB, 16 * kk, jb, lane), af);
+#pragma unroll
+        for (int nd = 0; nd < 4; ++nd) {
+          uint32_t bf[4];
+          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
+          mma16816(M[2 * nd], af, bf[0], bf[1]);
+          mma16816(M[2 * nd + 1], af, bf[2], bf[3]);
+        }
       }
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<uint32_t *>(sv + kSavedM + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
+              pack_bf16(M[nt][2 * hh], M[nt][2 * hh + 1]);
+    }
+    } else if (warp < 8) {
+    {  // Qt rows t in [jb, jb+16): Qd + P (-W)
+      float Q[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int tl = g4 + 8 * hh, t = 16 * i + tl;
-          const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
-          float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
-          if (mat == 0) {
-            v0 = s < t ? bet[t] * v0 : 0.f;
-            v1 = s + 1 < t ? bet[t] * v1 : 0.f;
-            if (j == i) {
-              AD[i * 256 + tl * 16 + sl] = v0;
-              AD[i * 256 + tl * 16 + sl + 1] = v1;
-            } else {
-              *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
-            }
-          } else {
-            v0 = s <= t ? v0 : 0.f;
-            v1 = s + 1 <= t ? v1 : 0.f;
-            *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
-          }
+          const float2 v = unpack_bf16(*reinterpret_cast<const uint32_t *>(
+              hom + HO_QD + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)));
+          Q[nt][2 * hh] = v.x;
+          Q[nt][2 * hh + 1] = v.y;
         }
-    }
-    bar_sync(BAR_PROD, NPROD);
-
-    // ---- (3) T_ii = (I + A_ii)^{-1}, one column per thread, in registers ----
-    if (ptid < 64) {
-      const int i = ptid >> 4, u = ptid & 15;
-      const float *A = AD + i * 256;
-      float x[16];
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        float v = t == u ? 1.f : 0.f;
+      for (int kk = 0; kk < 4; ++kk) {
+        if (kk > (warp & 3)) break;
+        uint32_t af[4];
+        ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);
 #pragma unroll
-        for (int s = 0; s < t; ++s) v = fmaf(-A[t * 16 + s], x[s], v);
-        x[t] = v;
-      }
-      __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TI + i * 512);
-#pragma unroll
-      for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
-    }
-    bar_sync(BAR_PROD, NPROD);
-
-    // ---- (4) W = (I+A)^{-1} beta Kd (stored negated), U = (I+A)^{-1} beta V; 16 columns per
-    //      warp, each warp's substitution independent of the others ----
-    {
-      const bool isW = pwarp < 4;
-      const int n0 = (pwarp & 3) * 16;
-      const uint32_t Yb = ho + (isW ? HO_W : HO_U);
-      uint8_t *Ym = hom + (isW ? HO_W : HO_U);
-      const uint8_t *Xm = sm + (isW ? OFF_XK : OFF_XV);
-      const uint32_t Rs = s_base + OFF_RS + pwarp * 512;
-      uint8_t *Rm = sm + OFF_RS + pwarp * 512;
-      const float sg = isW ? 1.f : -1.f, so = isW ? -1.f : 1.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float acc[2][4] = {};
-#pragma unroll
-        for (int j = 0; j < i; ++j) {
-          uint32_t af[4], bf[4];
-          ldsm_x4(a_frag_addr(s_base + OFF_AB, 16 * i, 16 * j, lane), af);
-          ldsm_x4_t(bkn_frag_addr(Yb, 16 * j, n0, lane), bf);
-          mma16816(acc[0], af, bf[0], bf[1]);
-          mma16816(acc[1], af, bf[2], bf[3]);
+        for (int nd = 0; nd < 4; ++nd) {
+          uint32_t bf[4];
+          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
+          mma16816(Q[2 * nd], af, bf[0], bf[1]);
+          mma16816(Q[2 * nd + 1], af, bf[2], bf[3]);
         }
-        // R = X_i -/+ acc  (the stored Y of the W half is -W) -> bf16 staging [t][col] 16x16
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int tl = g4 + 8 * hh;
-            const int col = n0 + nt * 8 + 2 * c4;
-            const float2 x = unpack_bf16(*reinterpret_cast<const uint32_t *>(Xm + sw64(16 * i + tl, col)));
-            *reinterpret_cast<uint32_t *>(Rm + tl * 32 + (nt * 8 + 2 * c4) * 2) =
-                pack_bf16(x.x + sg * acc[nt][2 * hh], x.y + sg * acc[nt][2 * hh + 1]);
-          }
-        __syncwarp();
-        uint32_t af[4], bf[4];
-        ldsm_x4(s_base + OFF_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
-        ldsm_x4_t(Rs + ((lane & 7) + ((lane >> 3) & 1) * 8) * 32 + (lane >> 4) * 16, bf);
-        float y[2][4] = {};
-        mma16816(y[0], af, bf[0], bf[1]);
-        mma16816(y[1], af, bf[2], bf[3]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int t = 16 * i + g4 + 8 * hh;
-            const int col = n0 + nt * 8 + 2 * c4;
-            *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(so * y[nt][2 * hh], so * y[nt][2 * hh + 1]);
-          }
-        __syncwarp();
       }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<uint32_t *>(sv + kSavedQt + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
+              pack_bf16(Q[nt][2 * hh], Q[nt][2 * hh + 1]);
     }
-    // hand the chunk's operands to the scan group
-    bar_arrive(BAR_FULL + buf, NT);
+    }
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// kda_fwd_scan
+// ---------------------------------------------------------------------------------------
+constexpr int NT2 = 128;
+constexpr int OFF2_REC = 0;                 // 2 x HO_SIZE, swizzled tiles
+constexpr int OFF2_O = 2 * HO_SIZE;         // O staging, 2 x 8 KB
+constexpr int OFF2_MBAR = OFF2_O + 2 * 8192; // two mbarriers
+constexpr int SMEM2 = OFF2_MBAR + 16;
+
+__global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p) {
+  extern __shared__ __align__(1024) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int T = p.T, H = p.H, nc = p.nc;
+  const uint32_t s_base = smem_u32(sm);
+  const int g4 = lane >> 2, c4 = lane & 3;
+  const int64_t row_stride = (int64_t)H * D;
+  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
+  const int jb = warp * 16;
+
+  const uint32_t mbar = s_base + OFF2_MBAR;
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar + 8, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {  // one bulk copy of the chunk's whole record (thread 0)
+    if (tid == 0) {
+      const uint8_t *rec = (const uint8_t *)p.ws + ((int64_t)bh * nc + c) * HO_SIZE;
+      mbar_expect_tx(mbar + (c & 1) * 8, HO_SIZE);
+      bulk_g2s(s_base + OFF2_REC + (c & 1) * HO_SIZE, rec, HO_SIZE, mbar + (c & 1) * 8);
+    }
+  };
+
+  float S[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float2 v = make_float2(0.f, 0.f);
+      if (p.state0)
+        v = *reinterpret_cast<const float2 *>(p.state0 + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4);
+      S[nt][2 * hh] = v.x;
+      S[nt][2 * hh + 1] = v.y;
+    }
+  __nv_bfloat16 *og = (__nv_bfloat16 *)p.o;
+  issue(0);
+  for (int c = 0; c < nc; ++c) {
+    const int buf = c & 1;
+    const uint32_t ho = s_base + OFF2_REC + buf * HO_SIZE;
+    const float *eG = reinterpret_cast<const float *>(sm + OFF2_REC + buf * HO_SIZE + HO_EG);
+    const uint32_t ost = s_base + OFF2_O + buf * 8192;
+    // chunk c's record landed (bounded wait); the barrier also marks chunk c-1 consumed
+    if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (c >> 1) & 1))) {
+      if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+      break;
+    }
+    if (c + 1 < nc) issue(c + 1);
+    uint32_t sa[4][4];  // S as bf16 A fragments (rows j, k = d)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      sa[kk][0] = pack_bf16(S[2 * kk][0], S[2 * kk][1]);
+      sa[kk][1] = pack_bf16(S[2 * kk][2], S[2 * kk][3]);
+      sa[kk][2] = pack_bf16(S[2 * kk + 1][0], S[2 * kk + 1][1]);
+      sa[kk][3] = pack_bf16(S[2 * kk + 1][2], S[2 * kk + 1][3]);
+    }
+    uint32_t ua[4][4];  // Unew^T as A fragments (rows j, k = t)
+    {
+      float X[8][4];  // Unew^T = U^T + S (-W)^T
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) {
+        uint32_t r[4];
+        ldsm_x4_t(ct_frag_addr(ho + HO_U, 16 * pp, jb, lane), r);
+        const float2 a = unpack_bf16(r[0]), bq = unpack_bf16(r[1]), cq = unpack_bf16(r[2]), dq = unpack_bf16(r[3]);
+        X[2 * pp][0] = a.x; X[2 * pp][1] = a.y; X[2 * pp][2] = bq.x; X[2 * pp][3] = bq.y;
+        X[2 * pp + 1][0] = cq.x; X[2 * pp + 1][1] = cq.y; X[2 * pp + 1][2] = dq.x; X[2 * pp + 1][3] = dq.y;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+          uint32_t bf[4];
+          ldsm_x4(bnk_frag_addr(ho + HO_W, 16 * pp, 16 * kk, lane), bf);
+          mma16816(X[2 * pp], sa[kk], bf[0], bf[1]);
+          mma16816(X[2 * pp + 1], sa[kk], bf[2], bf[3]);
+        }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        ua[kk][0] = pack_bf16(X[2 * kk][0], X[2 * kk][1]);
+        ua[kk][1] = pack_bf16(X[2 * kk][2], X[2 * kk][3]);
+        ua[kk][2] = pack_bf16(X[2 * kk + 1][0], X[2 * kk + 1][1]);
+        ua[kk][3] = pack_bf16(X[2 * kk + 1][2], X[2 * kk + 1][3]);
+      }
+    }
+    // O^T = S Qd^T + Unew^T P^T  (16 t-columns at a time)
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      float O[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t bf[4];
+        ldsm_x4(bnk_frag_addr(ho + HO_QD, 16 * pp, 16 * kk, lane), bf);
+        mma16816(O[0], sa[kk], bf[0], bf[1]);
+        mma16816(O[1], sa[kk], bf[2], bf[3]);
+      }
+#pragma unroll
+      for (int kk = 0; kk <= pp; ++kk) {
+        uint32_t bf[4];
+        ldsm_x4(bnk_frag_addr(ho + HO_P, 16 * pp, 16 * kk, lane), bf);
+        mma16816(O[0], ua[kk], bf[0], bf[1]);
+        mma16816(O[1], ua[kk], bf[2], bf[3]);
+      }
+      stsm_x4_t(ct_frag_addr(ost, 16 * pp, jb, lane), pack_bf16(O[0][0], O[0][1]), pack_bf16(O[0][2], O[0][3]),
+                pack_bf16(O[1][0], O[1][1]), pack_bf16(O[1][2], O[1][3]));
+    }
+    // the state-dependent part of the backward's per-chunk record: S0 and Unew^T (bf16)
+    if (p.saved) {
+      uint8_t *sv = (uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
+          *reinterpret_cast<uint32_t *>(sv + kSavedS0 + sw64(row, col)) = sa[kk][x];
+          *reinterpret_cast<uint32_t *>(sv + kSavedUnT + sw64(row, col)) = ua[kk][x];
+        }
+    }
+    // S <- S diag(e^gamma_C) + Unew^T Kb
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float e0 = eG[nt * 8 + 2 * c4], e1 = eG[nt * 8 + 2 * c4 + 1];
+      S[nt][0] *= e0; S[nt][1] *= e1; S[nt][2] *= e0; S[nt][3] *= e1;
+    }
+#pragma unroll
+    for (int nd = 0; nd < 4; ++nd)
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t bf[4];
+        ldsm_x4_t(bkn_frag_addr(ho + HO_KB, 16 * kk, 16 * nd, lane), bf);
+        mma16816(S[2 * nd], ua[kk], bf[0], bf[1]);
+        mma16816(S[2 * nd + 1], ua[kk], bf[2], bf[3]);
+      }
+    __syncthreads();                 // O staging complete
+    const int t0 = c * C;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int u = tid + it * NT2, r = u >> 3, ch = u & 7, t = t0 + r;
+      if (t < T)
+        *reinterpret_cast<uint4 *>(og + base_bh + (int64_t)t * row_stride + ch * 8) =
+            *reinterpret_cast<const uint4 *>(sm + OFF2_O + buf * 8192 + sw64(r, ch * 8));
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+      *reinterpret_cast<float2 *>(p.stateT + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4) =
+          make_float2(S[nt][2 * hh], S[nt][2 * hh + 1]);
 }
 
 template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
-  auto kern = kda_fwd_tc_kernel<Tb>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+  auto k1 = kda_fwd_chunks_kernel<Tb>;
+  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1)) return KDA_ERR_CUDA;
+  k1<<<p.B * p.H * p.nc, NT1, SMEM1, st>>>(p);
+  count_launch();
+  if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
     return KDA_ERR_CUDA;
-  kern<<<p.B * p.H, NT, SMEM, st>>>(p);
+  kda_fwd_scan_kernel<<<p.B * p.H, NT2, SMEM2, st>>>(p);
   count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
 
 }  // namespace tcfwd
+
+int tc_fwd_device_status(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tcfwd::g_fwd_status, sizeof(int)) != cudaSuccess) return KDA_ERR_CUDA;
+  if (reset && v) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(tcfwd::g_fwd_status, &z, sizeof(int)) != cudaSuccess) return KDA_ERR_CUDA;
+  }
+  return v;
+}
+
+size_t tc_fwd_workspace_bytes(const KdaDesc *d) {
+  return (size_t)(d->B * d->H * ((d->T + d->chunk - 1) / d->chunk)) * tcfwd::HO_SIZE;
+}
 
 int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st) {
   if (dtype_beta == KDA_BF16) return tcfwd::launch<__nv_bfloat16>(p, st);

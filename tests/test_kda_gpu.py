@@ -128,3 +128,9 @@ def test_strong_decay_stays_finite(cuda):
     for k in OUT_KEYS:
         assert np.isfinite(got[k]).all(), k
         assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))
+
+
+def test_no_device_wait_timed_out(cuda):
+    """Every bounded device-side wait in the runs above completed (status word still 0)."""
+    from mlx_vit_b200 import _lib
+    assert _lib.lib().kda_device_status(0) == 0
