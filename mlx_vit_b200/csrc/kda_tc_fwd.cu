@@ -69,11 +69,9 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
-  const int nc = p.nc, idx = blockIdx.x, bh = idx / nc, c = idx % nc;
-  const int b = bh / p.H, h = bh % p.H, T = p.T, H = p.H, t0 = c * C;
+  const int nc = p.nc, T = p.T, H = p.H, nchunks = p.B * p.H * nc;
   const uint32_t s_base = smem_u32(sm);
   const int64_t row_stride = (int64_t)H * D;
-  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
   float *GS = reinterpret_cast<float *>(sm + OFF_GS);
   float *AD = reinterpret_cast<float *>(sm + OFF_AD);
   float *vec = reinterpret_cast<float *>(sm + OFF_VEC);
@@ -84,26 +82,42 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   const uint32_t ho = s_base + OFF_OUT;
   float *eG = reinterpret_cast<float *>(hom + HO_EG);
   const Tb *betag = (const Tb *)p.beta;
+  const __nv_bfloat16 *src[3] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
+                                 (const __nv_bfloat16 *)p.v};
 
-  {  // loads: q, k, v tiles (swizzled), g fp32, beta
-    const __nv_bfloat16 *src[3] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
-                                   (const __nv_bfloat16 *)p.v};
+  // the CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...; the loads of the
+  // next chunk are issued as soon as this chunk's raw tiles are consumed
+  auto issue_loads = [&](int i) {  // q, k, v tiles (swizzled) and g (fp32) of chunk i
+    const int bh_ = i / nc, c_ = i % nc, b_ = bh_ / H, h_ = bh_ % H, t0_ = c_ * C;
+    const int64_t base_ = ((int64_t)b_ * T * H + h_) * D;
     for (int u = tid; u < 3 * 512; u += NT1) {
-      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
+      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0_ + r;
       const bool in = t < T;
       cp_async16(s_base + OFF_QS + which * 8192 + sw64(r, ch * 8),
-                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
+                 src[which] + base_ + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
     }
     for (int u = tid; u < 1024; u += NT1) {
-      const int r = u >> 4, ch = u & 15, t = t0 + r;
+      const int r = u >> 4, ch = u & 15, t = t0_ + r;
       const bool in = t < T;
-      cp_async16(s_base + OFF_GS + r * 256 + ch * 16, p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
+      cp_async16(s_base + OFF_GS + r * 256 + ch * 16, p.g + base_ + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
     }
     cp_async_commit();
-    if (tid < C) bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
-    cp_async_wait_all();
-    __syncthreads();
-  }
+  };
+  auto load_beta = [&](int i) -> float {
+    const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
+    return t < T ? to_f(betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H]) : 0.f;
+  };
+  int idx = blockIdx.x;
+  if (idx < nchunks) issue_loads(idx);
+  float beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : 0.f;
+
+  for (; idx < nchunks; idx += gridDim.x) {
+  const int bh = idx / nc, c = idx % nc, b = bh / H, h = bh % H, t0 = c * C;
+  (void)b; (void)h; (void)t0;
+  if (tid == 0) bulk_wait_read_all();  // the previous chunk's bulk stores have read smem
+  cp_async_wait_all();
+  if (tid < C) bet[tid] = beta_next;
+  __syncthreads();
 
   // ---- (1a) gamma = cumsum(g): 8 segments of 8 rows per channel ----
   {
@@ -245,6 +259,12 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
     __syncthreads();
   }
 
+  __syncthreads();  // the raw tiles are consumed: prefetch the next chunk behind the GEMMs
+  if (idx + (int)gridDim.x < nchunks) {
+    issue_loads(idx + gridDim.x);
+    if (tid < C) beta_next = load_beta(idx + gridDim.x);
+  }
+
   // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T: the 20 (block row i, block column j <= i,
   //      matrix) tasks spread evenly over the 8 producer warps ----
   for (int task = warp; task < 20; task += 16) {
@@ -349,19 +369,18 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
     }
   }
 
+  fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
-  // ---- the record for kda_fwd_scan (row-major bf16 tiles + e^{gamma_C}) ----
-  {
-    uint8_t *rec = (uint8_t *)p.ws + (int64_t)idx * HO_SIZE;  // same swizzled layout as smem
-    for (int u = tid; u < HO_SIZE / 16; u += NT1)
-      *reinterpret_cast<uint4 *>(rec + u * 16) = *reinterpret_cast<const uint4 *>(hom + u * 16);
+  // ---- the record for kda_fwd_scan: one bulk copy, same swizzled layout as in smem ----
+  if (tid == 0) {
+    bulk_s2g((uint8_t *)p.ws + (int64_t)idx * HO_SIZE, ho, HO_SIZE);
+    bulk_commit();
   }
   // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-3,
   //      rows d' in [jb, jb+16)), Qt = Qd + P (-W) (warps 4-7, rows t in [jb, jb+16)) ----
   if (p.saved) {
     uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
     const int jb = (warp & 3) * 16;
-    if (tid < 64) reinterpret_cast<float *>(sv + kSavedEG)[tid] = eG[tid];
     if (warp < 4) {  // warps 8..15 have no part in this step
     {  // Mneg = Kb^T (-W), rows d' in [jb, jb+16)
       float M[8][4] = {};
@@ -381,7 +400,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(sv + kSavedM + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
+          *reinterpret_cast<uint32_t *>(sm + OFF_XK + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
               pack_bf16(M[nt][2 * hh], M[nt][2 * hh + 1]);
     }
     } else if (warp < 8) {
@@ -413,11 +432,21 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(sv + kSavedQt + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
+          *reinterpret_cast<uint32_t *>(sm + OFF_XV + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
               pack_bf16(Q[nt][2 * hh], Q[nt][2 * hh + 1]);
     }
     }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // Mneg, Qt (staged in the free beta-Kd / beta-V tiles) and e^{gamma_C}
+      bulk_s2g(sv + kSavedM, s_base + OFF_XK, 8192);
+      bulk_s2g(sv + kSavedQt, s_base + OFF_XV, 8192);
+      bulk_s2g(sv + kSavedEG, ho + HO_EG, 256);
+      bulk_commit();
+    }
   }
+  }  // chunk loop
+  if (tid == 0) bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -585,7 +614,12 @@ template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
   auto k1 = kda_fwd_chunks_kernel<Tb>;
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1)) return KDA_ERR_CUDA;
-  k1<<<p.B * p.H * p.nc, NT1, SMEM1, st>>>(p);
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KDA_ERR_CUDA;
+  const int nchunks = p.B * p.H * p.nc;
+  k1<<<nchunks < nsm ? nchunks : nsm, NT1, SMEM1, st>>>(p);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
     return KDA_ERR_CUDA;
