@@ -321,7 +321,10 @@ def run_ours(args, rank, world, local_rank):
     if os.path.exists(tf):
         try:
             with open(tf) as f:
-                line["roofline"]["traffic"] = json.load(f).get(dom)
+                tr = json.load(f).get(dom)
+                line["roofline"]["traffic"] = tr
+                line["roofline"]["traffic_note"] = ("ncu DRAM read+write bytes of the call's kernels "
+                                                    "(profiles/kda_cfg2_traffic.md)")
         except Exception:
             pass
     if world == 1 and not args.no_cpu_baseline:
