@@ -29,12 +29,16 @@ struct Params {
 };
 
 // Per-chunk record the tensor-core forward saves for the tensor-core backward (D = C = 64):
-// S0 = chunk-entry state [j][d], Unew^T [j][t], Mneg = -Kb^T W [d'][d], Qt = Qd - P W [t][d]
-// (all bf16, 64 x 64 with the 128-byte row swizzle of the shared-memory tiles, so that one
-// bulk copy lands them ready for ldmatrix) and e^{gamma_C} [d] (fp32).  With them the state cotangent obeys
-//   dS_entry = dS_exit diag(e^{gamma_C}) + dS_exit Mneg + dO^T Qt.
-constexpr int kSavedS0 = 0, kSavedUnT = 8192, kSavedM = 16384, kSavedQt = 24576, kSavedEG = 32768;
-constexpr int kSavedChunk = 32768 + 256;
+// S0 = chunk-entry state [j][d], Unew^T [j][t], the decay-weighted P = Q K^T (lower incl.) and
+// M = K K^T (strict lower) [t][s], Tinv = (I + beta M)^{-1} [t][s], Mneg = -Kb^T W [d'][d],
+// Qt = Qd - P W [t][d] (all bf16, 64 x 64 with the 128-byte row swizzle of the shared-memory
+// tiles, so that one bulk copy lands them ready for ldmatrix) and e^{gamma_C} [d] (fp32).
+// With them the state cotangent obeys
+//   dS_entry = dS_exit diag(e^{gamma_C}) + dS_exit Mneg + dO^T Qt
+// and the chunk gradients need no triangular solve.
+constexpr int kSavedS0 = 0, kSavedUnT = 8192, kSavedP = 16384, kSavedMkk = 24576, kSavedTinv = 32768;
+constexpr int kSavedM = 40960, kSavedQt = 49152, kSavedEG = 57344;
+constexpr int kSavedChunk = 57344 + 256;
 
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }

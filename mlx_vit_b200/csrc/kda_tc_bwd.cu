@@ -17,8 +17,9 @@
 //   kda_bwd_state_scan  one CTA per (b, h) walks the chunks backwards carrying dS in mma
 //                       registers, using the forward's saved Mneg = -Kb^T W and Qt = Qd - P W;
 //                       it writes every chunk's exit cotangent dS1 (bf16) to the workspace.
-//   kda_bwd_chunks      one CTA per (b, h, chunk), independent of each other: recomputes the
-//                       chunk's decay-weighted M and P, T_ii and dR, and produces all gradients.
+//   kda_bwd_chunks      one CTA per (b, h, chunk), independent of each other: takes the
+//                       chunk's decay-weighted P, M and Tinv from the saved record, forms
+//                       dR = Tinv^T dU as one GEMM, and produces all gradients.
 // Chunks whose decay is too strong for the factored form are flagged and redone by the exact
 // fp32 per-chunk kernel (kda_bwd_flagged_chunks_kernel).
 #include <mutex>
@@ -165,11 +166,12 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
 constexpr int CK_NT = 256;
 constexpr int O_QS = 0, O_KS = 8192, O_VS = 16384, O_DO = 24576;   // raw bf16 tiles [t][d]
 constexpr int O_GS = 32768;                                         // g -> gamma -> F -> dgamma fp32
-constexpr int O_S0 = 49152, O_UN = 57344, O_DS = 65536;             // S0 [j][d], Unew^T [j][t], dS1 [j][d]
-constexpr int O_KD = 73728, O_QD = 81920, O_KF = 90112, O_KB = 98304;
-constexpr int O_AB = 106496, O_AD = 114688, O_TI = 118784;          // bf16 A off-diag, fp32 A diag, T_ii
-constexpr int O_MK = 120832, O_PB = 129024, O_DR = 137216, O_DP = 145408, O_DK = 153600;
-constexpr int O_RS = 161792;                                        // 8 warps x 256 B staging
+// S0 [j][d], Unew^T [j][t], P [t][s], M [t][s], Tinv [t][s]: one bulk copy of the saved record
+constexpr int O_S0 = 49152, O_UN = 57344, O_PB = 65536, O_MK = 73728, O_TF = 81920;
+constexpr int O_DS = 90112;                                         // dS1 [j][d]
+constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
+constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
+constexpr int O_RS = 155648;                                        // 8 warps x 256 B staging
 constexpr int O_VEC = O_RS + 8 * 256;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088,
               V_EG = 2112, V_DB = 2176, V_DGM = 2240, V_FLAG = 2304;
@@ -187,7 +189,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const int64_t row_stride = (int64_t)H * D;
   const int64_t base_bh = ((int64_t)b * T * H + h) * D;
   float *GS = reinterpret_cast<float *>(sm + O_GS);
-  float *AD = reinterpret_cast<float *>(sm + O_AD);
   float *vec = reinterpret_cast<float *>(sm + O_VEC);
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
   float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *dbacc = vec + V_DB, *dgacc = vec + V_DGM;
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
   const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
 
-  // ---- P0: loads in two groups: q, k, g first (for P1-P4), the rest lands behind P1-P4 ----
+  // ---- P0: loads in two groups: q, k, g first (for P1-P2), the rest lands behind P1-P2 ----
   {
     const __nv_bfloat16 *src[4] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
                                    (const __nv_bfloat16 *)p.v, (const __nv_bfloat16 *)p.dO};
@@ -218,12 +219,12 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
                  src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
     }
-    if (tid == 0) {  // S0 and Unew^T (adjacent in the saved record) and dS1, already swizzled
+    if (tid == 0) {  // S0, Unew^T, P, M, Tinv (adjacent in the saved record) and dS1, swizzled
       const uint32_t mbar = s_base + O_MBAR;
       mbar_init(mbar, 1);
       mbar_fence_init();
-      mbar_expect_tx(mbar, 3 * 8192);
-      bulk_g2s(s_base + O_S0, rec + kSavedS0, 2 * 8192, mbar);
+      mbar_expect_tx(mbar, 6 * 8192);
+      bulk_g2s(s_base + O_S0, rec + kSavedS0, 5 * 8192, mbar);
       bulk_g2s(s_base + O_DS, ds_exit, 8192, mbar);
     }
     cp_async_commit();
@@ -316,75 +317,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   }
   __syncthreads();
 
-  // ---- P3: M = KD G KF^T (strict lower) and P = QD G KF^T (lower incl.); the 20 (block row i,
-  //      block column j <= i, matrix) tasks are spread evenly over the 8 warps ----
-  for (int task = warp; task < 20; task += 8) {
-    const int mat = task & 1, pr = task >> 1;  // pr enumerates (i, j), j <= i
-    const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
-    const int j = pr - i * (i + 1) / 2;
-    float acc[2][4] = {};
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t af[4];
-      ldsm_x4(a_frag_addr(s_base + (mat ? O_QD : O_KD), 16 * i, 16 * kk, lane), af);
-      if (j < i) {  // scale the k = d columns by e^{r_i - r_j}
-        const float *G = gij + (i * 4 + j) * 64;
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const int d = 16 * kk + (x >> 1) * 8 + 2 * c4;
-          const float2 v = unpack_bf16(af[x]);
-          const float2 gg = *reinterpret_cast<const float2 *>(G + d);
-          af[x] = pack_bf16(v.x * gg.x, v.y * gg.y);
-        }
-      }
-      uint32_t bf[4];
-      ldsm_x4(bnk_frag_addr(s_base + O_KF, 16 * j, 16 * kk, lane), bf);
-      mma16816(acc[0], af, bf[0], bf[1]);
-      mma16816(acc[1], af, bf[2], bf[3]);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int tl = g4 + 8 * hh, t = 16 * i + tl;
-        const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
-        float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
-        if (mat == 0) {
-          v0 = s < t ? v0 : 0.f;
-          v1 = s + 1 < t ? v1 : 0.f;
-          *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, s)) = pack_bf16(v0, v1);
-          if (j == i) {
-            AD[i * 256 + tl * 16 + sl] = bet[t] * v0;
-            AD[i * 256 + tl * 16 + sl + 1] = bet[t] * v1;
-          } else {
-            *reinterpret_cast<uint32_t *>(sm + O_AB + sw64(t, s)) = pack_bf16(bet[t] * v0, bet[t] * v1);
-          }
-        } else {
-          v0 = s <= t ? v0 : 0.f;
-          v1 = s + 1 <= t ? v1 : 0.f;
-          *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, s)) = pack_bf16(v0, v1);
-        }
-      }
-  }
-  __syncthreads();
-  // ---- P4: T_ii = (I + A_ii)^{-1} ----
-  if (tid < 64) {
-    const int i = tid >> 4, u = tid & 15;
-    const float *A = AD + i * 256;
-    float x[16];
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      float v = t == u ? 1.f : 0.f;
-#pragma unroll
-      for (int s = 0; s < t; ++s) v = fmaf(-A[t * 16 + s], x[s], v);
-      x[t] = v;
-    }
-    __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + O_TI + i * 512);
-#pragma unroll
-    for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
-  }
-  __syncthreads();
-
   // ---- the second load group (v, dO, S0, Unew^T, dS1) ----
   cp_async_wait_group<0>();
   if (__syncthreads_or(!mbar_wait(s_base + O_MBAR, 0))) {
@@ -423,38 +355,41 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
         mma16816(du[mt], af, bf[0], bf[1]);
       }
     }
-    uint8_t *Rm = sm + O_RS + warp * 256;
-    const uint32_t Rs = s_base + O_RS + warp * 256;
-    __nv_bfloat16 *dvg = (__nv_bfloat16 *)p.dv;
-    for (int i = 3; i >= 0; --i) {
-      float z[4] = {du[i][0], du[i][1], du[i][2], du[i][3]};
-      for (int j = i + 1; j < 4; ++j) {
-        uint32_t af[4], bf[2];
-        ldsm_x4_t(ct_frag_addr(s_base + O_AB, 16 * j, 16 * i, lane), af);  // A_ji^T
-        ldsm_x2_t(s_base + O_DR + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
-        float tmp[4] = {};
-        mma16816(tmp, af, bf[0], bf[1]);
+    // dR = Tinv^T dU: stage this warp's dU columns (bf16) in the DR tile, then one GEMM over
+    // the lower block triangle of Tinv
 #pragma unroll
-        for (int x = 0; x < 4; ++x) z[x] -= tmp[x];
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(16 * i + g4 + 8 * hh, n0 + 2 * c4)) =
+            pack_bf16(du[i][2 * hh], du[i][2 * hh + 1]);
+    __syncwarp();
+    float y[4][4] = {};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t bf[2];
+      ldsm_x2_t(s_base + O_DR + sw64(16 * k + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
+#pragma unroll
+      for (int i = 0; i <= k; ++i) {
+        uint32_t af[4];
+        ldsm_x4_t(ct_frag_addr(s_base + O_TF, 16 * k, 16 * i, lane), af);  // Tinv_ki^T
+        mma16816(y[i], af, bf[0], bf[1]);
       }
-      *reinterpret_cast<uint32_t *>(Rm + g4 * 16 + c4 * 4) = pack_bf16(z[0], z[1]);
-      *reinterpret_cast<uint32_t *>(Rm + (g4 + 8) * 16 + c4 * 4) = pack_bf16(z[2], z[3]);
-      __syncwarp();
-      uint32_t af[4], bf[2];
-      ldsm_x4_t(s_base + O_TI + i * 512 + ((lane & 7) + (lane >> 4) * 8) * 32 + ((lane >> 3) & 1) * 16, af);
-      ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
-      float y[4] = {};
-      mma16816(y, af, bf[0], bf[1]);
+    }
+    __syncwarp();
+    __nv_bfloat16 *dvg = (__nv_bfloat16 *)p.dv;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
       float dbv[2] = {0.f, 0.f};
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
-        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(t, col)) = pack_bf16(y[2 * hh], y[2 * hh + 1]);
+        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(t, col)) = pack_bf16(y[i][2 * hh], y[i][2 * hh + 1]);
         const float2 vv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_VS + sw64(t, col)));
-        dbv[hh] = y[2 * hh] * vv.x + y[2 * hh + 1] * vv.y;
+        dbv[hh] = y[i][2 * hh] * vv.x + y[i][2 * hh + 1] * vv.y;
         if (t0 + t < T)
           *reinterpret_cast<uint32_t *>(dvg + base_bh + (int64_t)(t0 + t) * row_stride + col) =
-              pack_bf16(bet[t] * y[2 * hh], bet[t] * y[2 * hh + 1]);
+              pack_bf16(bet[t] * y[i][2 * hh], bet[t] * y[i][2 * hh + 1]);
       }
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -463,7 +398,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         if (c4 == 0) atomicAdd(&dbacc[16 * i + g4 + 8 * hh], v);
       }
-      __syncwarp();
     }
   }
   __syncthreads();

@@ -4,7 +4,7 @@
 //                  state-independent quantity of the chunk, written as a per-chunk record
 //                  (-W, U, Qd, Kb, P as bf16 tiles, e^{gamma_C}) to the forward workspace,
 //                  and, for training, the state-independent part of the backward's record
-//                  (Mneg = -Kb^T W, Qt = Qd - P W).
+//                  (P, M, Tinv = (I+A)^{-1}, Mneg = -Kb^T W, Qt = Qd - P W).
 //  kda_fwd_scan    one CTA of 4 warps per (b, h): streams the chunk records (double-buffered
 //                  cp.async) and advances the fp32 state, which each warp keeps as 16 rows of
 //                  mma accumulator registers:
@@ -55,7 +55,9 @@ constexpr int OFF_AD = OFF_AB + 8192;                    // A diagonal blocks fp
 constexpr int OFF_TI = OFF_AD + 4096;                    // T_ii bf16 4x16x16
 constexpr int OFF_XK = OFF_TI + 2048;                    // beta Kd
 constexpr int OFF_XV = OFF_XK + 8192;                    // beta V
-constexpr int OFF_RS = OFF_XV + 8192;                    // per-warp 16x16 staging
+constexpr int OFF_MK = OFF_XV + 8192;                    // M = Kdec Kinc^T strict lower (bf16)
+constexpr int OFF_TF = OFF_MK + 8192;                    // Tinv = (I + A)^{-1} (bf16), after OFF_MK
+constexpr int OFF_RS = OFF_TF + 8192;                    // per-warp 16x16 staging
 constexpr int OFF_VEC = OFF_RS + 16 * 256;
 // vectors (floats): bet[64] refs[4][64] part[8][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
@@ -63,6 +65,59 @@ constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V
 constexpr int SMEM1 = OFF_VEC + (2368 + 4) * 4;
 
 __device__ __forceinline__ int ki_index(int i, int j) { return i * (i + 1) / 2 + j; }
+
+// Block forward substitution Y = (I+A)^{-1} X for the 8 columns n0..n0+7, by one warp:
+//   Y_i = T_ii (X_i - sum_{j<i} A_ij Y_j),  i = ib..3  (rows of blocks below ib are zero).
+// Y is a swizzled tile at byte offset y_off from OFF_OUT, stored as so * Y; the stored values
+// of earlier blocks are read back with the sign sg = -so.  X is a swizzled tile at x_off, or the
+// identity when x_off < 0 (Y is then Tinv).
+__device__ __forceinline__ void solve_columns(uint8_t *sm, uint32_t s_base, int y_off, int x_off, int n0,
+                                              int ib, float sg, float so, int warp, int lane) {
+  const int g4 = lane >> 2, c4 = lane & 3, l15 = lane & 15;
+  const uint32_t Yb = s_base + OFF_OUT + y_off;
+  uint8_t *Ym = sm + OFF_OUT + y_off;
+  const uint32_t Rs = s_base + OFF_RS + warp * 256;
+  uint8_t *Rm = sm + OFF_RS + warp * 256;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (i < ib) continue;
+    float acc[4] = {};
+#pragma unroll
+    for (int j = 0; j < i; ++j) {
+      if (j < ib) continue;
+      uint32_t af[4], bf[2];
+      ldsm_x4(a_frag_addr(s_base + OFF_AB, 16 * i, 16 * j, lane), af);
+      ldsm_x2_t(Yb + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
+      mma16816(acc, af, bf[0], bf[1]);
+    }
+    // R = X_i + sg * acc -> bf16 staging [t][col] 16x8
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int tl = g4 + 8 * hh, col = n0 + 2 * c4;
+      float2 x;
+      if (x_off >= 0) {
+        x = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + x_off + sw64(16 * i + tl, col)));
+      } else {
+        x.x = 16 * i + tl == col ? 1.f : 0.f;
+        x.y = 16 * i + tl == col + 1 ? 1.f : 0.f;
+      }
+      *reinterpret_cast<uint32_t *>(Rm + tl * 16 + c4 * 4) =
+          pack_bf16(x.x + sg * acc[2 * hh], x.y + sg * acc[2 * hh + 1]);
+    }
+    __syncwarp();
+    uint32_t af[4], bf[2];
+    ldsm_x4(s_base + OFF_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
+    ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
+    float y[4] = {};
+    mma16816(y, af, bf[0], bf[1]);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
+      *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(so * y[2 * hh], so * y[2 * hh + 1]);
+    }
+    __syncwarp();
+  }
+}
 
 template <typename Tb>
 __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
@@ -254,6 +309,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
         }
       }
       AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
       *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(s <= t ? mq : 0.f);
     }
     __syncthreads();
@@ -290,8 +346,11 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
         const int sl = nt * 8 + 2 * c4, s = 16 * j + sl;
         float v0 = acc[nt][2 * hh], v1 = acc[nt][2 * hh + 1];
         if (mat == 0) {
-          v0 = s < t ? bet[t] * v0 : 0.f;
-          v1 = s + 1 < t ? bet[t] * v1 : 0.f;
+          v0 = s < t ? v0 : 0.f;
+          v1 = s + 1 < t ? v1 : 0.f;
+          *reinterpret_cast<uint32_t *>(sm + OFF_MK + sw64(t, s)) = pack_bf16(v0, v1);
+          v0 *= bet[t];
+          v1 *= bet[t];
           if (j == i) {
             AD[i * 256 + tl * 16 + sl] = v0;
             AD[i * 256 + tl * 16 + sl + 1] = v1;
@@ -326,54 +385,26 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   __syncthreads();
 
   // ---- (4) W = (I+A)^{-1} beta Kd (stored negated), U = (I+A)^{-1} beta V; 8 columns per
-  //      warp, each warp's substitution independent of the others ----
-  {
-    const bool isW = warp < 8;
-    const int n0 = (warp & 7) * 8, l15 = lane & 15;
-    const uint32_t Yb = ho + (isW ? HO_W : HO_U);
-    uint8_t *Ym = hom + (isW ? HO_W : HO_U);
-    const uint8_t *Xm = sm + (isW ? OFF_XK : OFF_XV);
-    const uint32_t Rs = s_base + OFF_RS + warp * 256;
-    uint8_t *Rm = sm + OFF_RS + warp * 256;
-    const float sg = isW ? 1.f : -1.f, so = isW ? -1.f : 1.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float acc[4] = {};
-#pragma unroll
-      for (int j = 0; j < i; ++j) {
-        uint32_t af[4], bf[2];
-        ldsm_x4(a_frag_addr(s_base + OFF_AB, 16 * i, 16 * j, lane), af);
-        ldsm_x2_t(Yb + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
-        mma16816(acc, af, bf[0], bf[1]);
-      }
-      // R = X_i -/+ acc  (the stored Y of the W half is -W) -> bf16 staging [t][col] 16x8
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int tl = g4 + 8 * hh, col = n0 + 2 * c4;
-        const float2 x = unpack_bf16(*reinterpret_cast<const uint32_t *>(Xm + sw64(16 * i + tl, col)));
-        *reinterpret_cast<uint32_t *>(Rm + tl * 16 + c4 * 4) =
-            pack_bf16(x.x + sg * acc[2 * hh], x.y + sg * acc[2 * hh + 1]);
-      }
-      __syncwarp();
-      uint32_t af[4], bf[2];
-      ldsm_x4(s_base + OFF_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
-      ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
-      float y[4] = {};
-      mma16816(y, af, bf[0], bf[1]);
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
-        *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(so * y[2 * hh], so * y[2 * hh + 1]);
-      }
-      __syncwarp();
-    }
-  }
+  //      warp, each warp's substitution independent of the others.  For training, warps 8-15
+  //      then also solve for the 8 columns (warp - 8) * 8.. of Tinv = (I+A)^{-1} itself, which
+  //      the backward applies as one GEMM instead of a second triangular solve. ----
+  if (warp < 8)
+    solve_columns(sm, s_base, HO_W, OFF_XK, (warp & 7) * 8, 0, 1.f, -1.f, warp, lane);
+  else
+    solve_columns(sm, s_base, HO_U, OFF_XV, (warp & 7) * 8, 0, -1.f, 1.f, warp, lane);
+  if (p.saved && warp >= 8)
+    solve_columns(sm, s_base, OFF_TF - OFF_OUT, -1, (warp & 7) * 8, (warp & 7) >> 1, -1.f, 1.f, warp, lane);
 
   fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
   // ---- the record for kda_fwd_scan: one bulk copy, same swizzled layout as in smem ----
   if (tid == 0) {
     bulk_s2g((uint8_t *)p.ws + (int64_t)idx * HO_SIZE, ho, HO_SIZE);
+    if (p.saved) {  // P, M, Tinv for the backward
+      uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
+      bulk_s2g(sv + kSavedP, ho + HO_P, 8192);
+      bulk_s2g(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192);
+    }
     bulk_commit();
   }
   // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-3,
