@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
 // ---------------------------------------------------------------------------------------
 // chunk-parallel gradients
 // ---------------------------------------------------------------------------------------
-constexpr int CK_NT = 256;
+constexpr int CK_NT = 512;  // 16 warps; warp w owns row block mt = w / 4, columns 16 * (w % 4)..
 constexpr int O_QS = 0, O_KS = 8192, O_VS = 16384, O_DO = 24576;   // raw bf16 tiles [t][d]
 constexpr int O_GS = 32768;                                         // g -> gamma -> F -> dgamma fp32
 // S0 [j][d], Unew^T [j][t], P [t][s], M [t][s], Tinv [t][s]: one bulk copy of the saved record
@@ -171,10 +171,9 @@ constexpr int O_S0 = 49152, O_UN = 57344, O_PB = 65536, O_MK = 73728, O_TF = 819
 constexpr int O_DS = 90112;                                         // dS1 [j][d]
 constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
 constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
-constexpr int O_RS = 155648;                                        // 8 warps x 256 B staging
-constexpr int O_VEC = O_RS + 8 * 256;
-constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088,
-              V_EG = 2112, V_DB = 2176, V_DGM = 2240, V_FLAG = 2304;
+constexpr int O_VEC = 155648;
+constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
+              V_EG = 2368, V_DB = 2432, V_DGM = 2496, V_FLAG = 2560;
 constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;
 constexpr int CK_SMEM = O_MBAR + 8;
 
@@ -183,6 +182,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
+  const int mt = warp >> 2, nq = warp & 3, n0 = 16 * nq;
   const int nc = p.nc, idx = blockIdx.x, bh = idx / nc, c = idx % nc;
   const int b = bh / p.H, h = bh % p.H, T = p.T, H = p.H, t0 = c * C;
   const uint32_t s_base = smem_u32(sm);
@@ -236,20 +236,20 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     cp_async_wait_group<1>();
     __syncthreads();
   }
-  // ---- P1: gamma = cumsum(g), guard, per-block vectors ----
+  // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
   {
     const int d = tid & 63, seg = tid >> 6;
     float acc = 0.f;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc += GS[(seg * 16 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) acc += GS[(seg * 8 + r) * 64 + d];
     part[seg * 64 + d] = acc;
     __syncthreads();
     float off = 0.f;
     for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      off += GS[(seg * 16 + r) * 64 + d];
-      GS[(seg * 16 + r) * 64 + d] = off;
+    for (int r = 0; r < 8; ++r) {
+      off += GS[(seg * 8 + r) * 64 + d];
+      GS[(seg * 8 + r) * 64 + d] = off;
     }
     __syncthreads();
   }
@@ -315,9 +315,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     *reinterpret_cast<uint4 *>(sm + O_KF + off) = make_uint4(okf[0], okf[1], okf[2], okf[3]);
     *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
   }
-  __syncthreads();
 
-  // ---- the second load group (v, dO, S0, Unew^T, dS1) ----
+  // ---- the second load group (v, dO, S0, Unew^T, P, M, Tinv, dS1) ----
   cp_async_wait_group<0>();
   if (__syncthreads_or(!mbar_wait(s_base + O_MBAR, 0))) {
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
@@ -328,112 +327,100 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     const int d = tid & 63, jq = tid >> 6;
     float a = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int row = jq * 16 + j;
+    for (int j = 0; j < 8; ++j) {
+      const int row = jq * 8 + j;
       a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(row, d))) *
            __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
     }
     atomicAdd(&dgacc[d], a * eG[d]);
   }
-  // ---- P5: dU = P^T dO + Kb dS1^T and dR = (I + A)^{-T} dU, 8 value columns per warp ----
+  // ---- P5: dU = P^T dO + Kb dS1^T (staged bf16 in the DP tile), dR = Tinv^T dU ----
   {
-    const int n0 = warp * 8, l15 = lane & 15;
-    float du[4][4] = {};
+    float du[2][4] = {};
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        if (kk >= mt) {
-          uint32_t af[4], bf[2];
-          ldsm_x4_t(ct_frag_addr(s_base + O_PB, 16 * kk, 16 * mt, lane), af);  // P^T
-          ldsm_x2_t(s_base + O_DO + sw64(16 * kk + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
-          mma16816(du[mt], af, bf[0], bf[1]);
-        }
-        uint32_t af[4], bf[2];
-        ldsm_x4(a_frag_addr(s_base + O_KB, 16 * mt, 16 * kk, lane), af);
-        ldsm_x2(s_base + O_DS + sw64(n0 + (l15 & 7), 16 * kk + ((l15 >> 3) << 3)), bf);
-        mma16816(du[mt], af, bf[0], bf[1]);
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t af[4], bf[4];
+      if (kk >= mt) {
+        ldsm_x4_t(ct_frag_addr(s_base + O_PB, 16 * kk, 16 * mt, lane), af);  // P^T
+        ldsm_x4_t(bkn_frag_addr(s_base + O_DO, 16 * kk, n0, lane), bf);
+        mma16816(du[0], af, bf[0], bf[1]);
+        mma16816(du[1], af, bf[2], bf[3]);
       }
+      ldsm_x4(a_frag_addr(s_base + O_KB, 16 * mt, 16 * kk, lane), af);
+      ldsm_x4(bnk_frag_addr(s_base + O_DS, n0, 16 * kk, lane), bf);
+      mma16816(du[0], af, bf[0], bf[1]);
+      mma16816(du[1], af, bf[2], bf[3]);
     }
-    // dR = Tinv^T dU: stage this warp's dU columns (bf16) in the DR tile, then one GEMM over
-    // the lower block triangle of Tinv
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh)
-        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(16 * i + g4 + 8 * hh, n0 + 2 * c4)) =
-            pack_bf16(du[i][2 * hh], du[i][2 * hh + 1]);
-    __syncwarp();
-    float y[4][4] = {};
+        *reinterpret_cast<uint32_t *>(sm + O_DP + sw64(16 * mt + g4 + 8 * hh, n0 + 8 * nt + 2 * c4)) =
+            pack_bf16(du[nt][2 * hh], du[nt][2 * hh + 1]);
+  }
+  __syncthreads();
+  {
+    float y[2][4] = {};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      uint32_t bf[2];
-      ldsm_x2_t(s_base + O_DR + sw64(16 * k + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
-#pragma unroll
-      for (int i = 0; i <= k; ++i) {
-        uint32_t af[4];
-        ldsm_x4_t(ct_frag_addr(s_base + O_TF, 16 * k, 16 * i, lane), af);  // Tinv_ki^T
-        mma16816(y[i], af, bf[0], bf[1]);
-      }
+      if (k < mt) continue;
+      uint32_t af[4], bf[4];
+      ldsm_x4_t(ct_frag_addr(s_base + O_TF, 16 * k, 16 * mt, lane), af);  // Tinv_k,mt^T
+      ldsm_x4_t(bkn_frag_addr(s_base + O_DP, 16 * k, n0, lane), bf);
+      mma16816(y[0], af, bf[0], bf[1]);
+      mma16816(y[1], af, bf[2], bf[3]);
     }
-    __syncwarp();
     __nv_bfloat16 *dvg = (__nv_bfloat16 *)p.dv;
+    float dbv[2] = {0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float dbv[2] = {0.f, 0.f};
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
-        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(t, col)) = pack_bf16(y[i][2 * hh], y[i][2 * hh + 1]);
+        const int t = 16 * mt + g4 + 8 * hh, col = n0 + 8 * nt + 2 * c4;
+        *reinterpret_cast<uint32_t *>(sm + O_DR + sw64(t, col)) = pack_bf16(y[nt][2 * hh], y[nt][2 * hh + 1]);
         const float2 vv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_VS + sw64(t, col)));
-        dbv[hh] = y[i][2 * hh] * vv.x + y[i][2 * hh + 1] * vv.y;
+        dbv[hh] += y[nt][2 * hh] * vv.x + y[nt][2 * hh + 1] * vv.y;
         if (t0 + t < T)
           *reinterpret_cast<uint32_t *>(dvg + base_bh + (int64_t)(t0 + t) * row_stride + col) =
-              pack_bf16(bet[t] * y[i][2 * hh], bet[t] * y[i][2 * hh + 1]);
+              pack_bf16(bet[t] * y[nt][2 * hh], bet[t] * y[nt][2 * hh + 1]);
       }
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        float v = dbv[hh];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (c4 == 0) atomicAdd(&dbacc[16 * i + g4 + 8 * hh], v);
-      }
+    for (int hh = 0; hh < 2; ++hh) {
+      float v = dbv[hh];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
     }
   }
   __syncthreads();
 
-  // ---- P6..P8: per warp 16 rows (block mt) x 32 columns (half nh) of dq, dk ----
-  const int mt = warp >> 1, nh = warp & 1;
-  float DQ[4][4], DKp[4][4], DKm[4][4], Fv[4][4];
+  // ---- P6..P8: per warp rows 16 * mt.. and columns n0.. of dq, dk ----
+  float DQ[2][4], DKp[2][4], DKm[2][4], Fv[2][4];
   {
-    float dRS[4][4] = {}, dOS[4][4] = {}, dKb[4][4] = {};
+    float dRS[2][4] = {}, dOS[2][4] = {}, dKb[2][4] = {};
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t aR[4], aO[4], aU[4];
+      uint32_t aR[4], aO[4], aU[4], bS[4], bD[4];
       ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
       ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
       ldsm_x4_t(ct_frag_addr(s_base + O_UN, 16 * kk, 16 * mt, lane), aU);  // Unew rows t, k = j
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bS[4], bD[4];
-        ldsm_x4_t(bkn_frag_addr(s_base + O_S0, 16 * kk, 32 * nh + 16 * np, lane), bS);
-        ldsm_x4_t(bkn_frag_addr(s_base + O_DS, 16 * kk, 32 * nh + 16 * np, lane), bD);
-        mma16816(dRS[2 * np], aR, bS[0], bS[1]);
-        mma16816(dRS[2 * np + 1], aR, bS[2], bS[3]);
-        mma16816(dOS[2 * np], aO, bS[0], bS[1]);
-        mma16816(dOS[2 * np + 1], aO, bS[2], bS[3]);
-        mma16816(dKb[2 * np], aU, bD[0], bD[1]);
-        mma16816(dKb[2 * np + 1], aU, bD[2], bD[3]);
-      }
+      ldsm_x4_t(bkn_frag_addr(s_base + O_S0, 16 * kk, n0, lane), bS);
+      ldsm_x4_t(bkn_frag_addr(s_base + O_DS, 16 * kk, n0, lane), bD);
+      mma16816(dRS[0], aR, bS[0], bS[1]);
+      mma16816(dRS[1], aR, bS[2], bS[3]);
+      mma16816(dOS[0], aO, bS[0], bS[1]);
+      mma16816(dOS[1], aO, bS[2], bS[3]);
+      mma16816(dKb[0], aU, bD[0], bD[1]);
+      mma16816(dKb[1], aU, bD[2], bD[3]);
     }
-    float dbr[2] = {0.f, 0.f}, dgc[4][2] = {};
+    float dbr[2] = {0.f, 0.f}, dgc[2][2] = {};
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const int t = 16 * mt + g4 + 8 * hh, d = 32 * nh + 8 * nt + 2 * c4 + x, e = 2 * hh + x;
+          const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4 + x, e = 2 * hh + x;
           const float F = GS[t * 64 + d];
           const float eg = F * erb[mt * 64 + d], eb = __fdividef(egr[mt * 64 + d], F);
           const float kv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_KS + sw64(t, d)));
@@ -452,48 +439,45 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         float v = dgc[nt][x];
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 8);
         v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if (g4 == 0) atomicAdd(&dgacc[32 * nh + 8 * nt + 2 * c4 + x], v);
+        if (g4 == 0) atomicAdd(&dgacc[n0 + 8 * nt + 2 * c4 + x], v);
       }
   }
-  // ---- P7: dP = dO Unew^T (s <= t), dKK = -beta dR Unew^T (s < t), dbeta += dA . M ----
-  {
+  // ---- P7: block (mt, sb = nq) of dP = dO Unew^T (s <= t) and dKK = -beta dR Unew^T (s < t),
+  //      dbeta += dA . M ----
+  if (nq <= mt) {
+    const int sb = nq;
+    float aP[2][4] = {}, aA[2][4] = {};
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t aO[4], aR[4], bU[4];
+      ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
+      ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
+      ldsm_x4_t(bkn_frag_addr(s_base + O_UN, 16 * kk, 16 * sb, lane), bU);
+      mma16816(aP[0], aO, bU[0], bU[1]);
+      mma16816(aP[1], aO, bU[2], bU[3]);
+      mma16816(aA[0], aR, bU[0], bU[1]);
+      mma16816(aA[1], aR, bU[2], bU[3]);
+    }
     float dbr[2] = {0.f, 0.f};
 #pragma unroll
-    for (int np = 0; np < 2; ++np) {
-      const int sb = 2 * nh + np;
-      if (sb > mt) continue;
-      float aP[2][4] = {}, aA[2][4] = {};
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t aO[4], aR[4], bU[4];
-        ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
-        ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
-        ldsm_x4_t(bkn_frag_addr(s_base + O_UN, 16 * kk, 16 * sb, lane), bU);
-        mma16816(aP[0], aO, bU[0], bU[1]);
-        mma16816(aP[1], aO, bU[2], bU[3]);
-        mma16816(aA[0], aR, bU[0], bU[1]);
-        mma16816(aA[1], aR, bU[2], bU[3]);
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = 16 * mt + g4 + 8 * hh, s = 16 * sb + 8 * nt + 2 * c4;
+        const float p0 = s <= t ? aP[nt][2 * hh] : 0.f, p1 = s + 1 <= t ? aP[nt][2 * hh + 1] : 0.f;
+        const float a0 = s < t ? -aA[nt][2 * hh] : 0.f, a1 = s + 1 < t ? -aA[nt][2 * hh + 1] : 0.f;
+        *reinterpret_cast<uint32_t *>(sm + O_DP + sw64(t, s)) = pack_bf16(p0, p1);
+        *reinterpret_cast<uint32_t *>(sm + O_DK + sw64(t, s)) = pack_bf16(bet[t] * a0, bet[t] * a1);
+        const float2 m = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_MK + sw64(t, s)));
+        dbr[hh] += a0 * m.x + a1 * m.y;
       }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int t = 16 * mt + g4 + 8 * hh, s = 16 * sb + 8 * nt + 2 * c4;
-          const float p0 = s <= t ? aP[nt][2 * hh] : 0.f, p1 = s + 1 <= t ? aP[nt][2 * hh + 1] : 0.f;
-          const float a0 = s < t ? -aA[nt][2 * hh] : 0.f, a1 = s + 1 < t ? -aA[nt][2 * hh + 1] : 0.f;
-          *reinterpret_cast<uint32_t *>(sm + O_DP + sw64(t, s)) = pack_bf16(p0, p1);
-          *reinterpret_cast<uint32_t *>(sm + O_DK + sw64(t, s)) = pack_bf16(bet[t] * a0, bet[t] * a1);
-          const float2 m = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_MK + sw64(t, s)));
-          dbr[hh] += a0 * m.x + a1 * m.y;
-        }
-    }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       float v = dbr[hh];
@@ -505,54 +489,46 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   __syncthreads();
   // ---- P8: decayed products ----
   {
-    float Q2[4][4] = {}, K2[4][4] = {}, M2[4][4] = {};
+    float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {};
     for (int j = 0; j <= mt; ++j) {  // rows t in block mt, columns s in block j
-      float T1[4][4] = {}, T2[4][4] = {};
-      uint32_t aP[4], aK[4];
+      float T1[2][4] = {}, T2[2][4] = {};
+      uint32_t aP[4], aK[4], bK[4];
       ldsm_x4(a_frag_addr(s_base + O_DP, 16 * mt, 16 * j, lane), aP);
       ldsm_x4(a_frag_addr(s_base + O_DK, 16 * mt, 16 * j, lane), aK);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bK[4];
-        ldsm_x4_t(bkn_frag_addr(s_base + O_KF, 16 * j, 32 * nh + 16 * np, lane), bK);
-        mma16816(T1[2 * np], aP, bK[0], bK[1]);
-        mma16816(T1[2 * np + 1], aP, bK[2], bK[3]);
-        mma16816(T2[2 * np], aK, bK[0], bK[1]);
-        mma16816(T2[2 * np + 1], aK, bK[2], bK[3]);
-      }
+      ldsm_x4_t(bkn_frag_addr(s_base + O_KF, 16 * j, n0, lane), bK);
+      mma16816(T1[0], aP, bK[0], bK[1]);
+      mma16816(T1[1], aP, bK[2], bK[3]);
+      mma16816(T2[0], aK, bK[0], bK[1]);
+      mma16816(T2[1], aK, bK[2], bK[3]);
       const float *G = gij + (mt * 4 + j) * 64;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float gv = G[32 * nh + 8 * nt + 2 * c4 + (e & 1)];
+          const float gv = G[n0 + 8 * nt + 2 * c4 + (e & 1)];
           Q2[nt][e] += gv * T1[nt][e];
           K2[nt][e] += gv * T2[nt][e];
         }
     }
     for (int i = mt; i < 4; ++i) {  // rows s in block mt, sum over t in block i
-      float T3[4][4] = {};
-      uint32_t aKt[4], aPt[4];
+      float T3[2][4] = {};
+      uint32_t aKt[4], aPt[4], bK[4], bQ[4];
       ldsm_x4_t(ct_frag_addr(s_base + O_DK, 16 * i, 16 * mt, lane), aKt);
       ldsm_x4_t(ct_frag_addr(s_base + O_DP, 16 * i, 16 * mt, lane), aPt);
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bK[4], bQ[4];
-        ldsm_x4_t(bkn_frag_addr(s_base + O_KD, 16 * i, 32 * nh + 16 * np, lane), bK);
-        ldsm_x4_t(bkn_frag_addr(s_base + O_QD, 16 * i, 32 * nh + 16 * np, lane), bQ);
-        mma16816(T3[2 * np], aKt, bK[0], bK[1]);
-        mma16816(T3[2 * np + 1], aKt, bK[2], bK[3]);
-        mma16816(T3[2 * np], aPt, bQ[0], bQ[1]);
-        mma16816(T3[2 * np + 1], aPt, bQ[2], bQ[3]);
-      }
+      ldsm_x4_t(bkn_frag_addr(s_base + O_KD, 16 * i, n0, lane), bK);
+      ldsm_x4_t(bkn_frag_addr(s_base + O_QD, 16 * i, n0, lane), bQ);
+      mma16816(T3[0], aKt, bK[0], bK[1]);
+      mma16816(T3[1], aKt, bK[2], bK[3]);
+      mma16816(T3[0], aPt, bQ[0], bQ[1]);
+      mma16816(T3[1], aPt, bQ[2], bQ[3]);
       const float *G = gij + (i * 4 + mt) * 64;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) M2[nt][e] += G[32 * nh + 8 * nt + 2 * c4 + (e & 1)] * T3[nt][e];
+        for (int e = 0; e < 4; ++e) M2[nt][e] += G[n0 + 8 * nt + 2 * c4 + (e & 1)] * T3[nt][e];
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         DQ[nt][e] += Fv[nt][e] * Q2[nt][e];
@@ -563,32 +539,33 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   // ---- P9: dgamma, dg = reverse cumsum, outputs ----
   __syncthreads();  // every warp is done reading gamma, MK and PB
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt)
+  for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const int t = 16 * mt + g4 + 8 * hh, d = 32 * nh + 8 * nt + 2 * c4;
+      const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4;
       const float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t, d)));
       const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
       const int e = 2 * hh;
-      GS[t * 64 + d] = qv.x * DQ[nt][e] + kv.x * (DKp[nt][e] - DKm[nt][e]);
-      GS[t * 64 + d + 1] = qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]);
+      *reinterpret_cast<float2 *>(GS + t * 64 + d) =
+          make_float2(qv.x * DQ[nt][e] + kv.x * (DKp[nt][e] - DKm[nt][e]),
+                      qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]));
       *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, d)) = pack_bf16(DQ[nt][e], DQ[nt][e + 1]);
       *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, d)) =
           pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
     }
   __syncthreads();
-  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up): 4 segments of 16 rows
+  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up): 8 segments of 8 rows
     const int d = tid & 63, seg = tid >> 6;
     float ssum = 0.f;
 #pragma unroll
-    for (int r = 0; r < 16; ++r) ssum += GS[(seg * 16 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) ssum += GS[(seg * 8 + r) * 64 + d];
     part[seg * 64 + d] = ssum;
     __syncthreads();
     float acc = dgacc[d];
-    for (int s2 = seg + 1; s2 < 4; ++s2) acc += part[s2 * 64 + d];
+    for (int s2 = seg + 1; s2 < 8; ++s2) acc += part[s2 * 64 + d];
 #pragma unroll
-    for (int r = 15; r >= 0; --r) {
-      const int t = seg * 16 + r;
+    for (int r = 7; r >= 0; --r) {
+      const int t = seg * 8 + r;
       acc += GS[t * 64 + d];
       if (t0 + t < T) p.dg[base_bh + (int64_t)(t0 + t) * row_stride + d] = acc;
     }
