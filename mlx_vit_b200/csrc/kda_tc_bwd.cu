@@ -300,15 +300,16 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     for (int e = 0; e < 4; ++e) {
       const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
       const int d = d0 + 2 * e;
-      const float F0 = __expf(GS[t * 64 + d] - refs[blk * 64 + d]);
-      const float F1 = __expf(GS[t * 64 + d + 1] - refs[blk * 64 + d + 1]);
-      GS[t * 64 + d] = F0;  // from here on GS holds F = e^{gamma - r_b(t)}
-      GS[t * 64 + d + 1] = F1;
+      const float2 gm = *reinterpret_cast<const float2 *>(GS + t * 64 + d);
+      const float2 rf = *reinterpret_cast<const float2 *>(refs + blk * 64 + d);
+      const float2 er = *reinterpret_cast<const float2 *>(egr + blk * 64 + d);
+      const float F0 = __expf(gm.x - rf.x), F1 = __expf(gm.y - rf.y);
+      *reinterpret_cast<float2 *>(GS + t * 64 + d) = make_float2(F0, F1);  // GS holds F = e^{gamma - r_b(t)}
       const float i0 = __fdividef(1.f, F0), i1 = __fdividef(1.f, F1);
       okd[e] = pack_bf16(kf.x * F0, kf.y * F1);
       oqd[e] = pack_bf16(qf.x * F0, qf.y * F1);
       okf[e] = pack_bf16(kf.x * i0, kf.y * i1);
-      okb[e] = pack_bf16(kf.x * i0 * egr[blk * 64 + d], kf.y * i1 * egr[blk * 64 + d + 1]);
+      okb[e] = pack_bf16(kf.x * i0 * er.x, kf.y * i1 * er.y);
     }
     *reinterpret_cast<uint4 *>(sm + O_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
     *reinterpret_cast<uint4 *>(sm + O_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
@@ -415,22 +416,30 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     }
     float dbr[2] = {0.f, 0.f}, dgc[2][2] = {};
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int nt = 0; nt < 2; ++nt) {
+      const int d = n0 + 8 * nt + 2 * c4;
+      const float2 er = *reinterpret_cast<const float2 *>(erb + mt * 64 + d);
+      const float2 eq = *reinterpret_cast<const float2 *>(egr + mt * 64 + d);
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = 16 * mt + g4 + 8 * hh;
+        const float2 F = *reinterpret_cast<const float2 *>(GS + t * 64 + d);
+        const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
+        const float nb = -bet[t];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4 + x, e = 2 * hh + x;
-          const float F = GS[t * 64 + d];
-          const float eg = F * erb[mt * 64 + d], eb = __fdividef(egr[mt * 64 + d], F);
-          const float kv = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_KS + sw64(t, d)));
-          Fv[nt][e] = F;
+          const int e = 2 * hh + x;
+          const float f = x ? F.y : F.x, k_ = x ? kv.y : kv.x;
+          const float eg = f * (x ? er.y : er.x), eb = __fdividef(x ? eq.y : eq.x, f);
+          Fv[nt][e] = f;
           DQ[nt][e] = dOS[nt][e] * eg;
-          DKp[nt][e] = -bet[t] * dRS[nt][e] * eg;
+          DKp[nt][e] = nb * dRS[nt][e] * eg;
           DKm[nt][e] = dKb[nt][e] * eb;
-          dbr[hh] -= dRS[nt][e] * kv * eg;
-          dgc[nt][x] += kv * DKm[nt][e];
+          dbr[hh] -= dRS[nt][e] * k_ * eg;
+          dgc[nt][x] += k_ * DKm[nt][e];
         }
+      }
+    }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       float v = dbr[hh];
@@ -502,13 +511,15 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       mma16816(T2[1], aK, bK[2], bK[3]);
       const float *G = gij + (mt * 4 + j) * 64;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt) {
+        const float2 g2 = *reinterpret_cast<const float2 *>(G + n0 + 8 * nt + 2 * c4);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float gv = G[n0 + 8 * nt + 2 * c4 + (e & 1)];
+          const float gv = (e & 1) ? g2.y : g2.x;
           Q2[nt][e] += gv * T1[nt][e];
           K2[nt][e] += gv * T2[nt][e];
         }
+      }
     }
     for (int i = mt; i < 4; ++i) {  // rows s in block mt, sum over t in block i
       float T3[2][4] = {};
@@ -523,9 +534,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       mma16816(T3[1], aPt, bQ[2], bQ[3]);
       const float *G = gij + (i * 4 + mt) * 64;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt) {
+        const float2 g2 = *reinterpret_cast<const float2 *>(G + n0 + 8 * nt + 2 * c4);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) M2[nt][e] += G[n0 + 8 * nt + 2 * c4 + (e & 1)] * T3[nt][e];
+        for (int e = 0; e < 4; ++e) M2[nt][e] += ((e & 1) ? g2.y : g2.x) * T3[nt][e];
+      }
     }
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)

@@ -243,14 +243,18 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
       const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
       const int d = d0 + 2 * e;
       float F[2], iF[2], eg[2], eb[2];
+      const float2 rf2 = *reinterpret_cast<const float2 *>(refs + blk * 64 + d);
+      const float2 er2 = *reinterpret_cast<const float2 *>(erb + blk * 64 + d);
+      const float2 eq2 = *reinterpret_cast<const float2 *>(egr + blk * 64 + d);
+      const float rf[2] = {rf2.x, rf2.y}, er[2] = {er2.x, er2.y}, eq[2] = {eq2.x, eq2.y};
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         const float gm = gam[2 * e + x];
-        F[x] = __expf(gm - refs[blk * 64 + d + x]);
+        F[x] = __expf(gm - rf[x]);
         if (!big) {
           iF[x] = __fdividef(1.f, F[x]);
-          eg[x] = F[x] * erb[blk * 64 + d + x];
-          eb[x] = iF[x] * egr[blk * 64 + d + x];
+          eg[x] = F[x] * er[x];
+          eb[x] = iF[x] * eq[x];
         } else {
           iF[x] = 0.f;
           eg[x] = __expf(gm);
@@ -268,8 +272,9 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
         float s0 = 0.f, s1 = 0.f;
         if (i >= blk) {
           if (!big) {
-            s0 = iF[0] * gij[(i * 4 + blk) * 64 + d];
-            s1 = iF[1] * gij[(i * 4 + blk) * 64 + d + 1];
+            const float2 gg = *reinterpret_cast<const float2 *>(gij + (i * 4 + blk) * 64 + d);
+            s0 = iF[0] * gg.x;
+            s1 = iF[1] * gg.y;
           } else {
             s0 = __expf(refs[i * 64 + d] - gam[2 * e]);
             s1 = __expf(refs[i * 64 + d + 1] - gam[2 * e + 1]);
