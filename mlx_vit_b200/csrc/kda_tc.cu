@@ -21,3 +21,42 @@ size_t tc_saved_bytes(const KdaDesc *d) {
   return (size_t)(d->B * d->H * nc) * kSavedChunk;
 }
 }  // namespace kda
+
+// ---- tensor maps ----
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "kda_tma.cuh"
+
+namespace kda {
+
+static PFN_cuTensorMapEncodeTiled encode_fn() {
+  static PFN_cuTensorMapEncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+  });
+  return fn;
+}
+
+int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32) {
+  PFN_cuTensorMapEncodeTiled fn = encode_fn();
+  if (!fn) return KDA_ERR_CUDA;
+  const int64_t es = fp32 ? 4 : 2;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(H * D * es), (cuuint64_t)(T * H * D * es)};
+  const cuuint32_t box[4] = {(cuuint32_t)D, 1, 64, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                        const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        fp32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? KDA_OK : KDA_ERR_INVALID_ARG;
+}
+
+}  // namespace kda

@@ -24,6 +24,7 @@
 // 2318-2456) with U = (I+A)^{-1} beta (V - K_proj S^T) split into U - W S^T.
 #include "kda_common.cuh"
 #include "kda_mma.cuh"
+#include "kda_tma.cuh"
 
 namespace kda {
 namespace tcfwd {
@@ -42,12 +43,12 @@ constexpr int HO_SIZE = 40960 + 256;
 // kda_fwd_chunks
 // ---------------------------------------------------------------------------------------
 constexpr int NT1 = 512;  // 16 warps: every phase splits into more independent pieces
-constexpr int OFF_OUT = 0;                               // the record, swizzled tiles
-constexpr int OFF_QS = OFF_OUT + HO_SIZE;                // raw q/k/v tiles (bf16, swizzled)
-constexpr int OFF_KS = OFF_QS + 8192;
+constexpr int OFF_QS = 0;                                // raw q/k/v tiles (TMA, 128-byte swizzle,
+constexpr int OFF_KS = OFF_QS + 8192;                    //   1024-byte aligned)
 constexpr int OFF_VS = OFF_KS + 8192;
-constexpr int OFF_GS = OFF_VS + 8192;                    // g -> gamma (fp32 [t][d]) 16 KB
-constexpr int OFF_KD = OFF_GS + 16384;                   // Kdec
+constexpr int OFF_GS = OFF_VS + 8192;                    // g (TMA) -> gamma (fp32 [t][d]) 16 KB
+constexpr int OFF_OUT = OFF_GS + 16384;                  // the record, swizzled tiles
+constexpr int OFF_KD = OFF_OUT + HO_SIZE;                // Kdec
 constexpr int OFF_QD = OFF_KD + 8192;                    // Qdec
 constexpr int OFF_KI = OFF_QD + 8192;                    // Kinc, 10 tiles of 16x64
 constexpr int OFF_AB = OFF_KI + 10 * 2048;               // A off-diagonal blocks (bf16)
@@ -62,7 +63,8 @@ constexpr int OFF_VEC = OFF_RS + 16 * 256;
 // vectors (floats): bet[64] refs[4][64] part[8][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
               V_FLAG = 2368;
-constexpr int SMEM1 = OFF_VEC + (2368 + 4) * 4;
+constexpr int OFF_MBAR1 = OFF_VEC + (2368 + 4) * 4;      // mbarrier of the TMA loads
+constexpr int SMEM1 = OFF_MBAR1 + 8;
 
 __device__ __forceinline__ int ki_index(int i, int j) { return i * (i + 1) / 2 + j; }
 
@@ -120,13 +122,16 @@ __device__ __forceinline__ void solve_columns(uint8_t *sm, uint32_t s_base, int 
 }
 
 template <typename Tb>
-__global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
+__global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
   const int nc = p.nc, T = p.T, H = p.H, nchunks = p.B * p.H * nc;
   const uint32_t s_base = smem_u32(sm);
-  const int64_t row_stride = (int64_t)H * D;
+  if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
+    if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
+    return;
+  }
   float *GS = reinterpret_cast<float *>(sm + OFF_GS);
   float *AD = reinterpret_cast<float *>(sm + OFF_AD);
   float *vec = reinterpret_cast<float *>(sm + OFF_VEC);
@@ -137,26 +142,24 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   const uint32_t ho = s_base + OFF_OUT;
   float *eG = reinterpret_cast<float *>(hom + HO_EG);
   const Tb *betag = (const Tb *)p.beta;
-  const __nv_bfloat16 *src[3] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
-                                 (const __nv_bfloat16 *)p.v};
 
-  // the CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...; the loads of the
-  // next chunk are issued as soon as this chunk's raw tiles are consumed
+  // the CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...; the TMA loads of
+  // the next chunk are issued as soon as this chunk's raw tiles are consumed
+  const uint32_t mbar = s_base + OFF_MBAR1;
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
   auto issue_loads = [&](int i) {  // q, k, v tiles (swizzled) and g (fp32) of chunk i
-    const int bh_ = i / nc, c_ = i % nc, b_ = bh_ / H, h_ = bh_ % H, t0_ = c_ * C;
-    const int64_t base_ = ((int64_t)b_ * T * H + h_) * D;
-    for (int u = tid; u < 3 * 512; u += NT1) {
-      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0_ + r;
-      const bool in = t < T;
-      cp_async16(s_base + OFF_QS + which * 8192 + sw64(r, ch * 8),
-                 src[which] + base_ + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
+    if (tid == 0) {
+      const int bh_ = i / nc, t0_ = (i % nc) * C, b_ = bh_ / H, h_ = bh_ % H;
+      mbar_expect_tx(mbar, 3 * 8192 + 16384);
+      tma_load_rows(s_base + OFF_QS, &tm.m[0], h_, t0_, b_, mbar);
+      tma_load_rows(s_base + OFF_KS, &tm.m[1], h_, t0_, b_, mbar);
+      tma_load_rows(s_base + OFF_VS, &tm.m[2], h_, t0_, b_, mbar);
+      tma_load_rows(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
     }
-    for (int u = tid; u < 1024; u += NT1) {
-      const int r = u >> 4, ch = u & 15, t = t0_ + r;
-      const bool in = t < T;
-      cp_async16(s_base + OFF_GS + r * 256 + ch * 16, p.g + base_ + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
-    }
-    cp_async_commit();
   };
   auto load_beta = [&](int i) -> float {
     const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
@@ -166,11 +169,12 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
   if (idx < nchunks) issue_loads(idx);
   float beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : 0.f;
 
-  for (; idx < nchunks; idx += gridDim.x) {
-  const int bh = idx / nc, c = idx % nc, b = bh / H, h = bh % H, t0 = c * C;
-  (void)b; (void)h; (void)t0;
+  for (int it = 0; idx < nchunks; idx += gridDim.x, ++it) {
   if (tid == 0) bulk_wait_read_all();  // the previous chunk's bulk stores have read smem
-  cp_async_wait_all();
+  if (__syncthreads_or(!mbar_wait(mbar, it & 1))) {  // this chunk's q, k, v, g
+    if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+    break;
+  }
   if (tid < C) bet[tid] = beta_next;
   __syncthreads();
 
@@ -489,21 +493,23 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p) {
 // kda_fwd_scan
 // ---------------------------------------------------------------------------------------
 constexpr int NT2 = 128;
-constexpr int OFF2_REC = 0;                 // 2 x HO_SIZE, swizzled tiles
-constexpr int OFF2_O = 2 * HO_SIZE;         // O staging, 2 x 8 KB
-constexpr int OFF2_MBAR = OFF2_O + 2 * 8192; // two mbarriers
+constexpr int OFF2_O = 0;                   // O staging, 2 x 8 KB (TMA stores, 1024-byte aligned)
+constexpr int OFF2_REC = 2 * 8192;          // 2 x HO_SIZE, swizzled tiles
+constexpr int OFF2_MBAR = OFF2_REC + 2 * HO_SIZE; // two mbarriers
 constexpr int SMEM2 = OFF2_MBAR + 16;
 
-__global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p) {
+__global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  const int T = p.T, H = p.H, nc = p.nc;
+  const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
   const int g4 = lane >> 2, c4 = lane & 3;
-  const int64_t row_stride = (int64_t)H * D;
-  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
   const int jb = warp * 16;
+  if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
+    if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
+    return;
+  }
 
   const uint32_t mbar = s_base + OFF2_MBAR;
   if (tid == 0) {
@@ -531,14 +537,15 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p) {
       S[nt][2 * hh] = v.x;
       S[nt][2 * hh + 1] = v.y;
     }
-  __nv_bfloat16 *og = (__nv_bfloat16 *)p.o;
   issue(0);
   for (int c = 0; c < nc; ++c) {
     const int buf = c & 1;
     const uint32_t ho = s_base + OFF2_REC + buf * HO_SIZE;
     const float *eG = reinterpret_cast<const float *>(sm + OFF2_REC + buf * HO_SIZE + HO_EG);
     const uint32_t ost = s_base + OFF2_O + buf * 8192;
-    // chunk c's record landed (bounded wait); the barrier also marks chunk c-1 consumed
+    // chunk c's record landed (bounded wait); the barrier also marks chunk c-1 consumed and
+    // (thread 0 waits for it) the TMA store of chunk c-2's O, which used this O buffer
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
     if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (c >> 1) & 1))) {
       if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
       break;
@@ -628,16 +635,14 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p) {
         mma16816(S[2 * nd], ua[kk], bf[0], bf[1]);
         mma16816(S[2 * nd + 1], ua[kk], bf[2], bf[3]);
       }
-    __syncthreads();                 // O staging complete
-    const int t0 = c * C;
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int u = tid + it * NT2, r = u >> 3, ch = u & 7, t = t0 + r;
-      if (t < T)
-        *reinterpret_cast<uint4 *>(og + base_bh + (int64_t)t * row_stride + ch * 8) =
-            *reinterpret_cast<const uint4 *>(sm + OFF2_O + buf * 8192 + sw64(r, ch * 8));
+    fence_proxy_async_smem();
+    __syncthreads();                 // O staging complete: one TMA store (rows past T dropped)
+    if (tid == 0) {
+      tma_store_rows(&tm.m[0], ost, h, c * C, b);
+      bulk_commit();
     }
   }
+  if (tid == 0) bulk_wait_all();
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -655,11 +660,17 @@ int launch(const Params &p, cudaStream_t st) {
       cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return KDA_ERR_CUDA;
   const int nchunks = p.B * p.H * p.nc;
-  k1<<<nchunks < nsm ? nchunks : nsm, NT1, SMEM1, st>>>(p);
+  TmaMaps tm;
+  const void *srcs[4] = {p.q, p.k, p.v, p.g};
+  for (int i = 0; i < 4; ++i)
+    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3)) return e;
+  k1<<<nchunks < nsm ? nchunks : nsm, NT1, SMEM1, st>>>(p, tm);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
     return KDA_ERR_CUDA;
-  kda_fwd_scan_kernel<<<p.B * p.H, NT2, SMEM2, st>>>(p);
+  TmaMaps to;
+  if (int e = tma_map_bthd(&to.m[0], p.o, p.B, p.T, p.H, D, false)) return e;
+  kda_fwd_scan_kernel<<<p.B * p.H, NT2, SMEM2, st>>>(p, to);
   count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
