@@ -27,6 +27,7 @@
 
 #include "kda_common.cuh"
 #include "kda_mma.cuh"
+#include "kda_tma.cuh"
 
 namespace kda {
 
@@ -49,21 +50,25 @@ __host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (siz
 // state-cotangent scan
 // ---------------------------------------------------------------------------------------
 constexpr int SC_NT = 128;
-constexpr int SC_DO = 0, SC_MN = 8192, SC_QT = 16384, SC_EG = 24576, SC_BUF = 24576 + 256;
-constexpr int SC_MBAR = 2 * SC_BUF;
+// per buffer: dO tile (TMA, 1024-byte aligned) at SC_DO + buf * 8192; the record span Mneg, Qt,
+// e^{gamma_C} at SC_RC + buf * SC_RCB
+constexpr int SC_DO = 0, SC_RC = 16384, SC_RCB = 16384 + 256;
+constexpr int SC_MN = 0, SC_QT = 8192, SC_EG = 16384;
+constexpr int SC_MBAR = SC_RC + 2 * SC_RCB;
 constexpr int SC_SMEM = SC_MBAR + 16;
 
-__global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) {
+__global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3, jb = warp * 16;
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  const int T = p.T, H = p.H, nc = p.nc;
+  const int H = p.H, nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
-  const int64_t row_stride = (int64_t)H * D;
-  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
-  const __nv_bfloat16 *dOg = (const __nv_bfloat16 *)p.dO;
   __nv_bfloat16 *ds_exit = (__nv_bfloat16 *)p.ws;
+  if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
+    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_MISALIGNED);
+    return;
+  }
   if (bh == 0 && tid == 0)  // the chunk kernel that follows appends flagged chunks to a fresh list
     *reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc)) = 0;
 
@@ -74,21 +79,15 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
     mbar_fence_init();
   }
   __syncthreads();
-  // dO rows (strided in [B, T, H, D]) by cp.async; Mneg, Qt, e^{gamma_C} (one contiguous,
-  // already swizzled span of the saved record) by one bulk copy
+  // dO tile by TMA; Mneg, Qt, e^{gamma_C} (one contiguous, already swizzled span of the saved
+  // record) by one bulk copy; both complete on the buffer's mbarrier
   auto issue = [&](int c, int buf) {
-    const uint32_t base = s_base + buf * SC_BUF;
     const uint8_t *rec = (const uint8_t *)p.saved_in + ((int64_t)bh * nc + c) * kSavedChunk;
     if (tid == 0) {
-      mbar_expect_tx(mbar + buf * 8, kSavedChunk - kSavedM);
-      bulk_g2s(base + SC_MN, rec + kSavedM, kSavedChunk - kSavedM, mbar + buf * 8);
+      mbar_expect_tx(mbar + buf * 8, 8192 + kSavedChunk - kSavedM);
+      tma_load_rows(s_base + SC_DO + buf * 8192, &tm.m[0], h, c * C, b, mbar + buf * 8);
+      bulk_g2s(s_base + SC_RC + buf * SC_RCB, rec + kSavedM, kSavedChunk - kSavedM, mbar + buf * 8);
     }
-    for (int u = tid; u < 512; u += SC_NT) {
-      const int r = u >> 3, ch = u & 7, t = c * C + r;
-      const bool in = t < T;
-      cp_async16(base + SC_DO + sw64(r, ch * 8), dOg + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
-    }
-    cp_async_commit();
   };
 
   float dS[8][4];
@@ -105,14 +104,13 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
   issue(nc - 1, 0);
   for (int i = 0; i < nc; ++i) {
     const int c = nc - 1 - i, buf = i & 1;
-    cp_async_wait_all();
     if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (i >> 1) & 1))) {
       if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
       return;
     }
     if (i + 1 < nc) issue(c - 1, buf ^ 1);
-    const uint32_t base = s_base + buf * SC_BUF;
-    const float *eG = reinterpret_cast<const float *>(sm + buf * SC_BUF + SC_EG);
+    const uint32_t base = s_base + SC_RC + buf * SC_RCB, dob = s_base + SC_DO + buf * 8192;
+    const float *eG = reinterpret_cast<const float *>(sm + SC_RC + buf * SC_RCB + SC_EG);
     uint32_t da[4][4];
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -137,7 +135,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p) 
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t ao[4];
-      ldsm_x4_t(ct_frag_addr(base + SC_DO, 16 * kk, jb, lane), ao);  // dO^T rows j, k = t
+      ldsm_x4_t(ct_frag_addr(dob, 16 * kk, jb, lane), ao);  // dO^T rows j, k = t
 #pragma unroll
       for (int nd = 0; nd < 4; ++nd) {
         uint32_t bm[4], bq[4];
@@ -174,11 +172,11 @@ constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
 constexpr int O_VEC = 155648;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
               V_EG = 2368, V_DB = 2432, V_DGM = 2496, V_FLAG = 2560;
-constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;
-constexpr int CK_SMEM = O_MBAR + 8;
+constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // two mbarriers
+constexpr int CK_SMEM = O_MBAR + 16;
 
 template <typename Tb>
-__global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
+__global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
@@ -197,44 +195,37 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
   const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
 
-  // ---- P0: loads in two groups: q, k, g first (for P1-P2), the rest lands behind P1-P2 ----
-  {
-    const __nv_bfloat16 *src[4] = {(const __nv_bfloat16 *)p.q, (const __nv_bfloat16 *)p.k,
-                                   (const __nv_bfloat16 *)p.v, (const __nv_bfloat16 *)p.dO};
-    for (int u = tid; u < 2 * 512; u += CK_NT) {
-      const int which = u >> 9, r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
-      const bool in = t < T;
-      cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
-                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
-    }
-    for (int u = tid; u < 1024; u += CK_NT) {
-      const int r = u >> 4, ch = u & 15, t = t0 + r;
-      const bool in = t < T;
-      cp_async16(s_base + O_GS + r * 256 + ch * 16, p.g + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 4, in ? 16 : 0);
-    }
-    cp_async_commit();
-    for (int u = tid; u < 2 * 512; u += CK_NT) {
-      const int which = 2 + (u >> 9), r = (u >> 3) & 63, ch = u & 7, t = t0 + r;
-      const bool in = t < T;
-      cp_async16(s_base + which * 8192 + sw64(r, ch * 8),
-                 src[which] + base_bh + (int64_t)(in ? t : 0) * row_stride + ch * 8, in ? 16 : 0);
-    }
-    if (tid == 0) {  // S0, Unew^T, P, M, Tinv (adjacent in the saved record) and dS1, swizzled
-      const uint32_t mbar = s_base + O_MBAR;
-      mbar_init(mbar, 1);
-      mbar_fence_init();
-      mbar_expect_tx(mbar, 6 * 8192);
-      bulk_g2s(s_base + O_S0, rec + kSavedS0, 5 * 8192, mbar);
-      bulk_g2s(s_base + O_DS, ds_exit, 8192, mbar);
-    }
-    cp_async_commit();
-    if (tid < C) {
-      bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
-      dbacc[tid] = 0.f;
-      dgacc[tid] = 0.f;
-    }
-    cp_async_wait_group<1>();
-    __syncthreads();
+  // ---- P0: loads in two groups on two mbarriers: q, k, g (TMA) for P1-P2; v, dO (TMA), the
+  //      saved record's S0, Unew^T, P, M, Tinv and dS1 (bulk copies) land behind P1-P2 ----
+  const uint32_t mbar = s_base + O_MBAR;
+  if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
+    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_MISALIGNED);
+    return;
+  }
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_init(mbar + 8, 1);
+    mbar_fence_init();
+    mbar_expect_tx(mbar, 2 * 8192 + 16384);
+    tma_load_rows(s_base + O_QS, &tm.m[0], h, t0, b, mbar);
+    tma_load_rows(s_base + O_KS, &tm.m[1], h, t0, b, mbar);
+    tma_load_rows(s_base + O_GS, &tm.m[4], h, t0, b, mbar);
+    mbar_expect_tx(mbar + 8, 2 * 8192 + 6 * 8192);
+    tma_load_rows(s_base + O_VS, &tm.m[2], h, t0, b, mbar + 8);
+    tma_load_rows(s_base + O_DO, &tm.m[3], h, t0, b, mbar + 8);
+    bulk_g2s(s_base + O_S0, rec + kSavedS0, 5 * 8192, mbar + 8);
+    bulk_g2s(s_base + O_DS, ds_exit, 8192, mbar + 8);
+  }
+  if (tid < C) {
+    bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
+    dbacc[tid] = 0.f;
+    dgacc[tid] = 0.f;
+  }
+  __syncthreads();  // the mbarriers are initialised
+  if (__syncthreads_or(!mbar_wait(mbar, 0))) {
+    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+    mbar_wait(mbar + 8, 0);
+    return;
   }
   // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
   {
@@ -266,8 +257,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   const int big = __syncthreads_or(bigloc);
   if (big) {  // redone exactly by the flagged-chunk kernel
     if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
-    cp_async_wait_group<0>();  // leave no copy in flight into this CTA's shared memory
-    mbar_wait(s_base + O_MBAR, 0);
+    mbar_wait(mbar + 8, 0);  // leave no copy in flight into this CTA's shared memory
     return;
   }
   if (tid < 64) {
@@ -318,8 +308,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
   }
 
   // ---- the second load group (v, dO, S0, Unew^T, P, M, Tinv, dS1) ----
-  cp_async_wait_group<0>();
-  if (__syncthreads_or(!mbar_wait(s_base + O_MBAR, 0))) {
+  if (__syncthreads_or(!mbar_wait(mbar + 8, 0))) {
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
     return;
   }
@@ -566,8 +555,15 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
       *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, d)) =
           pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
     }
+  fence_proxy_async_smem();
   __syncthreads();
-  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up): 8 segments of 8 rows
+  if (tid == 0) {  // dq, dk: TMA stores of the staged tiles (rows past T are dropped)
+    tma_store_rows(&tm.m[5], s_base + O_MK, h, t0, b);
+    tma_store_rows(&tm.m[6], s_base + O_PB, h, t0, b);
+    bulk_commit();
+  }
+  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up), in place in GS:
+     // 8 segments of 8 rows
     const int d = tid & 63, seg = tid >> 6;
     float ssum = 0.f;
 #pragma unroll
@@ -580,32 +576,36 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p) {
     for (int r = 7; r >= 0; --r) {
       const int t = seg * 8 + r;
       acc += GS[t * 64 + d];
-      if (t0 + t < T) p.dg[base_bh + (int64_t)(t0 + t) * row_stride + d] = acc;
+      GS[t * 64 + d] = acc;
     }
     if (tid < 64 && t0 + tid < T)
       ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(dbacc[tid]);
   }
-  __nv_bfloat16 *dqg = (__nv_bfloat16 *)p.dq, *dkg = (__nv_bfloat16 *)p.dk;
-  for (int u = tid; u < 512; u += CK_NT) {
-    const int r = u >> 3, ch = u & 7, t = t0 + r;
-    if (t < T) {
-      const int64_t o = base_bh + (int64_t)t * row_stride + ch * 8;
-      *reinterpret_cast<uint4 *>(dqg + o) = *reinterpret_cast<const uint4 *>(sm + O_MK + sw64(r, ch * 8));
-      *reinterpret_cast<uint4 *>(dkg + o) = *reinterpret_cast<const uint4 *>(sm + O_PB + sw64(r, ch * 8));
-    }
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tma_store_rows(&tm.m[7], s_base + O_GS, h, t0, b);
+    bulk_commit();
+    bulk_wait_read_all();  // shared memory stays valid until the stores have read it
   }
 }
 
 template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
+  TmaMaps tm;  // 0 q, 1 k, 2 v, 3 dO, 4 g (loads); 5 dq, 6 dk, 7 dg (stores)
+  const void *base[8] = {p.q, p.k, p.v, p.dO, p.g, p.dq, p.dk, p.dg};
+  for (int i = 0; i < 8; ++i)
+    if (int e = tma_map_bthd(&tm.m[i], base[i], p.B, p.T, p.H, D, i == 4 || i == 7)) return e;
+  TmaMaps tms;
+  tms.m[0] = tm.m[3];
   if (cudaFuncSetAttribute(kda_bwd_state_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM))
     return KDA_ERR_CUDA;
-  kda_bwd_state_scan_kernel<<<p.B * p.H, SC_NT, SC_SMEM, st>>>(p);
+  kda_bwd_state_scan_kernel<<<p.B * p.H, SC_NT, SC_SMEM, st>>>(p, tms);
   count_launch();
   auto kern = kda_bwd_chunks_kernel<Tb>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_SMEM)) return KDA_ERR_CUDA;
   const int n = p.B * p.H * p.nc;
-  kern<<<n, CK_NT, CK_SMEM, st>>>(p);
+  kern<<<n, CK_NT, CK_SMEM, st>>>(p, tm);
   count_launch();
   if (cudaPeekAtLastError() != cudaSuccess) return KDA_ERR_CUDA;
   const int *flags = reinterpret_cast<const int *>((const uint8_t *)p.ws + ws_flags_offset(n));

@@ -13,7 +13,7 @@
 namespace kda {
 
 struct alignas(64) TmaMaps {
-  CUtensorMap m[5];
+  CUtensorMap m[8];
 };
 
 // Encodes the map of a [B, T, H, D] tensor (bf16 or fp32, D = 64) with a box of 64 rows of
