@@ -50,12 +50,14 @@ __host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (siz
 // state-cotangent scan
 // ---------------------------------------------------------------------------------------
 constexpr int SC_NT = 128;
-// per buffer: dO tile (TMA, 1024-byte aligned) at SC_DO + buf * 8192; the record span Mneg, Qt,
-// e^{gamma_C} at SC_RC + buf * SC_RCB
-constexpr int SC_DO = 0, SC_RC = 16384, SC_RCB = 16384 + 256;
+// a ring of SC_NB chunk buffers, loads running two chunks ahead: per slot the dO tile (TMA,
+// 1024-byte aligned) at SC_DO + slot * 8192 and the record span Mneg, Qt, e^{gamma_C} at
+// SC_RC + slot * SC_RCB; the exit-cotangent staging (two 8 KB tiles) at SC_DSX
+constexpr int SC_NB = 3;
+constexpr int SC_DO = 0, SC_DSX = SC_NB * 8192, SC_RC = SC_DSX + 2 * 8192, SC_RCB = 16384 + 256;
 constexpr int SC_MN = 0, SC_QT = 8192, SC_EG = 16384;
-constexpr int SC_MBAR = SC_RC + 2 * SC_RCB;
-constexpr int SC_SMEM = SC_MBAR + 16;
+constexpr int SC_MBAR = SC_RC + SC_NB * SC_RCB;
+constexpr int SC_SMEM = SC_MBAR + 8 * SC_NB;
 
 __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -74,8 +76,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
 
   const uint32_t mbar = s_base + SC_MBAR;
   if (tid == 0) {
-    mbar_init(mbar, 1);
-    mbar_init(mbar + 8, 1);
+    for (int i = 0; i < SC_NB; ++i) mbar_init(mbar + 8 * i, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -87,6 +88,12 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
       mbar_expect_tx(mbar + buf * 8, 8192 + kSavedChunk - kSavedM);
       tma_load_rows(s_base + SC_DO + buf * 8192, &tm.m[0], h, c * C, b, mbar + buf * 8);
       bulk_g2s(s_base + SC_RC + buf * SC_RCB, rec + kSavedM, kSavedChunk - kSavedM, mbar + buf * 8);
+    }
+  };
+  auto store_exit = [&](int i) {  // thread 0: the staged exit cotangent of step i (chunk nc-1-i)
+    if (tid == 0) {
+      bulk_s2g(ds_exit + ((int64_t)bh * nc + nc - 1 - i) * D * D, s_base + SC_DSX + (i & 1) * 8192, 8192);
+      bulk_commit();
     }
   };
 
@@ -102,13 +109,16 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
       dS[nt][2 * hh + 1] = v.y;
     }
   issue(nc - 1, 0);
+  if (nc > 1) issue(nc - 2, 1);
   for (int i = 0; i < nc; ++i) {
-    const int c = nc - 1 - i, buf = i & 1;
-    if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (i >> 1) & 1))) {
+    const int c = nc - 1 - i, buf = i % SC_NB;
+    if (tid == 0) bulk_wait_read_all();  // the exit-cotangent store of step i - 2 has read its staging
+    if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (i / SC_NB) & 1))) {
       if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
       return;
     }
-    if (i + 1 < nc) issue(c - 1, buf ^ 1);
+    if (i + 2 < nc) issue(c - 2, (i + 2) % SC_NB);
+    if (i > 0) store_exit(i - 1);
     const uint32_t base = s_base + SC_RC + buf * SC_RCB, dob = s_base + SC_DO + buf * 8192;
     const float *eG = reinterpret_cast<const float *>(sm + SC_RC + buf * SC_RCB + SC_EG);
     uint32_t da[4][4];
@@ -119,14 +129,14 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
       da[kk][2] = pack_bf16(dS[2 * kk + 1][0], dS[2 * kk + 1][1]);
       da[kk][3] = pack_bf16(dS[2 * kk + 1][2], dS[2 * kk + 1][3]);
     }
-    __nv_bfloat16 *dst = ds_exit + ((int64_t)bh * nc + c) * D * D;
+    {  // stage the exit cotangent (bf16, swizzled) for one bulk store at the next step
+      const uint32_t dsx = s_base + SC_DSX + (i & 1) * 8192;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-      for (int x = 0; x < 4; ++x) {
-        const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
-        *reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(dst) + sw64(row, col)) = da[kk][x];
-      }
+      for (int kk = 0; kk < 4; ++kk)
+        stsm_x4(dsx + sw64(jb + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * kk + (lane >> 4) * 8), da[kk][0],
+                da[kk][1], da[kk][2], da[kk][3]);
+      fence_proxy_async_smem();
+    }
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const float e0 = eG[nt * 8 + 2 * c4], e1 = eG[nt * 8 + 2 * c4 + 1];
@@ -148,6 +158,9 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
       }
     }
   }
+  __syncthreads();
+  store_exit(nc - 1);
+  if (tid == 0) bulk_wait_all();
   if (p.dstate0) {
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)

@@ -5,8 +5,8 @@
 //                  (-W, U, Qd, Kb, P as bf16 tiles, e^{gamma_C}) to the forward workspace,
 //                  and, for training, the state-independent part of the backward's record
 //                  (P, M, Tinv = (I+A)^{-1}, Mneg = -Kb^T W, Qt = Qd - P W).
-//  kda_fwd_scan    one CTA of 4 warps per (b, h): streams the chunk records (double-buffered
-//                  cp.async) and advances the fp32 state, which each warp keeps as 16 rows of
+//  kda_fwd_scan    one CTA of 4 warps per (b, h): streams the chunk records (bulk copies, two
+//                  chunks ahead) and advances the fp32 state, which each warp keeps as 16 rows of
 //                  mma accumulator registers:
 //                    Unew^T = U^T - S W^T;  O^T = S Qd^T + Unew^T P^T;  S <- S diag(e^{gamma_C}) + Unew^T Kb
 //
@@ -493,10 +493,12 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 // kda_fwd_scan
 // ---------------------------------------------------------------------------------------
 constexpr int NT2 = 128;
+constexpr int NREC = 3;                     // record ring: chunk c + 2 loads while c is scanned
 constexpr int OFF2_O = 0;                   // O staging, 2 x 8 KB (TMA stores, 1024-byte aligned)
-constexpr int OFF2_REC = 2 * 8192;          // 2 x HO_SIZE, swizzled tiles
-constexpr int OFF2_MBAR = OFF2_REC + 2 * HO_SIZE; // two mbarriers
-constexpr int SMEM2 = OFF2_MBAR + 16;
+constexpr int OFF2_SV = 2 * 8192;           // S0 | Unew^T staging for the saved record, 2 x 16 KB
+constexpr int OFF2_REC = OFF2_SV + 2 * 16384; // NREC x HO_SIZE, swizzled tiles
+constexpr int OFF2_MBAR = OFF2_REC + NREC * HO_SIZE; // NREC mbarriers
+constexpr int SMEM2 = OFF2_MBAR + 8 * NREC;
 
 __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -513,16 +515,16 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
 
   const uint32_t mbar = s_base + OFF2_MBAR;
   if (tid == 0) {
-    mbar_init(mbar, 1);
-    mbar_init(mbar + 8, 1);
+    for (int i = 0; i < NREC; ++i) mbar_init(mbar + 8 * i, 1);
     mbar_fence_init();
   }
   __syncthreads();
   auto issue = [&](int c) {  // one bulk copy of the chunk's whole record (thread 0)
     if (tid == 0) {
       const uint8_t *rec = (const uint8_t *)p.ws + ((int64_t)bh * nc + c) * HO_SIZE;
-      mbar_expect_tx(mbar + (c & 1) * 8, HO_SIZE);
-      bulk_g2s(s_base + OFF2_REC + (c & 1) * HO_SIZE, rec, HO_SIZE, mbar + (c & 1) * 8);
+      const int r = c % NREC;
+      mbar_expect_tx(mbar + r * 8, HO_SIZE);
+      bulk_g2s(s_base + OFF2_REC + r * HO_SIZE, rec, HO_SIZE, mbar + r * 8);
     }
   };
 
@@ -538,19 +540,20 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       S[nt][2 * hh + 1] = v.y;
     }
   issue(0);
+  if (nc > 1) issue(1);
   for (int c = 0; c < nc; ++c) {
-    const int buf = c & 1;
-    const uint32_t ho = s_base + OFF2_REC + buf * HO_SIZE;
-    const float *eG = reinterpret_cast<const float *>(sm + OFF2_REC + buf * HO_SIZE + HO_EG);
-    const uint32_t ost = s_base + OFF2_O + buf * 8192;
+    const int buf = c & 1, r = c % NREC;
+    const uint32_t ho = s_base + OFF2_REC + r * HO_SIZE;
+    const float *eG = reinterpret_cast<const float *>(sm + OFF2_REC + r * HO_SIZE + HO_EG);
+    const uint32_t ost = s_base + OFF2_O + buf * 8192, svst = s_base + OFF2_SV + buf * 16384;
     // chunk c's record landed (bounded wait); the barrier also marks chunk c-1 consumed and
-    // (thread 0 waits for it) the TMA store of chunk c-2's O, which used this O buffer
+    // (thread 0 waits for it) the stores of chunk c-2, which used this O / S0 staging
     if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
-    if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (c >> 1) & 1))) {
+    if (__syncthreads_or(!mbar_wait(mbar + r * 8, (c / NREC) & 1))) {
       if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
       break;
     }
-    if (c + 1 < nc) issue(c + 1);
+    if (c + 2 < nc) issue(c + 2);
     uint32_t sa[4][4];  // S as bf16 A fragments (rows j, k = d)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -608,17 +611,15 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       stsm_x4_t(ct_frag_addr(ost, 16 * pp, jb, lane), pack_bf16(O[0][0], O[0][1]), pack_bf16(O[0][2], O[0][3]),
                 pack_bf16(O[1][0], O[1][1]), pack_bf16(O[1][2], O[1][3]));
     }
-    // the state-dependent part of the backward's per-chunk record: S0 and Unew^T (bf16)
+    // the state-dependent part of the backward's per-chunk record: S0 and Unew^T (bf16),
+    // staged for one bulk store
     if (p.saved) {
-      uint8_t *sv = (uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const int row = jb + g4 + (x & 1) * 8, col = 16 * kk + (x >> 1) * 8 + 2 * c4;
-          *reinterpret_cast<uint32_t *>(sv + kSavedS0 + sw64(row, col)) = sa[kk][x];
-          *reinterpret_cast<uint32_t *>(sv + kSavedUnT + sw64(row, col)) = ua[kk][x];
-        }
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t a = sw64(jb + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * kk + (lane >> 4) * 8);
+        stsm_x4(svst + a, sa[kk][0], sa[kk][1], sa[kk][2], sa[kk][3]);
+        stsm_x4(svst + 8192 + a, ua[kk][0], ua[kk][1], ua[kk][2], ua[kk][3]);
+      }
     }
     // S <- S diag(e^gamma_C) + Unew^T Kb
 #pragma unroll
@@ -639,6 +640,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     __syncthreads();                 // O staging complete: one TMA store (rows past T dropped)
     if (tid == 0) {
       tma_store_rows(&tm.m[0], ost, h, c * C, b);
+      if (p.saved) bulk_s2g((uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk + kSavedS0, svst, 16384);
       bulk_commit();
     }
   }
