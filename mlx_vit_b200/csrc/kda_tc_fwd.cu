@@ -19,7 +19,8 @@
 //  2. M = Kdec Kinc^T, P = Qdec Kinc^T per block pair (mma.sync): the decay-weighted K K^T and
 //     Q K^T with both factors of e^{gamma_t - gamma_s} bounded; A = beta M (strict lower)
 //  3. T_ii = (I + A_ii)^{-1} for the four 16x16 diagonal blocks (fp32 substitution)
-//  4. block forward substitution W = (I+A)^{-1} beta Kd, U = (I+A)^{-1} beta V (mma.sync)
+//  4. Tinv = (I+A)^{-1} by block forward substitution (mma.sync), then W = Tinv beta Kd,
+//     U = Tinv beta V as one GEMM
 // This is the chunkwise WY algebra of the reference's chunkwise path (nope_gdn_mlx.py:549-613,
 // 2318-2456) with U = (I+A)^{-1} beta (V - K_proj S^T) split into U - W S^T.
 #include "kda_common.cuh"
@@ -161,21 +162,21 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       tma_load_rows(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
     }
   };
-  auto load_beta = [&](int i) -> float {
+  // beta of the next chunk, kept raw until its use so that the load does not stall anyone
+  auto load_beta = [&](int i) -> Tb {
     const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
-    return t < T ? to_f(betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H]) : 0.f;
+    return t < T ? betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H] : from_f<Tb>(0.f);
   };
   int idx = blockIdx.x;
   if (idx < nchunks) issue_loads(idx);
-  float beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : 0.f;
+  Tb beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : from_f<Tb>(0.f);
 
   for (int it = 0; idx < nchunks; idx += gridDim.x, ++it) {
-  if (tid == 0) bulk_wait_read_all();  // the previous chunk's bulk stores have read smem
   if (__syncthreads_or(!mbar_wait(mbar, it & 1))) {  // this chunk's q, k, v, g
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
     break;
   }
-  if (tid < C) bet[tid] = beta_next;
+  if (tid < C) bet[tid] = to_f(beta_next);
   __syncthreads();
 
   // ---- (1a) gamma = cumsum(g): 8 segments of 8 rows per channel ----
@@ -208,6 +209,8 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
     if (lane == 0) flag[warp] = any;
   }
+  // the previous chunk's bulk stores have read the record and staging tiles written from here on
+  if (tid == 0) bulk_wait_read_all();
   __syncthreads();
   const bool big = flag[0] | flag[1];
   if (tid < 64) {
@@ -393,16 +396,39 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   }
   __syncthreads();
 
-  // ---- (4) W = (I+A)^{-1} beta Kd (stored negated), U = (I+A)^{-1} beta V; 8 columns per
-  //      warp, each warp's substitution independent of the others.  For training, warps 8-15
-  //      then also solve for the 8 columns (warp - 8) * 8.. of Tinv = (I+A)^{-1} itself, which
-  //      the backward applies as one GEMM instead of a second triangular solve. ----
-  if (warp < 8)
-    solve_columns(sm, s_base, HO_W, OFF_XK, (warp & 7) * 8, 0, 1.f, -1.f, warp, lane);
-  else
-    solve_columns(sm, s_base, HO_U, OFF_XV, (warp & 7) * 8, 0, -1.f, 1.f, warp, lane);
-  if (p.saved && warp >= 8)
-    solve_columns(sm, s_base, OFF_TF - OFF_OUT, -1, (warp & 7) * 8, (warp & 7) >> 1, -1.f, 1.f, warp, lane);
+  // ---- (4) Tinv = (I+A)^{-1}: block forward substitution on the identity, 8 columns per warp
+  //      (warps 0-7; the rows above a column's diagonal block are zero and skipped) ----
+  if (warp < 8) solve_columns(sm, s_base, OFF_TF - OFF_OUT, -1, warp * 8, warp >> 1, -1.f, 1.f, warp, lane);
+  __syncthreads();
+  // ---- (5) W = Tinv beta Kd (stored negated) and U = Tinv beta V as one block-triangular GEMM;
+  //      warp (row block i, 32 of the 128 columns of [W | U]) ----
+  {
+    const int i = warp >> 2, q = warp & 3, c0 = 32 * (q & 1);
+    const bool isW = q < 2;
+    const uint32_t xb = s_base + (isW ? OFF_XK : OFF_XV);
+    float acc[4][4] = {};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (k > i) break;
+      uint32_t af[4];
+      ldsm_x4(a_frag_addr(s_base + OFF_TF, 16 * i, 16 * k, lane), af);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_t(bkn_frag_addr(xb, 16 * k, c0 + 16 * np, lane), bf);
+        mma16816(acc[2 * np], af, bf[0], bf[1]);
+        mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+      }
+    }
+    const float so = isW ? -1.f : 1.f;
+    uint8_t *Ym = hom + (isW ? HO_W : HO_U);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        *reinterpret_cast<uint32_t *>(Ym + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
+            pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
+  }
 
   fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
@@ -416,66 +442,60 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     }
     bulk_commit();
   }
-  // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-3,
-  //      rows d' in [jb, jb+16)), Qt = Qd + P (-W) (warps 4-7, rows t in [jb, jb+16)) ----
+  // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-7) and
+  //      Qt = Qd + P (-W) (warps 8-15), each warp 16 rows x 32 columns ----
   if (p.saved) {
     uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
-    const int jb = (warp & 3) * 16;
-    if (warp < 4) {  // warps 8..15 have no part in this step
-    {  // Mneg = Kb^T (-W), rows d' in [jb, jb+16)
-      float M[8][4] = {};
+    const int rb = (warp >> 1) & 3, jb = rb * 16, nh = warp & 1;
+    float X[4][4];
+    if (warp < 8) {  // Mneg rows d' in [jb, jb+16)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) X[nt][e] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t af[4];
         ldsm_x4_t(ct_frag_addr(ho + HO_KB, 16 * kk, jb, lane), af);
 #pragma unroll
-        for (int nd = 0; nd < 4; ++nd) {
+        for (int np = 0; np < 2; ++np) {
           uint32_t bf[4];
-          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
-          mma16816(M[2 * nd], af, bf[0], bf[1]);
-          mma16816(M[2 * nd + 1], af, bf[2], bf[3]);
+          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 32 * nh + 16 * np, lane), bf);
+          mma16816(X[2 * np], af, bf[0], bf[1]);
+          mma16816(X[2 * np + 1], af, bf[2], bf[3]);
         }
       }
+    } else {  // Qt rows t in [jb, jb+16)
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(sm + OFF_XK + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
-              pack_bf16(M[nt][2 * hh], M[nt][2 * hh + 1]);
-    }
-    } else if (warp < 8) {
-    {  // Qt rows t in [jb, jb+16): Qd + P (-W)
-      float Q[8][4];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const float2 v = unpack_bf16(*reinterpret_cast<const uint32_t *>(
-              hom + HO_QD + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)));
-          Q[nt][2 * hh] = v.x;
-          Q[nt][2 * hh + 1] = v.y;
+              hom + HO_QD + sw64(jb + g4 + 8 * hh, 32 * nh + nt * 8 + 2 * c4)));
+          X[nt][2 * hh] = v.x;
+          X[nt][2 * hh + 1] = v.y;
         }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        if (kk > (warp & 3)) break;
+        if (kk > rb) break;
         uint32_t af[4];
         ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);
 #pragma unroll
-        for (int nd = 0; nd < 4; ++nd) {
+        for (int np = 0; np < 2; ++np) {
           uint32_t bf[4];
-          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 16 * nd, lane), bf);
-          mma16816(Q[2 * nd], af, bf[0], bf[1]);
-          mma16816(Q[2 * nd + 1], af, bf[2], bf[3]);
+          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 32 * nh + 16 * np, lane), bf);
+          mma16816(X[2 * np], af, bf[0], bf[1]);
+          mma16816(X[2 * np + 1], af, bf[2], bf[3]);
         }
       }
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(sm + OFF_XV + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
-              pack_bf16(Q[nt][2 * hh], Q[nt][2 * hh + 1]);
     }
-    }
+    uint8_t *dst = sm + (warp < 8 ? OFF_XK : OFF_XV);  // staged in the free beta-Kd / beta-V tiles
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        *reinterpret_cast<uint32_t *>(dst + sw64(jb + g4 + 8 * hh, 32 * nh + nt * 8 + 2 * c4)) =
+            pack_bf16(X[nt][2 * hh], X[nt][2 * hh + 1]);
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {  // Mneg, Qt (staged in the free beta-Kd / beta-V tiles) and e^{gamma_C}
