@@ -185,8 +185,8 @@ constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
 constexpr int O_VEC = 155648;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
               V_EG = 2368, V_DB = 2432, V_DGM = 2496, V_FLAG = 2560;
-constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // two mbarriers
-constexpr int CK_SMEM = O_MBAR + 16;
+constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // three mbarriers
+constexpr int CK_SMEM = O_MBAR + 24;
 
 template <typename Tb>
 __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
@@ -194,52 +194,81 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
   const int mt = warp >> 2, nq = warp & 3, n0 = 16 * nq;
-  const int nc = p.nc, idx = blockIdx.x, bh = idx / nc, c = idx % nc;
-  const int b = bh / p.H, h = bh % p.H, T = p.T, H = p.H, t0 = c * C;
+  const int nc = p.nc, T = p.T, H = p.H, nchunks = p.B * p.H * nc;
   const uint32_t s_base = smem_u32(sm);
   const int64_t row_stride = (int64_t)H * D;
-  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
   float *GS = reinterpret_cast<float *>(sm + O_GS);
   float *vec = reinterpret_cast<float *>(sm + O_VEC);
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
   float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *dbacc = vec + V_DB, *dgacc = vec + V_DGM;
   const Tb *betag = (const Tb *)p.beta;
-  int *flagged = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc));
-  const __nv_bfloat16 *ds_exit = (const __nv_bfloat16 *)p.ws + (int64_t)idx * D * D;
-  const uint8_t *rec = (const uint8_t *)p.saved_in + (int64_t)idx * kSavedChunk;
+  int *flagged = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset(nchunks));
 
-  // ---- P0: loads in two groups on two mbarriers: q, k, g (TMA) for P1-P2; v, dO (TMA), the
-  //      saved record's S0, Unew^T, P, M, Tinv and dS1 (bulk copies) land behind P1-P2 ----
+  // The CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...  The next
+  // chunk's inputs are loaded in three stages, each issued (by one thread: TMA tiles of
+  // q/k/v/dO/g, bulk copies of the saved record and dS1) as soon as the tiles it fills are dead:
+  //   0 (after P5): v, P, Tinv;  1 (after P7): dO, g, S0, Unew^T, M, dS1;  2 (after P8): q, k.
+  // Each stage completes on its own mbarrier.  The outputs dq, dk, dg leave by TMA stores
+  // from tiles that no load touches.
   const uint32_t mbar = s_base + O_MBAR;
   if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_MISALIGNED);
     return;
   }
+  auto issue_loads = [&](int i, int stage) {
+    if (tid != 0) return;
+    const int bh_ = i / nc, t0_ = (i % nc) * C, b_ = bh_ / H, h_ = bh_ % H;
+    const uint8_t *rec_ = (const uint8_t *)p.saved_in + (int64_t)i * kSavedChunk;
+    const uint32_t mb = mbar + 8 * stage;
+    if (stage == 0) {
+      mbar_expect_tx(mb, 3 * 8192);
+      tma_load_rows(s_base + O_VS, &tm.m[2], h_, t0_, b_, mb);
+      bulk_g2s(s_base + O_PB, rec_ + kSavedP, 8192, mb);
+      bulk_g2s(s_base + O_TF, rec_ + kSavedTinv, 8192, mb);
+    } else if (stage == 1) {
+      mbar_expect_tx(mb, 5 * 8192 + 16384);
+      tma_load_rows(s_base + O_DO, &tm.m[3], h_, t0_, b_, mb);
+      tma_load_rows(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
+      bulk_g2s(s_base + O_S0, rec_ + kSavedS0, 2 * 8192, mb);
+      bulk_g2s(s_base + O_MK, rec_ + kSavedMkk, 8192, mb);
+      bulk_g2s(s_base + O_DS, (const __nv_bfloat16 *)p.ws + (int64_t)i * D * D, 8192, mb);
+    } else {
+      mbar_expect_tx(mb, 2 * 8192);
+      tma_load_rows(s_base + O_QS, &tm.m[0], h_, t0_, b_, mb);
+      tma_load_rows(s_base + O_KS, &tm.m[1], h_, t0_, b_, mb);
+    }
+  };
+  // beta of the next chunk, kept raw until its use so that the load does not stall anyone
+  auto load_beta = [&](int i) -> Tb {
+    const int bh_ = i / nc, t = (i % nc) * C + tid;
+    return t < T ? betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H] : from_f<Tb>(0.f);
+  };
   if (tid == 0) {
-    mbar_init(mbar, 1);
-    mbar_init(mbar + 8, 1);
+    for (int i = 0; i < 3; ++i) mbar_init(mbar + 8 * i, 1);
     mbar_fence_init();
-    mbar_expect_tx(mbar, 2 * 8192 + 16384);
-    tma_load_rows(s_base + O_QS, &tm.m[0], h, t0, b, mbar);
-    tma_load_rows(s_base + O_KS, &tm.m[1], h, t0, b, mbar);
-    tma_load_rows(s_base + O_GS, &tm.m[4], h, t0, b, mbar);
-    mbar_expect_tx(mbar + 8, 2 * 8192 + 6 * 8192);
-    tma_load_rows(s_base + O_VS, &tm.m[2], h, t0, b, mbar + 8);
-    tma_load_rows(s_base + O_DO, &tm.m[3], h, t0, b, mbar + 8);
-    bulk_g2s(s_base + O_S0, rec + kSavedS0, 5 * 8192, mbar + 8);
-    bulk_g2s(s_base + O_DS, ds_exit, 8192, mbar + 8);
+  }
+  __syncthreads();
+  int idx = blockIdx.x;
+  if (idx < nchunks)
+    for (int stage = 0; stage < 3; ++stage) issue_loads(idx, stage);
+  Tb beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : from_f<Tb>(0.f);
+
+  for (int it = 0; idx < nchunks; idx += gridDim.x, ++it) {
+  const int bh = idx / nc, c = idx % nc, b = bh / H, h = bh % H, t0 = c * C;
+  const int64_t base_bh = ((int64_t)b * T * H + h) * D;
+  const int inext = idx + gridDim.x;
+  // ---- P0: this chunk's inputs (bounded waits) ----
+  if (__syncthreads_or(!mbar_wait(mbar, it & 1) || !mbar_wait(mbar + 8, it & 1) ||
+                       !mbar_wait(mbar + 16, it & 1))) {
+    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+    break;
   }
   if (tid < C) {
-    bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
+    bet[tid] = to_f(beta_next);
     dbacc[tid] = 0.f;
     dgacc[tid] = 0.f;
   }
-  __syncthreads();  // the mbarriers are initialised
-  if (__syncthreads_or(!mbar_wait(mbar, 0))) {
-    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
-    mbar_wait(mbar + 8, 0);
-    return;
-  }
+  if (inext < nchunks && tid < C) beta_next = load_beta(inext);
   // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
   {
     const int d = tid & 63, seg = tid >> 6;
@@ -270,8 +299,9 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   const int big = __syncthreads_or(bigloc);
   if (big) {  // redone exactly by the flagged-chunk kernel
     if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
-    mbar_wait(mbar + 8, 0);  // leave no copy in flight into this CTA's shared memory
-    return;
+    if (inext < nchunks)
+      for (int stage = 0; stage < 3; ++stage) issue_loads(inext, stage);
+    continue;
   }
   if (tid < 64) {
     const int d = tid;
@@ -289,6 +319,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
     eG[d] = __expf(gC);
   }
+  if (tid == 0) bulk_wait_read_all();  // the previous chunk's output stores have read KD, QD, KF
   __syncthreads();
 
   // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma} ----
@@ -320,11 +351,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
   }
 
-  // ---- the second load group (v, dO, S0, Unew^T, P, M, Tinv, dS1) ----
-  if (__syncthreads_or(!mbar_wait(mbar + 8, 0))) {
-    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
-    return;
-  }
+  __syncthreads();
   // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
   {
     const int d = tid & 63, jq = tid >> 6;
@@ -396,6 +423,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
   }
   __syncthreads();
+  if (inext < nchunks) issue_loads(inext, 0);  // v, P and Tinv are dead from here on
 
   // ---- P6..P8: per warp rows 16 * mt.. and columns n0.. of dq, dk ----
   float DQ[2][4], DKp[2][4], DKm[2][4], Fv[2][4];
@@ -498,6 +526,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
   }
   __syncthreads();
+  if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
   // ---- P8: decayed products ----
   {
     float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {};
@@ -552,35 +581,45 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       }
   }
   // ---- P9: dgamma, dg = reverse cumsum, outputs ----
-  __syncthreads();  // every warp is done reading gamma, MK and PB
+  // ---- P9: dgamma = q dq + k (dk_row - dk_col) in registers while q, k are still resident ----
+  float dgm[2][4];
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
-      const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4;
+      const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4, e = 2 * hh;
       const float2 qv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t, d)));
       const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
-      const int e = 2 * hh;
-      *reinterpret_cast<float2 *>(GS + t * 64 + d) =
-          make_float2(qv.x * DQ[nt][e] + kv.x * (DKp[nt][e] - DKm[nt][e]),
-                      qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]));
-      *reinterpret_cast<uint32_t *>(sm + O_MK + sw64(t, d)) = pack_bf16(DQ[nt][e], DQ[nt][e + 1]);
-      *reinterpret_cast<uint32_t *>(sm + O_PB + sw64(t, d)) =
+      dgm[nt][e] = qv.x * DQ[nt][e] + kv.x * (DKp[nt][e] - DKm[nt][e]);
+      dgm[nt][e + 1] = qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]);
+    }
+  __syncthreads();  // every warp is done with q, k and the P8 operand tiles
+  if (inext < nchunks) issue_loads(inext, 2);
+  // staging: dq (bf16) in KD, dk (bf16) in QD, dgamma (fp32 [t][d]) over KF and KB
+  float *DG = reinterpret_cast<float *>(sm + O_KF);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4, e = 2 * hh;
+      *reinterpret_cast<float2 *>(DG + t * 64 + d) = make_float2(dgm[nt][e], dgm[nt][e + 1]);
+      *reinterpret_cast<uint32_t *>(sm + O_KD + sw64(t, d)) = pack_bf16(DQ[nt][e], DQ[nt][e + 1]);
+      *reinterpret_cast<uint32_t *>(sm + O_QD + sw64(t, d)) =
           pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
     }
   fence_proxy_async_smem();
   __syncthreads();
   if (tid == 0) {  // dq, dk: TMA stores of the staged tiles (rows past T are dropped)
-    tma_store_rows(&tm.m[5], s_base + O_MK, h, t0, b);
-    tma_store_rows(&tm.m[6], s_base + O_PB, h, t0, b);
+    tma_store_rows(&tm.m[5], s_base + O_KD, h, t0, b);
+    tma_store_rows(&tm.m[6], s_base + O_QD, h, t0, b);
     bulk_commit();
   }
-  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up), in place in GS:
+  {  // dg = reverse cumsum of dgamma (+ dGamma_C from the last row up), in place:
      // 8 segments of 8 rows
     const int d = tid & 63, seg = tid >> 6;
     float ssum = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) ssum += GS[(seg * 8 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) ssum += DG[(seg * 8 + r) * 64 + d];
     part[seg * 64 + d] = ssum;
     __syncthreads();
     float acc = dgacc[d];
@@ -588,8 +627,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
     for (int r = 7; r >= 0; --r) {
       const int t = seg * 8 + r;
-      acc += GS[t * 64 + d];
-      GS[t * 64 + d] = acc;
+      acc += DG[t * 64 + d];
+      DG[t * 64 + d] = acc;
     }
     if (tid < 64 && t0 + tid < T)
       ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(dbacc[tid]);
@@ -597,10 +636,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   fence_proxy_async_smem();
   __syncthreads();
   if (tid == 0) {
-    tma_store_rows(&tm.m[7], s_base + O_GS, h, t0, b);
+    tma_store_rows(&tm.m[7], s_base + O_KF, h, t0, b);
     bulk_commit();
-    bulk_wait_read_all();  // shared memory stays valid until the stores have read it
   }
+  }  // chunk loop
+  if (tid == 0) bulk_wait_all();  // shared memory stays valid until the stores have read it
 }
 
 template <typename Tb>
@@ -618,7 +658,11 @@ int launch(const Params &p, cudaStream_t st) {
   auto kern = kda_bwd_chunks_kernel<Tb>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_SMEM)) return KDA_ERR_CUDA;
   const int n = p.B * p.H * p.nc;
-  kern<<<n, CK_NT, CK_SMEM, st>>>(p, tm);
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return KDA_ERR_CUDA;
+  kern<<<n < nsm ? n : nsm, CK_NT, CK_SMEM, st>>>(p, tm);
   count_launch();
   if (cudaPeekAtLastError() != cudaSuccess) return KDA_ERR_CUDA;
   const int *flags = reinterpret_cast<const int *>((const uint8_t *)p.ws + ws_flags_offset(n));
