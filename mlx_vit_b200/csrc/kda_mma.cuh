@@ -19,6 +19,13 @@ __device__ __forceinline__ uint32_t sw64(int row, int col) {
   return (uint32_t)(row * 128 + ((((col >> 3) ^ row) & 7) << 4) + ((col & 7) << 1));
 }
 
+// float index of element (row t, column d) of a 64 x 64 fp32 tile kept as two 64 x 32 halves,
+// each with the 128-byte swizzle (two TMA boxes of 32 columns): 8 consecutive rows of one
+// column pair fall in 8 different bank groups
+__device__ __forceinline__ int gsw(int t, int d) {
+  return ((d >> 5) << 11) + t * 32 + ((((d >> 2) & 7) ^ (t & 7)) << 2) + (d & 3);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&v);

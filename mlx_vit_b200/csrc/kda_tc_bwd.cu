@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     } else if (stage == 1) {
       mbar_expect_tx(mb, 5 * 8192 + 16384);
       tma_load_rows(s_base + O_DO, &tm.m[3], h_, t0_, b_, mb);
-      tma_load_rows(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
+      tma_load_rows_f32(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
       bulk_g2s(s_base + O_S0, rec_ + kSavedS0, 2 * 8192, mb);
       bulk_g2s(s_base + O_MK, rec_ + kSavedMkk, 8192, mb);
       bulk_g2s(s_base + O_DS, (const __nv_bfloat16 *)p.ws + (int64_t)i * D * D, 8192, mb);
@@ -274,15 +274,15 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     const int d = tid & 63, seg = tid >> 6;
     float acc = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc += GS[(seg * 8 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) acc += GS[gsw(seg * 8 + r, d)];
     part[seg * 64 + d] = acc;
     __syncthreads();
     float off = 0.f;
     for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      off += GS[(seg * 8 + r) * 64 + d];
-      GS[(seg * 8 + r) * 64 + d] = off;
+      off += GS[gsw(seg * 8 + r, d)];
+      GS[gsw(seg * 8 + r, d)] = off;
     }
     __syncthreads();
   }
@@ -291,8 +291,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     float span = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      span = fmaxf(span, GS[(i * 16) * 64 + tid] - GS[(i * 16 + 8) * 64 + tid]);
-      span = fmaxf(span, GS[(i * 16 + 8) * 64 + tid] - GS[(i * 16 + 15) * 64 + tid]);
+      span = fmaxf(span, GS[gsw(i * 16, tid)] - GS[gsw(i * 16 + 8, tid)]);
+      span = fmaxf(span, GS[gsw(i * 16 + 8, tid)] - GS[gsw(i * 16 + 15, tid)]);
     }
     bigloc = !(span <= kSpanMax);
   }
@@ -305,10 +305,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   if (tid < 64) {
     const int d = tid;
-    const float gC = GS[63 * 64 + d];
+    const float gC = GS[gsw(63, d)];
     float r[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = GS[(i * 16 + 8) * 64 + d];
+    for (int i = 0; i < 4; ++i) r[i] = GS[gsw(i * 16 + 8, d)];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       refs[i * 64 + d] = r[i];
@@ -334,11 +334,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     for (int e = 0; e < 4; ++e) {
       const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
       const int d = d0 + 2 * e;
-      const float2 gm = *reinterpret_cast<const float2 *>(GS + t * 64 + d);
+      const float2 gm = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
       const float2 rf = *reinterpret_cast<const float2 *>(refs + blk * 64 + d);
       const float2 er = *reinterpret_cast<const float2 *>(egr + blk * 64 + d);
       const float F0 = __expf(gm.x - rf.x), F1 = __expf(gm.y - rf.y);
-      *reinterpret_cast<float2 *>(GS + t * 64 + d) = make_float2(F0, F1);  // GS holds F = e^{gamma - r_b(t)}
+      *reinterpret_cast<float2 *>(GS + gsw(t, d)) = make_float2(F0, F1);  // GS holds F = e^{gamma - r_b(t)}
       const float i0 = __fdividef(1.f, F0), i1 = __fdividef(1.f, F1);
       okd[e] = pack_bf16(kf.x * F0, kf.y * F1);
       oqd[e] = pack_bf16(qf.x * F0, qf.y * F1);
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int t = 16 * mt + g4 + 8 * hh;
-        const float2 F = *reinterpret_cast<const float2 *>(GS + t * 64 + d);
+        const float2 F = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
         const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
         const float nb = -bet[t];
 #pragma unroll
@@ -595,14 +595,14 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
   __syncthreads();  // every warp is done with q, k and the P8 operand tiles
   if (inext < nchunks) issue_loads(inext, 2);
-  // staging: dq (bf16) in KD, dk (bf16) in QD, dgamma (fp32 [t][d]) over KF and KB
+  // staging: dq (bf16) in KD, dk (bf16) in QD, dgamma (fp32, gsw layout) over KF and KB
   float *DG = reinterpret_cast<float *>(sm + O_KF);
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int t = 16 * mt + g4 + 8 * hh, d = n0 + 8 * nt + 2 * c4, e = 2 * hh;
-      *reinterpret_cast<float2 *>(DG + t * 64 + d) = make_float2(dgm[nt][e], dgm[nt][e + 1]);
+      *reinterpret_cast<float2 *>(DG + gsw(t, d)) = make_float2(dgm[nt][e], dgm[nt][e + 1]);
       *reinterpret_cast<uint32_t *>(sm + O_KD + sw64(t, d)) = pack_bf16(DQ[nt][e], DQ[nt][e + 1]);
       *reinterpret_cast<uint32_t *>(sm + O_QD + sw64(t, d)) =
           pack_bf16(DKp[nt][e] + DKm[nt][e], DKp[nt][e + 1] + DKm[nt][e + 1]);
@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     const int d = tid & 63, seg = tid >> 6;
     float ssum = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) ssum += DG[(seg * 8 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) ssum += DG[gsw(seg * 8 + r, d)];
     part[seg * 64 + d] = ssum;
     __syncthreads();
     float acc = dgacc[d];
@@ -627,8 +627,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
     for (int r = 7; r >= 0; --r) {
       const int t = seg * 8 + r;
-      acc += DG[t * 64 + d];
-      DG[t * 64 + d] = acc;
+      acc += DG[gsw(t, d)];
+      DG[gsw(t, d)] = acc;
     }
     if (tid < 64 && t0 + tid < T)
       ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(dbacc[tid]);
@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   fence_proxy_async_smem();
   __syncthreads();
   if (tid == 0) {
-    tma_store_rows(&tm.m[7], s_base + O_KF, h, t0, b);
+    tma_store_rows_f32(&tm.m[7], s_base + O_KF, h, t0, b);
     bulk_commit();
   }
   }  // chunk loop

@@ -47,7 +47,7 @@ constexpr int NT1 = 512;  // 16 warps: every phase splits into more independent 
 constexpr int OFF_QS = 0;                                // raw q/k/v tiles (TMA, 128-byte swizzle,
 constexpr int OFF_KS = OFF_QS + 8192;                    //   1024-byte aligned)
 constexpr int OFF_VS = OFF_KS + 8192;
-constexpr int OFF_GS = OFF_VS + 8192;                    // g (TMA) -> gamma (fp32 [t][d]) 16 KB
+constexpr int OFF_GS = OFF_VS + 8192;                    // g (TMA) -> gamma (fp32, gsw layout) 16 KB
 constexpr int OFF_OUT = OFF_GS + 16384;                  // the record, swizzled tiles
 constexpr int OFF_KD = OFF_OUT + HO_SIZE;                // Kdec
 constexpr int OFF_QD = OFF_KD + 8192;                    // Qdec
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       tma_load_rows(s_base + OFF_QS, &tm.m[0], h_, t0_, b_, mbar);
       tma_load_rows(s_base + OFF_KS, &tm.m[1], h_, t0_, b_, mbar);
       tma_load_rows(s_base + OFF_VS, &tm.m[2], h_, t0_, b_, mbar);
-      tma_load_rows(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
+      tma_load_rows_f32(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
     }
   };
   // beta of the next chunk, kept raw until its use so that the load does not stall anyone
@@ -184,15 +184,15 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const int d = tid & 63, seg = tid >> 6;
     float acc = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc += GS[(seg * 8 + r) * 64 + d];
+    for (int r = 0; r < 8; ++r) acc += GS[gsw(seg * 8 + r, d)];
     part[seg * 64 + d] = acc;
     __syncthreads();
     float off = 0.f;
     for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      off += GS[(seg * 8 + r) * 64 + d];
-      GS[(seg * 8 + r) * 64 + d] = off;
+      off += GS[gsw(seg * 8 + r, d)];
+      GS[gsw(seg * 8 + r, d)] = off;
     }
     __syncthreads();
   }
@@ -203,8 +203,8 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     float span = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      span = fmaxf(span, GS[(i * 16) * 64 + tid] - GS[(i * 16 + 8) * 64 + tid]);
-      span = fmaxf(span, GS[(i * 16 + 8) * 64 + tid] - GS[(i * 16 + 15) * 64 + tid]);
+      span = fmaxf(span, GS[gsw(i * 16, tid)] - GS[gsw(i * 16 + 8, tid)]);
+      span = fmaxf(span, GS[gsw(i * 16 + 8, tid)] - GS[gsw(i * 16 + 15, tid)]);
     }
     const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
     if (lane == 0) flag[warp] = any;
@@ -215,10 +215,10 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   const bool big = flag[0] | flag[1];
   if (tid < 64) {
     const int d = tid;
-    const float gC = GS[63 * 64 + d];
+    const float gC = GS[gsw(63, d)];
     float r[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = GS[(i * 16 + (big ? 0 : 8)) * 64 + d];
+    for (int i = 0; i < 4; ++i) r[i] = GS[gsw((i * 16 + (big ? 0 : 8)), d)];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       refs[i * 64 + d] = r[i];
@@ -241,8 +241,8 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w},
                    vw[4] = {vq.x, vq.y, vq.z, vq.w};
     const float bt = bet[t];
-    const float4 ga4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0);
-    const float4 gb4 = *reinterpret_cast<const float4 *>(GS + t * 64 + d0 + 4);
+    const float4 ga4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0));
+    const float4 gb4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0 + 4));
     const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
     uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[4][4];
 #pragma unroll
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
         } else {
           iF[x] = 0.f;
           eg[x] = __expf(gm);
-          eb[x] = __expf(GS[63 * 64 + d + x] - gm);
+          eb[x] = __expf(GS[gsw(63, d + x)] - gm);
         }
       }
       okd[e] = pack_bf16(kf.x * F[0], kf.y * F[1]);
@@ -314,8 +314,8 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
           const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
           const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
           const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
-          const float e0 = __expf(GS[t * 64 + d] - GS[s * 64 + d]);
-          const float e1 = __expf(GS[t * 64 + d + 1] - GS[s * 64 + d + 1]);
+          const float e0 = __expf(GS[gsw(t, d)] - GS[gsw(s, d)]);
+          const float e1 = __expf(GS[gsw(t, d + 1)] - GS[gsw(s, d + 1)]);
           mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
           mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
         }
