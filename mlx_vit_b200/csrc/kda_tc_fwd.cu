@@ -333,13 +333,11 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     if (tid < C) beta_next = load_beta(idx + gridDim.x);
   }
 
-  // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T: the 20 (block row i, block column j <= i,
-  //      matrix) tasks spread evenly over the 8 producer warps ----
-  for (int task = warp; task < 20; task += 16) {
-    const int mat = task & 1, pr = task >> 1;
-    const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
-    const int j = pr - i * (i + 1) / 2;
-    if (big && j == i) continue;  // diagonal block already computed exactly
+  // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T per (block row i, block column j <= i), and
+  //      (3) T_ii = (I + A_ii)^{-1}.  Warps 0-3 take the diagonal M block i = warp and invert
+  //      it right away (one column per lane, fp32 substitution); warps 4-15 take the 10 P
+  //      blocks and the 6 off-diagonal M blocks. ----
+  auto mp_block = [&](int mat, int i, int j) {
     float acc[2][4] = {};
     const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
 #pragma unroll
@@ -364,8 +362,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
           v0 *= bet[t];
           v1 *= bet[t];
           if (j == i) {
-            AD[i * 256 + tl * 16 + sl] = v0;
-            AD[i * 256 + tl * 16 + sl + 1] = v1;
+            *reinterpret_cast<float2 *>(AD + i * 256 + tl * 16 + sl) = make_float2(v0, v1);
           } else {
             *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
           }
@@ -375,24 +372,36 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
           *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
         }
       }
-  }
-  __syncthreads();
-
-  // ---- (3) T_ii = (I + A_ii)^{-1}, one column per thread, in registers ----
-  if (tid < 64) {
-    const int i = tid >> 4, u = tid & 15;
-    const float *A = AD + i * 256;
-    float x[16];
+  };
+  if (warp < 4) {
+    const int i = warp;
+    if (!big) mp_block(0, i, i);  // (a big chunk's diagonal blocks are already exact)
+    __syncwarp();
+    if (lane < 16) {
+      const int u = lane;
+      const float *A = AD + i * 256;
+      float x[16];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      float v = t == u ? 1.f : 0.f;
+      for (int t = 0; t < 16; ++t) {
+        float v = t == u ? 1.f : 0.f;
 #pragma unroll
-      for (int s = 0; s < t; ++s) v = fmaf(-A[t * 16 + s], x[s], v);
-      x[t] = v;
+        for (int s2 = 0; s2 < t; ++s2) v = fmaf(-A[t * 16 + s2], x[s2], v);
+        x[t] = v;
+      }
+      __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TI + i * 512);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
     }
-    __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TI + i * 512);
-#pragma unroll
-    for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
+  } else {
+    for (int q = warp - 4; q < 16; q += 12) {
+      // q < 10: P block number q of the 10 pairs (i, j <= i); else off-diagonal M block q - 10
+      const int pr = q < 10 ? q : (q == 10 ? 1 : q == 11 ? 3 : q == 12 ? 4 : q - 7);
+      const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
+      const int j = pr - i * (i + 1) / 2;
+      const int mat = q < 10 ? 1 : 0;
+      if (big && j == i) continue;  // diagonal block already computed exactly
+      mp_block(mat, i, j);
+    }
   }
   __syncthreads();
 
