@@ -36,7 +36,8 @@ static __device__ int g_fwd_status;
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 
-// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, row-major)
+// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, swizzled): -W [t][d],
+// U^T [j][t], Qd [t][d], Kb [t][d], P [t][s] (lower block triangle), e^{gamma_C} (fp32)
 constexpr int HO_W = 0, HO_U = 8192, HO_QD = 16384, HO_KB = 24576, HO_P = 32768, HO_EG = 40960;
 constexpr int HO_SIZE = 40960 + 256;
 
@@ -430,24 +431,33 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       }
     }
     const float so = isW ? -1.f : 1.f;
-    uint8_t *Ym = hom + (isW ? HO_W : HO_U);
+    if (isW) {  // -W [t][d]
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        *reinterpret_cast<uint32_t *>(Ym + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
-            pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<uint32_t *>(hom + HO_W + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
+              pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
+    } else {  // U^T [j][t], by transposing stores
+#pragma unroll
+      for (int np = 0; np < 2; ++np)
+        stsm_x4_t(ct_frag_addr(ho + HO_U, c0 + 16 * np, 16 * i, lane), pack_bf16(acc[2 * np][0], acc[2 * np][1]),
+                  pack_bf16(acc[2 * np][2], acc[2 * np][3]), pack_bf16(acc[2 * np + 1][0], acc[2 * np + 1][1]),
+                  pack_bf16(acc[2 * np + 1][2], acc[2 * np + 1][3]));
+    }
   }
 
   fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
   // ---- the record for kda_fwd_scan: one bulk copy, same swizzled layout as in smem ----
   if (tid == 0) {
-    bulk_s2g((uint8_t *)p.ws + (int64_t)idx * HO_SIZE, ho, HO_SIZE);
+    // the record stays in L2 for kda_fwd_scan; the saved record streams out
+    bulk_s2g_hint((uint8_t *)p.ws + (int64_t)idx * HO_SIZE, ho, HO_SIZE, l2_policy_keep());
     if (p.saved) {  // P, M, Tinv for the backward
       uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
-      bulk_s2g(sv + kSavedP, ho + HO_P, 8192);
-      bulk_s2g(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192);
+      const uint64_t pol = l2_policy_stream();
+      bulk_s2g_hint(sv + kSavedP, ho + HO_P, 8192, pol);
+      bulk_s2g_hint(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192, pol);
     }
     bulk_commit();
   }
@@ -508,9 +518,10 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {  // Mneg, Qt (staged in the free beta-Kd / beta-V tiles) and e^{gamma_C}
-      bulk_s2g(sv + kSavedM, s_base + OFF_XK, 8192);
-      bulk_s2g(sv + kSavedQt, s_base + OFF_XV, 8192);
-      bulk_s2g(sv + kSavedEG, ho + HO_EG, 256);
+      const uint64_t pol = l2_policy_stream();
+      bulk_s2g_hint(sv + kSavedM, s_base + OFF_XK, 8192, pol);
+      bulk_s2g_hint(sv + kSavedQt, s_base + OFF_XV, 8192, pol);
+      bulk_s2g_hint(sv + kSavedEG, ho + HO_EG, 256, pol);
       bulk_commit();
     }
   }
@@ -597,7 +608,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
 #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         uint32_t r[4];
-        ldsm_x4_t(ct_frag_addr(ho + HO_U, 16 * pp, jb, lane), r);
+        ldsm_x4(a_frag_addr(ho + HO_U, jb, 16 * pp, lane), r);  // U^T rows j, columns t
         const float2 a = unpack_bf16(r[0]), bq = unpack_bf16(r[1]), cq = unpack_bf16(r[2]), dq = unpack_bf16(r[3]);
         X[2 * pp][0] = a.x; X[2 * pp][1] = a.y; X[2 * pp][2] = bq.x; X[2 * pp][3] = bq.y;
         X[2 * pp + 1][0] = cq.x; X[2 * pp + 1][1] = cq.y; X[2 * pp + 1][2] = dq.x; X[2 * pp + 1][3] = dq.y;
