@@ -29,7 +29,7 @@ struct Params {
 };
 
 // Per-chunk record the tensor-core forward saves for the tensor-core backward (D = C = 64):
-// S0 = chunk-entry state [j][d], Unew^T [j][t], the decay-weighted P = Q K^T (lower incl.) and
+// S0^T = transposed chunk-entry state [d][j], Unew [t][j], the decay-weighted P = Q K^T (lower incl.) and
 // M = K K^T (strict lower) [t][s], Tinv = (I + beta M)^{-1} [t][s], Mneg = -Kb^T W [d'][d],
 // Qt = Qd - P W [t][d] (all bf16, 64 x 64 with the 128-byte row swizzle of the shared-memory
 // tiles, so that one bulk copy lands them ready for ldmatrix) and e^{gamma_C} [d] (fp32).

@@ -368,7 +368,8 @@ kda_bwd_flagged_chunks_kernel(Params p, const int *flagged, const __nv_bfloat16 
     for (int i = threadIdx.x; i < D * D; i += blockDim.x) {  // records are 128-byte swizzled
       const int row = i / 64, col = i % 64;
       const int sw = row * 64 + ((((col >> 3) ^ row) & 7) << 3) + (col & 7);
-      S0[i] = __bfloat162float(s0[sw]);
+      const int swt = col * 64 + ((((row >> 3) ^ col) & 7) << 3) + (row & 7);  // S0 is stored transposed
+      S0[i] = __bfloat162float(s0[swt]);
       dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + sw]);
     }
     bwd_chunk_body<__nv_bfloat16, Tb>(p, sm, bh, c, false);

@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
 constexpr int CK_NT = 512;  // 16 warps; warp w owns row block mt = w / 4, columns 16 * (w % 4)..
 constexpr int O_QS = 0, O_KS = 8192, O_VS = 16384, O_DO = 24576;   // raw bf16 tiles [t][d]
 constexpr int O_GS = 32768;                                         // g -> gamma -> F -> dgamma fp32
-// S0 [j][d], Unew^T [j][t], P [t][s], M [t][s], Tinv [t][s]: one bulk copy of the saved record
+// S0^T [d][j], Unew [t][j], P [t][s], M [t][s], Tinv [t][s]: one bulk copy of the saved record
 constexpr int O_S0 = 49152, O_UN = 57344, O_PB = 65536, O_MK = 73728, O_TF = 81920;
 constexpr int O_DS = 90112;                                         // dS1 [j][d]
 constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int row = jq * 8 + j;
-      a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(row, d))) *
+      a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(d, row))) *
            __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
     }
     atomicAdd(&dgacc[d], a * eG[d]);
@@ -434,8 +434,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       uint32_t aR[4], aO[4], aU[4], bS[4], bD[4];
       ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
       ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
-      ldsm_x4_t(ct_frag_addr(s_base + O_UN, 16 * kk, 16 * mt, lane), aU);  // Unew rows t, k = j
-      ldsm_x4_t(bkn_frag_addr(s_base + O_S0, 16 * kk, n0, lane), bS);
+      ldsm_x4(a_frag_addr(s_base + O_UN, 16 * mt, 16 * kk, lane), aU);  // Unew rows t, k = j
+      ldsm_x4(bnk_frag_addr(s_base + O_S0, n0, 16 * kk, lane), bS);     // S0^T rows d, k = j
       ldsm_x4_t(bkn_frag_addr(s_base + O_DS, 16 * kk, n0, lane), bD);
       mma16816(dRS[0], aR, bS[0], bS[1]);
       mma16816(dRS[1], aR, bS[2], bS[3]);
@@ -498,7 +498,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       uint32_t aO[4], aR[4], bU[4];
       ldsm_x4(a_frag_addr(s_base + O_DO, 16 * mt, 16 * kk, lane), aO);
       ldsm_x4(a_frag_addr(s_base + O_DR, 16 * mt, 16 * kk, lane), aR);
-      ldsm_x4_t(bkn_frag_addr(s_base + O_UN, 16 * kk, 16 * sb, lane), bU);
+      ldsm_x4(bnk_frag_addr(s_base + O_UN, 16 * sb, 16 * kk, lane), bU);
       mma16816(aP[0], aO, bU[0], bU[1]);
       mma16816(aP[1], aO, bU[2], bU[3]);
       mma16816(aA[0], aR, bU[0], bU[1]);

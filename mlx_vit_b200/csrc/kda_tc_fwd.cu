@@ -25,6 +25,7 @@
 // 2318-2456) with U = (I+A)^{-1} beta (V - K_proj S^T) split into U - W S^T.
 #include "kda_common.cuh"
 #include "kda_mma.cuh"
+#include "kda_tc05.cuh"
 #include "kda_tma.cuh"
 
 namespace kda {
@@ -36,9 +37,11 @@ static __device__ int g_fwd_status;
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 
-// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, swizzled): -W [t][d],
-// U^T [j][t], Qd [t][d], Kb [t][d], P [t][s] (lower block triangle), e^{gamma_C} (fp32)
-constexpr int HO_W = 0, HO_U = 8192, HO_QD = 16384, HO_KB = 24576, HO_P = 32768, HO_EG = 40960;
+// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, swizzled): Qd [t][d]
+// and -W [t][d] (together the 128-row A operand of the scan's first MMA), U [t][j], P [t][s]
+// (zero above the diagonal) and Kb^T [d][t] (together the A operand of its second MMA), and
+// e^{gamma_C} (fp32)
+constexpr int HO_QD = 0, HO_W = 8192, HO_U = 16384, HO_P = 24576, HO_KBT = 32768, HO_EG = 40960;
 constexpr int HO_SIZE = 40960 + 256;
 
 // ---------------------------------------------------------------------------------------
@@ -60,7 +63,8 @@ constexpr int OFF_XK = OFF_TI + 2048;                    // beta Kd
 constexpr int OFF_XV = OFF_XK + 8192;                    // beta V
 constexpr int OFF_MK = OFF_XV + 8192;                    // M = Kdec Kinc^T strict lower (bf16)
 constexpr int OFF_TF = OFF_MK + 8192;                    // Tinv = (I + A)^{-1} (bf16), after OFF_MK
-constexpr int OFF_RS = OFF_TF + 8192;                    // per-warp 16x16 staging
+constexpr int OFF_KBS = OFF_TF + 8192;                   // Kb [t][d] (bf16)
+constexpr int OFF_RS = OFF_KBS + 8192;                   // per-warp 16x16 staging
 constexpr int OFF_VEC = OFF_RS + 16 * 256;
 // vectors (floats): bet[64] refs[4][64] part[8][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
@@ -168,6 +172,13 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
     return t < T ? betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H] : from_f<Tb>(0.f);
   };
+  // P's blocks above the diagonal are zero (the scan multiplies the whole tile); nothing else
+  // writes them, so they are cleared once
+  for (int u = tid; u < 192; u += NT1) {
+    const int blk = u >> 5, r = (u >> 1) & 15, half = u & 1;
+    const int i = blk < 3 ? 0 : blk < 5 ? 1 : 2, j = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+    *reinterpret_cast<uint4 *>(hom + HO_P + sw64(16 * i + r, 16 * j + 8 * half)) = make_uint4(0u, 0u, 0u, 0u);
+  }
   int idx = blockIdx.x;
   if (idx < nchunks) issue_loads(idx);
   Tb beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : from_f<Tb>(0.f);
@@ -296,7 +307,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     *reinterpret_cast<uint4 *>(sm + OFF_XK + off) = make_uint4(oxk[0], oxk[1], oxk[2], oxk[3]);
     *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
     *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
-    *reinterpret_cast<uint4 *>(hom + HO_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
+    *reinterpret_cast<uint4 *>(sm + OFF_KBS + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       if (i >= blk)
@@ -438,12 +449,19 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
         for (int hh = 0; hh < 2; ++hh)
           *reinterpret_cast<uint32_t *>(hom + HO_W + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
               pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
-    } else {  // U^T [j][t], by transposing stores
+    } else {  // U [t][j]
 #pragma unroll
-      for (int np = 0; np < 2; ++np)
-        stsm_x4_t(ct_frag_addr(ho + HO_U, c0 + 16 * np, 16 * i, lane), pack_bf16(acc[2 * np][0], acc[2 * np][1]),
-                  pack_bf16(acc[2 * np][2], acc[2 * np][3]), pack_bf16(acc[2 * np + 1][0], acc[2 * np + 1][1]),
-                  pack_bf16(acc[2 * np + 1][2], acc[2 * np + 1][3]));
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<uint32_t *>(hom + HO_U + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
+              pack_bf16(acc[nt][2 * hh], acc[nt][2 * hh + 1]);
+    }
+    {  // Kb^T: warp (i, q) transposes the 16 x 16 block (rows 16 i, columns 16 q) of Kb
+      uint32_t r[4];
+      ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * i, 16 * q, lane), r);
+      stsm_x4(ho + HO_KBT + sw64(16 * q + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * i + (lane >> 4) * 8), r[0], r[1],
+              r[2], r[3]);
     }
   }
 
@@ -475,7 +493,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t af[4];
-        ldsm_x4_t(ct_frag_addr(ho + HO_KB, 16 * kk, jb, lane), af);
+        ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * kk, jb, lane), af);
 #pragma unroll
         for (int np = 0; np < 2; ++np) {
           uint32_t bf[4];
@@ -532,13 +550,50 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 // ---------------------------------------------------------------------------------------
 // kda_fwd_scan
 // ---------------------------------------------------------------------------------------
-constexpr int NT2 = 128;
-constexpr int NREC = 3;                     // record ring: chunk c + 2 loads while c is scanned
-constexpr int OFF2_O = 0;                   // O staging, 2 x 8 KB (TMA stores, 1024-byte aligned)
-constexpr int OFF2_SV = 2 * 8192;           // S0 | Unew^T staging for the saved record, 2 x 16 KB
-constexpr int OFF2_REC = OFF2_SV + 2 * 16384; // NREC x HO_SIZE, swizzled tiles
-constexpr int OFF2_MBAR = OFF2_REC + NREC * HO_SIZE; // NREC mbarriers
-constexpr int SMEM2 = OFF2_MBAR + 8 * NREC;
+// One CTA of 5 warps per (b, h), on the tcgen05 tensor cores with one M = 128 accumulator in
+// TMEM (64 columns).  Per chunk, with Sᵀ [d][j] and Unew [t][j] as bf16 B operands in shared
+// memory and the record's stacked A operands [Qd; -W] and [P; Kb^T]:
+//   MMA A:  D = [Qd; -W] S^T            rows 0-63: Qd S^T,  rows 64-127: -W S^T
+//   warps 2-3 (rows 64-127): Unew = U - W S^T -> bf16 tile; then put e^{gamma_C} S^T (fp32
+//   state rows d, kept in registers) into rows 64-127 of D
+//   MMA B:  D += [P; Kb^T] Unew         rows 0-63: O = Qd S^T + P Unew,
+//                                       rows 64-127: S^T <- diag(e^{gamma_C}) S^T + Kb^T Unew
+//   warps 0-1 drain O (bf16, TMA store); warps 2-3 take the new state.
+// One thread of warp 4 issues the MMAs, the record loads (a three-slot ring of bulk copies, two
+// chunks ahead) and the stores; S^T | Unew of each chunk leave by one bulk store for the
+// backward.  Every CTA-wide barrier votes on failures, so a bounded wait that gives up takes
+// all warps out together.
+constexpr int NT2 = 160;
+constexpr int NREC = 3;                       // record ring
+constexpr int NSV = 3;                        // S^T | Unew tiles (B operands and saved-record staging)
+constexpr int REC_STRIDE = 41 * 1024;         // ring slot (HO_SIZE rounded up to 1024 bytes)
+constexpr int OFF2_O = 0;                     // O staging, 2 x 8 KB (TMA stores)
+constexpr int OFF2_SV = 2 * 8192;             // NSV x 16 KB
+constexpr int OFF2_REC = OFF2_SV + NSV * 16384;  // NREC x REC_STRIDE
+constexpr int OFF2_MBAR = OFF2_REC + NREC * REC_STRIDE;  // NREC record mbarriers, 2 MMA mbarriers, TMEM slot
+constexpr int SMEM2 = OFF2_MBAR + 64;
+constexpr uint32_t kIdescScan = idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
+
+// 64 fp32 values -> one 128-byte bf16 row of a swizzled tile
+__device__ __forceinline__ void store_row_bf16(uint8_t *tile, int row, const float *x) {
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch)
+    *reinterpret_cast<uint4 *>(tile + sw64(row, ch * 8)) =
+        make_uint4(pack_bf16(x[8 * ch], x[8 * ch + 1]), pack_bf16(x[8 * ch + 2], x[8 * ch + 3]),
+                   pack_bf16(x[8 * ch + 4], x[8 * ch + 5]), pack_bf16(x[8 * ch + 6], x[8 * ch + 7]));
+}
+// this thread's TMEM lane, 64 columns from taddr
+__device__ __forceinline__ void tmem_row64(uint32_t taddr, float *x) {
+  uint32_t v[32], w[32];
+  tmem_ld32(taddr, v);
+  tmem_ld32(taddr + 32, w);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    x[i] = __uint_as_float(v[i]);
+    x[32 + i] = __uint_as_float(w[i]);
+  }
+}
 
 __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -546,151 +601,144 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
-  const int g4 = lane >> 2, c4 = lane & 3;
-  const int jb = warp * 16;
-  if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
+  if (s_base & 1023) {  // swizzled tiles need a 1024-byte aligned base
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
     return;
   }
+  const uint32_t mrec = s_base + OFF2_MBAR, mA = mrec + 8 * NREC, mB = mA + 8;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * NREC + 16);
+  const bool leader = tid == 128, lower = warp >= 2 && warp < 4, upper = warp < 2;
+  const int m = 32 * warp + lane;  // TMEM lane / accumulator row of warps 0-3
+  const int r = m - 64;            // warps 2-3: row t of Unew, row d of S^T
 
-  const uint32_t mbar = s_base + OFF2_MBAR;
-  if (tid == 0) {
-    for (int i = 0; i < NREC; ++i) mbar_init(mbar + 8 * i, 1);
+  if (leader) {
+    for (int i = 0; i < NREC + 2; ++i) mbar_init(mrec + 8 * i, 1);
     mbar_fence_init();
   }
+  float S[64];  // warps 2-3: S^T[r][j] = S[j][r]
+#pragma unroll
+  for (int j = 0; j < 64; ++j) S[j] = 0.f;
+  if (lower && p.state0) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) S[j] = p.state0[(int64_t)bh * D * D + j * D + r];
+  }
+  if (lower) store_row_bf16(sm + OFF2_SV, r, S);
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tslot), 64);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();  // the S^T tile is read by the tensor cores
+  tc_fence_before();
   __syncthreads();
-  auto issue = [&](int c) {  // one bulk copy of the chunk's whole record (thread 0)
-    if (tid == 0) {
-      const uint8_t *rec = (const uint8_t *)p.ws + ((int64_t)bh * nc + c) * HO_SIZE;
-      const int r = c % NREC;
-      mbar_expect_tx(mbar + r * 8, HO_SIZE);
-      bulk_g2s(s_base + OFF2_REC + r * HO_SIZE, rec, HO_SIZE, mbar + r * 8);
-    }
-  };
+  tc_fence_after();
+  const uint32_t tD = *tslot;
+  const uint32_t tl = tD + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's lane quarter
 
-  float S[8][4];
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float2 v = make_float2(0.f, 0.f);
-      if (p.state0)
-        v = *reinterpret_cast<const float2 *>(p.state0 + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4);
-      S[nt][2 * hh] = v.x;
-      S[nt][2 * hh + 1] = v.y;
-    }
-  issue(0);
-  if (nc > 1) issue(1);
+  auto issue = [&](int c) {  // leader: one bulk copy of the chunk's whole record
+    const uint8_t *rec = (const uint8_t *)p.ws + ((int64_t)bh * nc + c) * HO_SIZE;
+    const int s = c % NREC;
+    mbar_expect_tx(mrec + s * 8, HO_SIZE);
+    bulk_g2s(s_base + OFF2_REC + s * REC_STRIDE, rec, HO_SIZE, mrec + s * 8);
+  };
+  if (leader)
+    for (int c = 0; c < nc && c < NREC - 1; ++c) issue(c);
+  bool failed = false;
   for (int c = 0; c < nc; ++c) {
-    const int buf = c & 1, r = c % NREC;
-    const uint32_t ho = s_base + OFF2_REC + r * HO_SIZE;
-    const float *eG = reinterpret_cast<const float *>(sm + OFF2_REC + r * HO_SIZE + HO_EG);
-    const uint32_t ost = s_base + OFF2_O + buf * 8192, svst = s_base + OFF2_SV + buf * 16384;
-    // chunk c's record landed (bounded wait); the barrier also marks chunk c-1 consumed and
-    // (thread 0 waits for it) the stores of chunk c-2, which used this O / S0 staging
-    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
-    if (__syncthreads_or(!mbar_wait(mbar + r * 8, (c / NREC) & 1))) {
-      if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
-      break;
+    const int buf = c & 1, slot = c % NREC;
+    const uint32_t rec = s_base + OFF2_REC + slot * REC_STRIDE;
+    const uint8_t *recm = sm + OFF2_REC + slot * REC_STRIDE;
+    const float *eG = reinterpret_cast<const float *>(recm + HO_EG);
+    const uint32_t sv = s_base + OFF2_SV + (c % NSV) * 16384;
+    uint8_t *svm = sm + OFF2_SV + (c % NSV) * 16384, *svnm = sm + OFF2_SV + ((c + 1) % NSV) * 16384;
+    // chunk c's record landed; the barrier also publishes S^T(c); the leader has seen the stores
+    // of chunk c-2 (same O staging, same S^T | Unew tiles as chunk c+1) read their sources
+    if (leader) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+    if (__syncthreads_or(!mbar_wait(mrec + slot * 8, (c / NREC) & 1))) { failed = true; break; }
+    if (leader) {
+      if (c + NREC - 1 < nc) issue(c + NREC - 1);
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tc_mma(tD, desc_k(rec + HO_QD, k), desc_mn(sv, k), kIdescScan, k > 0);
+      tc_commit(mA);
     }
-    if (c + 2 < nc) issue(c + 2);
-    uint32_t sa[4][4];  // S as bf16 A fragments (rows j, k = d)
+    bool ok = true;
+    if (lower) {  // Unew = U - W S^T; then rows 64-127 of D <- e^{gamma_C} S^T
+      ok = mbar_wait(mA, c & 1);
+      tc_fence_after();
+      float x[64];
+      tmem_row64(tl, x);
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      sa[kk][0] = pack_bf16(S[2 * kk][0], S[2 * kk][1]);
-      sa[kk][1] = pack_bf16(S[2 * kk][2], S[2 * kk][3]);
-      sa[kk][2] = pack_bf16(S[2 * kk + 1][0], S[2 * kk + 1][1]);
-      sa[kk][3] = pack_bf16(S[2 * kk + 1][2], S[2 * kk + 1][3]);
-    }
-    uint32_t ua[4][4];  // Unew^T as A fragments (rows j, k = t)
-    {
-      float X[8][4];  // Unew^T = U^T + S (-W)^T
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(recm + HO_U + sw64(r, ch * 8));
+        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int pp = 0; pp < 4; ++pp) {
-        uint32_t r[4];
-        ldsm_x4(a_frag_addr(ho + HO_U, jb, 16 * pp, lane), r);  // U^T rows j, columns t
-        const float2 a = unpack_bf16(r[0]), bq = unpack_bf16(r[1]), cq = unpack_bf16(r[2]), dq = unpack_bf16(r[3]);
-        X[2 * pp][0] = a.x; X[2 * pp][1] = a.y; X[2 * pp][2] = bq.x; X[2 * pp][3] = bq.y;
-        X[2 * pp + 1][0] = cq.x; X[2 * pp + 1][1] = cq.y; X[2 * pp + 1][2] = dq.x; X[2 * pp + 1][3] = dq.y;
-      }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp) {
-          uint32_t bf[4];
-          ldsm_x4(bnk_frag_addr(ho + HO_W, 16 * pp, 16 * kk, lane), bf);
-          mma16816(X[2 * pp], sa[kk], bf[0], bf[1]);
-          mma16816(X[2 * pp + 1], sa[kk], bf[2], bf[3]);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16(uw[e]);
+          x[8 * ch + 2 * e] += f.x;
+          x[8 * ch + 2 * e + 1] += f.y;
         }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ua[kk][0] = pack_bf16(X[2 * kk][0], X[2 * kk][1]);
-        ua[kk][1] = pack_bf16(X[2 * kk][2], X[2 * kk][3]);
-        ua[kk][2] = pack_bf16(X[2 * kk + 1][0], X[2 * kk + 1][1]);
-        ua[kk][3] = pack_bf16(X[2 * kk + 1][2], X[2 * kk + 1][3]);
       }
+      store_row_bf16(svm + 8192, r, x);
+      const float e = eG[r];
+      uint32_t v[32], w[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = __float_as_uint(e * S[j]);
+        w[j] = __float_as_uint(e * S[32 + j]);
+      }
+      tmem_st32(tl, v);
+      tmem_st32(tl + 32, w);
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
     }
-    // O^T = S Qd^T + Unew^T P^T  (16 t-columns at a time)
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    if (leader) {
+      tc_fence_after();
 #pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      float O[2][4] = {};
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t bf[4];
-        ldsm_x4(bnk_frag_addr(ho + HO_QD, 16 * pp, 16 * kk, lane), bf);
-        mma16816(O[0], sa[kk], bf[0], bf[1]);
-        mma16816(O[1], sa[kk], bf[2], bf[3]);
-      }
-#pragma unroll
-      for (int kk = 0; kk <= pp; ++kk) {
-        uint32_t bf[4];
-        ldsm_x4(bnk_frag_addr(ho + HO_P, 16 * pp, 16 * kk, lane), bf);
-        mma16816(O[0], ua[kk], bf[0], bf[1]);
-        mma16816(O[1], ua[kk], bf[2], bf[3]);
-      }
-      stsm_x4_t(ct_frag_addr(ost, 16 * pp, jb, lane), pack_bf16(O[0][0], O[0][1]), pack_bf16(O[0][2], O[0][3]),
-                pack_bf16(O[1][0], O[1][1]), pack_bf16(O[1][2], O[1][3]));
+      for (int k = 0; k < 4; ++k) tc_mma(tD, desc_k(rec + HO_P, k), desc_mn(sv + 8192, k), kIdescScan, 1);
+      tc_commit(mB);
     }
-    // the state-dependent part of the backward's per-chunk record: S0 and Unew^T (bf16),
-    // staged for one bulk store
-    if (p.saved) {
+    if (warp < 4) {
+      ok = mbar_wait(mB, c & 1);
+      tc_fence_after();
+      float x[64];
+      tmem_row64(tl, x);
+      if (upper) {
+        store_row_bf16(sm + OFF2_O + buf * 8192, m, x);  // O row t
+      } else {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t a = sw64(jb + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * kk + (lane >> 4) * 8);
-        stsm_x4(svst + a, sa[kk][0], sa[kk][1], sa[kk][2], sa[kk][3]);
-        stsm_x4(svst + 8192 + a, ua[kk][0], ua[kk][1], ua[kk][2], ua[kk][3]);
+        for (int j = 0; j < 64; ++j) S[j] = x[j];
+        store_row_bf16(svnm, r, S);  // S^T(c+1) row d
       }
+      fence_proxy_async_smem();
+      tc_fence_before();
     }
-    // S <- S diag(e^gamma_C) + Unew^T Kb
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float e0 = eG[nt * 8 + 2 * c4], e1 = eG[nt * 8 + 2 * c4 + 1];
-      S[nt][0] *= e0; S[nt][1] *= e1; S[nt][2] *= e0; S[nt][3] *= e1;
-    }
-#pragma unroll
-    for (int nd = 0; nd < 4; ++nd)
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t bf[4];
-        ldsm_x4_t(bkn_frag_addr(ho + HO_KB, 16 * kk, 16 * nd, lane), bf);
-        mma16816(S[2 * nd], ua[kk], bf[0], bf[1]);
-        mma16816(S[2 * nd + 1], ua[kk], bf[2], bf[3]);
-      }
-    fence_proxy_async_smem();
-    __syncthreads();                 // O staging complete: one TMA store (rows past T dropped)
-    if (tid == 0) {
-      tma_store_rows(&tm.m[0], ost, h, c * C, b);
-      if (p.saved) bulk_s2g((uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk + kSavedS0, svst, 16384);
+    if (__syncthreads_or(!ok)) { failed = true; break; }
+    if (leader) {  // O by TMA (rows past T dropped); S^T | Unew of chunk c for the backward
+      tma_store_rows(&tm.m[0], s_base + OFF2_O + buf * 8192, h, c * C, b);
+      if (p.saved) bulk_s2g((uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk + kSavedS0, sv, 16384);
       bulk_commit();
     }
   }
-  if (tid == 0) bulk_wait_all();
+  if (failed && leader) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+  if (!failed && lower) {
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
-      *reinterpret_cast<float2 *>(p.stateT + (int64_t)bh * D * D + (jb + g4 + 8 * hh) * D + nt * 8 + 2 * c4) =
-          make_float2(S[nt][2 * hh], S[nt][2 * hh + 1]);
+    for (int j = 0; j < 64; ++j) p.stateT[(int64_t)bh * D * D + j * D + r] = S[j];
+  }
+  if (leader) {
+    bulk_wait_all();
+    if (failed) {  // no MMA may still write TMEM when it is freed
+      mbar_wait(mA, 0);
+      mbar_wait(mA, 1);
+      mbar_wait(mB, 0);
+      mbar_wait(mB, 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) tmem_dealloc(tD, 64);
 }
 
 template <typename Tb>
