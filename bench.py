@@ -161,6 +161,7 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     from mlx_vit_b200 import _lib, cuda_kda, kda_forward, kda_backward
+    from mlx_vit_b200.shard import max_over_ranks
     from mlx_vit_b200.synthetic import make_inputs_torch
 
     dev = torch.device("cuda", local_rank)
@@ -237,11 +238,9 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
     launches = launches_per_step * args.steps
     total_ms = sum(fwd_ms) + sum(bwd_ms)
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
+    total_ms = max_over_ranks(total_ms, dev)
     ms_per_step = total_ms / args.steps
     tokens = B * T * world * args.steps
     value = tokens / (total_ms / 1e3)
@@ -277,10 +276,7 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = tokens / (float(te.item()) / 1e3)
+    e2e_value = tokens / (max_over_ranks(e0.elapsed_time(e1), dev) / 1e3)
 
     if rank != 0:
         return None

@@ -225,21 +225,21 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   if (tid == 0) bulk_wait_read_all();
   __syncthreads();
   const bool big = flag[0] | flag[1];
-  if (tid < 64) {
-    const int d = tid;
+  {  // per-block vectors, thread (slot, d): slot i < 4 -> block i's entries, slot 4 -> e^{gamma_C}
+    const int d = tid & 63, slot = tid >> 6, ro = big ? 0 : 8;
     const float gC = GS[gsw(63, d)];
-    float r[4];
+    if (slot < 4) {
+      const int i = slot;
+      const float ri = GS[gsw(i * 16 + ro, d)];
+      refs[i * 64 + d] = ri;
+      erb[i * 64 + d] = __expf(ri);
+      egr[i * 64 + d] = __expf(gC - ri);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = GS[gsw((i * 16 + (big ? 0 : 8)), d)];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      refs[i * 64 + d] = r[i];
-      erb[i * 64 + d] = __expf(r[i]);
-      egr[i * 64 + d] = __expf(gC - r[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j <= i ? __expf(r[i] - r[j]) : 0.f;
+      for (int j = 0; j < 4; ++j)
+        gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + ro, d)]) : (j == i ? 1.f : 0.f);
+    } else if (slot == 4) {
+      eG[d] = __expf(gC);
     }
-    eG[d] = __expf(gC);
   }
   __syncthreads();
 
@@ -422,42 +422,36 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   if (warp < 8) solve_columns(sm, s_base, OFF_TF - OFF_OUT, -1, warp * 8, warp >> 1, -1.f, 1.f, warp, lane);
   __syncthreads();
   // ---- (5) W = Tinv beta Kd (stored negated) and U = Tinv beta V as one block-triangular GEMM;
-  //      warp (row block i, 32 of the 128 columns of [W | U]) ----
+  //      warp w takes 16 of the 128 columns of [W | U] for the row blocks {0, 3} or {1, 2}, so
+  //      every warp does 5 of the 10 nonzero blocks of a column ----
   {
-    const int i = warp >> 2, q = warp & 3, c0 = 32 * (q & 1);
-    const bool isW = q < 2;
+    const int cg = warp & 7, c0 = 16 * (cg & 3);
+    const bool isW = cg < 4;
     const uint32_t xb = s_base + (isW ? OFF_XK : OFF_XV);
-    float acc[4][4] = {};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (k > i) break;
-      uint32_t af[4];
-      ldsm_x4(a_frag_addr(s_base + OFF_TF, 16 * i, 16 * k, lane), af);
+    for (int half = 0; half < 2; ++half) {
+      const int i = half == 0 ? (warp >> 3) : 3 - (warp >> 3);
+      float acc[2][4] = {};
 #pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t bf[4];
-        ldsm_x4_t(bkn_frag_addr(xb, 16 * k, c0 + 16 * np, lane), bf);
-        mma16816(acc[2 * np], af, bf[0], bf[1]);
-        mma16816(acc[2 * np + 1], af, bf[2], bf[3]);
+      for (int k = 0; k < 4; ++k) {
+        if (k > i) break;
+        uint32_t af[4], bf[4];
+        ldsm_x4(a_frag_addr(s_base + OFF_TF, 16 * i, 16 * k, lane), af);
+        ldsm_x4_t(bkn_frag_addr(xb, 16 * k, c0, lane), bf);
+        mma16816(acc[0], af, bf[0], bf[1]);
+        mma16816(acc[1], af, bf[2], bf[3]);
       }
-    }
-    const float so = isW ? -1.f : 1.f;
-    if (isW) {  // -W [t][d]
+      const float so = isW ? -1.f : 1.f;  // -W [t][d], U [t][j]
+      uint8_t *Y = hom + (isW ? HO_W : HO_U);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(hom + HO_W + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
+          *reinterpret_cast<uint32_t *>(Y + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
               pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
-    } else {  // U [t][j]
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          *reinterpret_cast<uint32_t *>(hom + HO_U + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
-              pack_bf16(acc[nt][2 * hh], acc[nt][2 * hh + 1]);
     }
     {  // Kb^T: warp (i, q) transposes the 16 x 16 block (rows 16 i, columns 16 q) of Kb
+      const int i = warp >> 2, q = warp & 3;
       uint32_t r[4];
       ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * i, 16 * q, lane), r);
       stsm_x4(ho + HO_KBT + sw64(16 * q + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * i + (lane >> 4) * 8), r[0], r[1],
