@@ -184,7 +184,9 @@ constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
 constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
 constexpr int O_VEC = 155648;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
-              V_EG = 2368, V_DB = 2432, V_DGM = 2496, V_FLAG = 2560;
+              V_EG = 2368, V_PDB = 2432, V_PDG = 3200, V_FLAG = 3968;
+// partial sums, each slot written by exactly one thread (no atomics): dbeta rows from P5, P6, P7
+// [3][4 column warps][64], dGamma_C columns from the state term [8] and P6 [4] ([12][64])
 constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // three mbarriers
 constexpr int CK_SMEM = O_MBAR + 24;
 
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   float *GS = reinterpret_cast<float *>(sm + O_GS);
   float *vec = reinterpret_cast<float *>(sm + O_VEC);
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
-  float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *dbacc = vec + V_DB, *dgacc = vec + V_DGM;
+  float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *pdb = vec + V_PDB, *pdg = vec + V_PDG;
   const Tb *betag = (const Tb *)p.beta;
   int *flagged = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset(nchunks));
 
@@ -265,8 +267,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   if (tid < C) {
     bet[tid] = to_f(beta_next);
-    dbacc[tid] = 0.f;
-    dgacc[tid] = 0.f;
   }
   if (inext < nchunks && tid < C) beta_next = load_beta(inext);
   // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       a += __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_S0 + sw64(d, row))) *
            __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_DS + sw64(row, d)));
     }
-    atomicAdd(&dgacc[d], a * eG[d]);
+    pdg[jq * 64 + d] = a * eG[d];
   }
   // ---- P5: dU = P^T dO + Kb dS1^T (staged bf16 in the DP tile), dR = Tinv^T dU ----
   {
@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       float v = dbv[hh];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
+      if (c4 == 0) pdb[(0 * 4 + nq) * 64 + 16 * mt + g4 + 8 * hh] = v;
     }
   }
   __syncthreads();
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       float v = dbr[hh];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
+      if (c4 == 0) pdb[(1 * 4 + nq) * 64 + 16 * mt + g4 + 8 * hh] = v;
     }
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         v += __shfl_xor_sync(0xffffffffu, v, 8);
         v += __shfl_xor_sync(0xffffffffu, v, 16);
-        if (g4 == 0) atomicAdd(&dgacc[n0 + 8 * nt + 2 * c4 + x], v);
+        if (g4 == 0) pdg[(8 + mt) * 64 + n0 + 8 * nt + 2 * c4 + x] = v;
       }
   }
   // ---- P7: block (mt, sb = nq) of dP = dO Unew^T (s <= t) and dKK = -beta dR Unew^T (s < t),
@@ -522,8 +522,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       float v = dbr[hh];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      if (c4 == 0) atomicAdd(&dbacc[16 * mt + g4 + 8 * hh], v);
+      if (c4 == 0) pdb[(2 * 4 + nq) * 64 + 16 * mt + g4 + 8 * hh] = v;
     }
+  } else if (c4 == 0) {  // blocks above the diagonal contribute nothing
+    pdb[(2 * 4 + nq) * 64 + 16 * mt + g4] = 0.f;
+    pdb[(2 * 4 + nq) * 64 + 16 * mt + g4 + 8] = 0.f;
   }
   __syncthreads();
   if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
@@ -622,7 +625,9 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     for (int r = 0; r < 8; ++r) ssum += DG[gsw(seg * 8 + r, d)];
     part[seg * 64 + d] = ssum;
     __syncthreads();
-    float acc = dgacc[d];
+    float acc = 0.f;  // dGamma_C
+#pragma unroll
+    for (int s2 = 0; s2 < 12; ++s2) acc += pdg[s2 * 64 + d];
     for (int s2 = seg + 1; s2 < 8; ++s2) acc += part[s2 * 64 + d];
 #pragma unroll
     for (int r = 7; r >= 0; --r) {
@@ -630,8 +635,12 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       acc += DG[gsw(t, d)];
       DG[gsw(t, d)] = acc;
     }
-    if (tid < 64 && t0 + tid < T)
-      ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(dbacc[tid]);
+    if (tid < 64 && t0 + tid < T) {
+      float db = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < 12; ++s2) db += pdb[s2 * 64 + tid];
+      ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(db);
+    }
   }
   fence_proxy_async_smem();
   __syncthreads();
