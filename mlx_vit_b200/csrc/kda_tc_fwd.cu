@@ -286,20 +286,18 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       oqe[e] = pack_bf16(qf.x * eg[0], qf.y * eg[1]);
       oxv[e] = pack_bf16(bt * vf.x, bt * vf.y);
       okb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
+      if (!big) {  // Kinc of the diagonal block only: k / F (the GEMMs rescale it per block pair)
+        oki[0][e] = pack_bf16(kf.x * iF[0], kf.y * iF[1]);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float s0 = 0.f, s1 = 0.f;
-        if (i >= blk) {
-          if (!big) {
-            const float2 gg = *reinterpret_cast<const float2 *>(gij + (i * 4 + blk) * 64 + d);
-            s0 = iF[0] * gg.x;
-            s1 = iF[1] * gg.y;
-          } else {
+        for (int i = 0; i < 4; ++i) {
+          float s0 = 0.f, s1 = 0.f;
+          if (i >= blk) {
             s0 = __expf(refs[i * 64 + d] - gam[2 * e]);
             s1 = __expf(refs[i * 64 + d + 1] - gam[2 * e + 1]);
           }
+          oki[i][e] = pack_bf16(kf.x * s0, kf.y * s1);
         }
-        oki[i][e] = pack_bf16(kf.x * s0, kf.y * s1);
       }
     }
     *reinterpret_cast<uint4 *>(sm + OFF_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
@@ -308,11 +306,16 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
     *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
     *reinterpret_cast<uint4 *>(sm + OFF_KBS + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
+    if (!big) {
+      *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(blk, blk) * 2048 + sw64(t & 15, d0)) =
+          make_uint4(oki[0][0], oki[0][1], oki[0][2], oki[0][3]);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (i >= blk)
-        *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(i, blk) * 2048 + sw64(t & 15, d0)) =
-            make_uint4(oki[i][0], oki[i][1], oki[i][2], oki[i][3]);
+      for (int i = 0; i < 4; ++i)
+        if (i >= blk)
+          *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(i, blk) * 2048 + sw64(t & 15, d0)) =
+              make_uint4(oki[i][0], oki[i][1], oki[i][2], oki[i][3]);
+    }
   }
   __syncthreads();
 
@@ -351,11 +354,23 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   //      blocks and the 6 off-diagonal M blocks. ----
   auto mp_block = [&](int mat, int i, int j) {
     float acc[2][4] = {};
-    const uint32_t kib = s_base + OFF_KI + ki_index(i, j) * 2048;
+    // a big chunk has every Kinc tile; otherwise only the diagonal ones (k / F) and the block
+    // pair's factor e^{r_i - r_j} scales the A operand along d
+    const bool scale = !big && j < i;
+    const uint32_t kib = s_base + OFF_KI + ki_index(scale ? j : i, j) * 2048;
+    const float *G = gij + (i * 4 + j) * 64;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t af[4], bf[4];
       ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af);
+      if (scale) {
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float2 v = unpack_bf16(af[x]);
+          const float2 gg = *reinterpret_cast<const float2 *>(G + 16 * kk + (x >> 1) * 8 + 2 * c4);
+          af[x] = pack_bf16(v.x * gg.x, v.y * gg.y);
+        }
+      }
       ldsm_x4(bnk_frag_addr(kib, 0, 16 * kk, lane), bf);
       mma16816(acc[0], af, bf[0], bf[1]);
       mma16816(acc[1], af, bf[2], bf[3]);
