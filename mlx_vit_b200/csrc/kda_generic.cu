@@ -350,55 +350,6 @@ kda_bwd_generic_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------------------------------
-// exact per-chunk backward for the chunks the tensor-core backward flagged (decay too strong
-// for its factored decay form): grid (B*H*nc), one chunk per CTA; S0 comes from the tensor-core
-// saved record (bf16), the exit cotangent dS from the workspace (bf16).
-// ---------------------------------------------------------------------------------------
-template <typename Tb>
-__global__ void __launch_bounds__(kGenThreads)
-kda_bwd_flagged_chunks_kernel(Params p, const int *flagged, const __nv_bfloat16 *ds_exit) {
-  extern __shared__ float sm[];
-  const int D = p.D, nc = p.nc, count = flagged[0];
-  for (int f = blockIdx.x; f < count; f += gridDim.x) {
-    const int idx = flagged[1 + f], bh = idx / nc, c = idx % nc;
-    float *S0 = sm, *dS = S0 + D * D;
-    const __nv_bfloat16 *s0 = (const __nv_bfloat16 *)((const uint8_t *)p.saved_in +
-                                                      (int64_t)idx * kSavedChunk + kSavedS0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) {  // records are 128-byte swizzled
-      const int row = i / 64, col = i % 64;
-      const int sw = row * 64 + ((((col >> 3) ^ row) & 7) << 3) + (col & 7);
-      const int swt = col * 64 + ((((row >> 3) ^ col) & 7) << 3) + (row & 7);  // S0 is stored transposed
-      S0[i] = __bfloat162float(s0[swt]);
-      dS[i] = __bfloat162float(ds_exit[(int64_t)idx * D * D + sw]);
-    }
-    bwd_chunk_body<__nv_bfloat16, Tb>(p, sm, bh, c, false);
-  }
-}
-
-size_t generic_bwd_smem(int D, int C);
-
-int bwd_flagged_chunks(const Params &p, int dtype_beta, const int *flags,
-                       const __nv_bfloat16 *ds_exit, cudaStream_t st) {
-  const size_t smem = generic_bwd_smem(p.D, p.C);
-  int n = p.B * p.H * p.nc;  // grid: at most one CTA per chunk, at most two per SM
-  if (n > 296) n = 296;
-  if (dtype_beta == KDA_BF16) {
-    auto kern = kda_bwd_flagged_chunks_kernel<__nv_bfloat16>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) return KDA_ERR_CUDA;
-    kern<<<n, kGenThreads, smem, st>>>(p, flags, ds_exit);
-  } else if (dtype_beta == KDA_F32) {
-    auto kern = kda_bwd_flagged_chunks_kernel<float>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) return KDA_ERR_CUDA;
-    kern<<<n, kGenThreads, smem, st>>>(p, flags, ds_exit);
-  } else {
-    return KDA_ERR_DTYPE;
-  }
-  count_launch();
-  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
-}
-
-// ---------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------
 size_t generic_fwd_smem(int D, int C, int dvs) {

@@ -20,10 +20,10 @@
 //   kda_bwd_chunks      one CTA per (b, h, chunk), independent of each other: takes the
 //                       chunk's decay-weighted P, M and Tinv from the saved record, forms
 //                       dR = Tinv^T dU as one GEMM, and produces all gradients.
-// Chunks whose decay is too strong for the factored form are flagged and redone by the exact
-// fp32 per-chunk kernel (kda_bwd_flagged_chunks_kernel).
+// Chunks whose decay is too strong for the factored form ("big": gamma moves more than
+// kSpanMax across half a 16-row block in some channel) take exact per-element decay factors in
+// the same kernel.
 #include <mutex>
-#include <type_traits>
 
 #include "kda_common.cuh"
 #include "kda_mma.cuh"
@@ -31,8 +31,6 @@
 
 namespace kda {
 
-int bwd_flagged_chunks(const Params &p, int dtype_beta, const int *flags,
-                       const __nv_bfloat16 *ds_exit, cudaStream_t st);
 
 namespace tcbwd {
 
@@ -42,9 +40,8 @@ static __device__ int g_bwd_status;
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 
-// workspace: exit cotangent per chunk (bf16 [j][d]), then the count and the list of flagged
-// chunks (ints)
-__host__ __device__ inline size_t ws_flags_offset(int64_t nchunks) { return (size_t)nchunks * 8192; }
+// workspace: the exit cotangent of every chunk (bf16 [j][d], swizzled)
+__host__ __device__ inline size_t ws_bytes(int64_t nchunks) { return (size_t)nchunks * 8192; }
 
 // ---------------------------------------------------------------------------------------
 // state-cotangent scan
@@ -64,15 +61,13 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3, jb = warp * 16;
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  const int H = p.H, nc = p.nc;
+  const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
   __nv_bfloat16 *ds_exit = (__nv_bfloat16 *)p.ws;
   if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_MISALIGNED);
     return;
   }
-  if (bh == 0 && tid == 0)  // the chunk kernel that follows appends flagged chunks to a fresh list
-    *reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset((int64_t)p.B * H * nc)) = 0;
 
   const uint32_t mbar = s_base + SC_MBAR;
   if (tid == 0) {
@@ -204,7 +199,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART, *erb = vec + V_ERB;
   float *egr = vec + V_EGR, *gij = vec + V_G, *eG = vec + V_EG, *pdb = vec + V_PDB, *pdg = vec + V_PDG;
   const Tb *betag = (const Tb *)p.beta;
-  int *flagged = reinterpret_cast<int *>((uint8_t *)p.ws + ws_flags_offset(nchunks));
 
   // The CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...  The next
   // chunk's inputs are loaded in three stages, each issued (by one thread: TMA tiles of
@@ -296,14 +290,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
     bigloc = !(span <= kSpanMax);
   }
+  // a "big" chunk (decay too strong for the factored form) keeps gamma itself and takes exact
+  // per-element decay factors in P2, P6 and P8; everything else is the same
   const int big = __syncthreads_or(bigloc);
-  if (big) {  // redone exactly by the flagged-chunk kernel
-    if (tid == 0) flagged[1 + atomicAdd(&flagged[0], 1)] = idx;
-    if (inext < nchunks)
-      for (int stage = 0; stage < 3; ++stage) issue_loads(inext, stage);
-    continue;
-  }
-  if (tid < 64) {
+  if (tid < 64 && big) eG[tid] = __expf(GS[gsw(63, tid)]);
+  if (tid < 64 && !big) {
     const int d = tid;
     const float gC = GS[gsw(63, d)];
     float r[4];
@@ -322,7 +313,29 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   if (tid == 0) bulk_wait_read_all();  // the previous chunk's output stores have read KD, QD, KF
   __syncthreads();
 
-  // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma} ----
+  // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma};
+  //      a big chunk builds KB only, with exact factors, and keeps a copy of gamma over the KD
+  //      and QD tiles for P8 (GS is reloaded before P8) ----
+  float *GB = reinterpret_cast<float *>(sm + O_KD);
+  if (big) {
+    for (int u = tid; u < 512; u += CK_NT) {
+      const int t = u >> 3, ch = u & 7, d0 = ch * 8;
+      const uint32_t off = sw64(t, d0);
+      const uint4 kq = *reinterpret_cast<const uint4 *>(sm + O_KS + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w};
+      uint32_t okb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 kf = unpack_bf16(kw[e]);
+        const int d = d0 + 2 * e;
+        const float2 gm = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
+        const float2 gc = *reinterpret_cast<const float2 *>(GS + gsw(63, d));
+        *reinterpret_cast<float2 *>(GB + gsw(t, d)) = gm;
+        okb[e] = pack_bf16(kf.x * __expf(gc.x - gm.x), kf.y * __expf(gc.y - gm.y));
+      }
+      *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
+    }
+  } else
   for (int u = tid; u < 512; u += CK_NT) {
     const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
     const uint32_t off = sw64(t, d0);
@@ -450,17 +463,27 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       const int d = n0 + 8 * nt + 2 * c4;
       const float2 er = *reinterpret_cast<const float2 *>(erb + mt * 64 + d);
       const float2 eq = *reinterpret_cast<const float2 *>(egr + mt * 64 + d);
+      const float2 gc = *reinterpret_cast<const float2 *>(GS + gsw(63, d));  // gamma_C (big chunks)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int t = 16 * mt + g4 + 8 * hh;
-        const float2 F = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
+        const float2 F = *reinterpret_cast<const float2 *>(GS + gsw(t, d));  // F, or gamma if big
         const float2 kv = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
         const float nb = -bet[t];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int e = 2 * hh + x;
-          const float f = x ? F.y : F.x, k_ = x ? kv.y : kv.x;
-          const float eg = f * (x ? er.y : er.x), eb = __fdividef(x ? eq.y : eq.x, f);
+          const float fg = x ? F.y : F.x, k_ = x ? kv.y : kv.x;
+          float f, eg, eb;  // e^{gamma_t} = f e^{r}, e^{gamma_C - gamma_t} = e^{gamma_C - r} / f
+          if (!big) {
+            f = fg;
+            eg = f * (x ? er.y : er.x);
+            eb = __fdividef(x ? eq.y : eq.x, f);
+          } else {
+            f = 1.f;
+            eg = __expf(fg);
+            eb = __expf((x ? gc.y : gc.x) - fg);
+          }
           Fv[nt][e] = f;
           DQ[nt][e] = dOS[nt][e] * eg;
           DKp[nt][e] = nb * dRS[nt][e] * eg;
@@ -531,7 +554,76 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   __syncthreads();
   if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
   // ---- P8: decayed products ----
-  {
+  if (big) {  // exact per-element factors e^{gamma_t - gamma_s} (gamma kept over KD | QD)
+    float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {}, gm[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float2 v = *reinterpret_cast<const float2 *>(GB + gsw(16 * mt + g4 + 8 * hh, n0 + 8 * nt + 2 * c4));
+        gm[nt][2 * hh] = v.x;
+        gm[nt][2 * hh + 1] = v.y;
+      }
+    auto bf = [&](int tile, int r, int c) {
+      return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
+    };
+    for (int s2 = 0; s2 < 16 * mt + 16; ++s2) {  // Q2, K2: sum over s <= t
+      float dp[2], dk[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = 16 * mt + g4 + 8 * hh;
+        dp[hh] = s2 <= t ? bf(O_DP, t, s2) : 0.f;
+        dk[hh] = s2 <= t ? bf(O_DK, t, s2) : 0.f;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int d = n0 + 8 * nt + 2 * c4;
+        const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s2, d));
+        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s2, d)));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int e = 2 * hh + x;
+            const float w = (x ? ks.y : ks.x) * __expf(fminf(gm[nt][e] - (x ? gs.y : gs.x), 0.f));
+            Q2[nt][e] = fmaf(dp[hh], w, Q2[nt][e]);
+            K2[nt][e] = fmaf(dk[hh], w, K2[nt][e]);
+          }
+      }
+    }
+    for (int t2 = 16 * mt; t2 < 64; ++t2) {  // M2: sum over t >= s
+      float dp[2], dk[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int s_ = 16 * mt + g4 + 8 * hh;
+        dp[hh] = t2 >= s_ ? bf(O_DP, t2, s_) : 0.f;
+        dk[hh] = t2 >= s_ ? bf(O_DK, t2, s_) : 0.f;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int d = n0 + 8 * nt + 2 * c4;
+        const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t2, d));
+        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t2, d)));
+        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t2, d)));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int e = 2 * hh + x;
+            const float w = __expf(fminf((x ? gt.y : gt.x) - gm[nt][e], 0.f));
+            M2[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, M2[nt][e]);
+          }
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        DQ[nt][e] += Q2[nt][e];
+        DKp[nt][e] += K2[nt][e];
+        DKm[nt][e] += M2[nt][e];
+      }
+  } else {
     float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {};
     for (int j = 0; j <= mt; ++j) {  // rows t in block mt, columns s in block j
       float T1[2][4] = {}, T2[2][4] = {};
@@ -673,10 +765,7 @@ int launch(const Params &p, cudaStream_t st) {
     return KDA_ERR_CUDA;
   kern<<<n < nsm ? n : nsm, CK_NT, CK_SMEM, st>>>(p, tm);
   count_launch();
-  if (cudaPeekAtLastError() != cudaSuccess) return KDA_ERR_CUDA;
-  const int *flags = reinterpret_cast<const int *>((const uint8_t *)p.ws + ws_flags_offset(n));
-  return bwd_flagged_chunks(p, std::is_same<Tb, float>::value ? KDA_F32 : KDA_BF16, flags,
-                            (const __nv_bfloat16 *)p.ws, st);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
 
 }  // namespace tcbwd
@@ -693,7 +782,7 @@ int tc_bwd_device_status(bool reset) {
 
 size_t tc_bwd_workspace_bytes(const KdaDesc *d) {
   const int64_t n = d->B * d->H * ((d->T + d->chunk - 1) / d->chunk);
-  return tcbwd::ws_flags_offset(n) + (size_t)(n + 1) * sizeof(int);
+  return tcbwd::ws_bytes(n);
 }
 
 int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st) {
