@@ -463,7 +463,6 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       const int d = n0 + 8 * nt + 2 * c4;
       const float2 er = *reinterpret_cast<const float2 *>(erb + mt * 64 + d);
       const float2 eq = *reinterpret_cast<const float2 *>(egr + mt * 64 + d);
-      const float2 gc = *reinterpret_cast<const float2 *>(GS + gsw(63, d));  // gamma_C (big chunks)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int t = 16 * mt + g4 + 8 * hh;
@@ -482,7 +481,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
           } else {
             f = 1.f;
             eg = __expf(fg);
-            eb = __expf((x ? gc.y : gc.x) - fg);
+            eb = __expf(GS[gsw(63, d + x)] - fg);  // gamma_C - gamma_t
           }
           Fv[nt][e] = f;
           DQ[nt][e] = dOS[nt][e] * eg;
@@ -555,7 +554,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
   // ---- P8: decayed products ----
   if (big) {  // exact per-element factors e^{gamma_t - gamma_s} (gamma kept over KD | QD)
-    float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {}, gm[2][4];
+    float gm[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -567,7 +566,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     auto bf = [&](int tile, int r, int c) {
       return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
     };
-    for (int s2 = 0; s2 < 16 * mt + 16; ++s2) {  // Q2, K2: sum over s <= t
+    for (int s2 = 0; s2 < 16 * mt + 16; ++s2) {  // dq, dk rows: sum over s <= t
       float dp[2], dk[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -586,12 +585,12 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
           for (int x = 0; x < 2; ++x) {
             const int e = 2 * hh + x;
             const float w = (x ? ks.y : ks.x) * __expf(fminf(gm[nt][e] - (x ? gs.y : gs.x), 0.f));
-            Q2[nt][e] = fmaf(dp[hh], w, Q2[nt][e]);
-            K2[nt][e] = fmaf(dk[hh], w, K2[nt][e]);
+            DQ[nt][e] = fmaf(dp[hh], w, DQ[nt][e]);
+            DKp[nt][e] = fmaf(dk[hh], w, DKp[nt][e]);
           }
       }
     }
-    for (int t2 = 16 * mt; t2 < 64; ++t2) {  // M2: sum over t >= s
+    for (int t2 = 16 * mt; t2 < 64; ++t2) {  // dk columns: sum over t >= s
       float dp[2], dk[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -611,18 +610,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
           for (int x = 0; x < 2; ++x) {
             const int e = 2 * hh + x;
             const float w = __expf(fminf((x ? gt.y : gt.x) - gm[nt][e], 0.f));
-            M2[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, M2[nt][e]);
+            DKm[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, DKm[nt][e]);
           }
       }
     }
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        DQ[nt][e] += Q2[nt][e];
-        DKp[nt][e] += K2[nt][e];
-        DKm[nt][e] += M2[nt][e];
-      }
   } else {
     float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {};
     for (int j = 0; j <= mt; ++j) {  // rows t in block mt, columns s in block j
