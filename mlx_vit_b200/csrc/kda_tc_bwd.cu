@@ -293,22 +293,20 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   // a "big" chunk (decay too strong for the factored form) keeps gamma itself and takes exact
   // per-element decay factors in P2, P6 and P8; everything else is the same
   const int big = __syncthreads_or(bigloc);
-  if (tid < 64 && big) eG[tid] = __expf(GS[gsw(63, tid)]);
-  if (tid < 64 && !big) {
-    const int d = tid;
-    const float gC = GS[gsw(63, d)];
-    float r[4];
+  {  // per-block vectors, thread (slot, d): slot i < 4 -> block i's entries, slot 4 -> e^{gamma_C}
+    const int d = tid & 63, slot = tid >> 6;
+    if (slot < 4 && !big) {
+      const int i = slot;
+      const float gC = GS[gsw(63, d)], ri = GS[gsw(i * 16 + 8, d)];
+      refs[i * 64 + d] = ri;
+      erb[i * 64 + d] = __expf(ri);
+      egr[i * 64 + d] = __expf(gC - ri);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = GS[gsw(i * 16 + 8, d)];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      refs[i * 64 + d] = r[i];
-      erb[i * 64 + d] = __expf(r[i]);
-      egr[i * 64 + d] = __expf(gC - r[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j <= i ? __expf(r[i] - r[j]) : 0.f;
+      for (int j = 0; j < 4; ++j)
+        gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + 8, d)]) : (j == i ? 1.f : 0.f);
+    } else if (slot == 4) {
+      eG[d] = __expf(GS[gsw(63, d)]);
     }
-    eG[d] = __expf(gC);
   }
   if (tid == 0) bulk_wait_read_all();  // the previous chunk's output stores have read KD, QD, KF
   __syncthreads();
