@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 1
+#define KDA_ABI_VERSION 2
 
 enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
 
@@ -125,6 +125,40 @@ KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const voi
             const void *saved, const void *dO, const float *dstateT,
             void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
             void *ws, size_t ws_bytes, void *stream);
+
+/* The layer's decay and write gates, fused into the kernels' load path (channel-wise KDA,
+ * GatedDeltaLayer.__call__, nope_gdn_mlx.py:802-816):
+ *   g    = -exp(A_log[h]) * softplus(f + dt_bias[h * Dk + d])   (softplus as :83-86)
+ *   beta = sigmoid(b), times 2 when allow_neg_eigval (:814-816).
+ * f is the gate projection f_proj_2(f_proj_1(x)) as [B, T, H, Dk] in dtype_qkv, b the write-
+ * gate logits b_proj(x) as [B, T, H] in dtype_beta; A_log [H] and dt_bias [H * Dk] are fp32
+ * (the reference keeps them fp32, :4943-4963).  Needs the tensor-core configuration
+ * (Dk = Dv = 64, chunk 64, bf16 q/k/v). */
+typedef struct KdaGate {
+  const void *f;
+  const float *A_log;
+  const float *dt_bias;
+  const void *b;
+  int32_t allow_neg_eigval;
+  int32_t reserved;
+} KdaGate;
+
+/* kda_fwd with the gates computed in-kernel from KdaGate instead of g and beta.
+ * Replaces: GatedDeltaLayer.__call__'s decay / write gate lines (:802-816) followed by the
+ * chunkwise path (see kda_fwd). */
+KDA_API int kda_fwd_gated(const KdaDesc *desc, const void *q, const void *k, const void *v,
+                          const KdaGate *gate, const float *state0, void *o, float *stateT,
+                          void *saved, void *ws, size_t ws_bytes, void *stream);
+
+/* kda_bwd through the fused gates: df (dtype_qkv, [B, T, H, Dk]) and db (dtype_beta,
+ * [B, T, H]) are the cotangents of f and b; dA_log [H] and ddt_bias [H * Dk] (fp32) are
+ * overwritten with the parameter gradients summed over batch and time.
+ * Replaces: the VJP of the same lines (MLX autograd through :802-816) and kda_bwd. */
+KDA_API int kda_bwd_gated(const KdaDesc *desc, const void *q, const void *k, const void *v,
+                          const KdaGate *gate, const float *state0, const void *saved,
+                          const void *dO, const float *dstateT, void *dq, void *dk, void *dv,
+                          void *df, void *db, float *dA_log, float *ddt_bias, float *dstate0,
+                          void *ws, size_t ws_bytes, void *stream);
 
 /* Size of the static device scratch kda_bwd_noalloc uses (32 MiB; enough for about 4000
  * chunks of 64 tokens x heads, e.g. B=8 H=12 T=1568 needs 2400). */

@@ -12,7 +12,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkda_b200.so")
 
-KDA_ABI_VERSION = 1
+KDA_ABI_VERSION = 2
 KDA_F32, KDA_BF16, KDA_F16 = 0, 1, 2
 KDA_FLAG_FORCE_GENERIC = 0x1
 
@@ -26,7 +26,7 @@ KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 # every symbol include/kda_b200.h declares
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
            "kda_saved_bytes", "kda_launch_counter", "kda_device_status", "kda_fwd", "kda_bwd",
-           "kda_bwd_noalloc")
+           "kda_bwd_noalloc", "kda_fwd_gated", "kda_bwd_gated")
 
 
 class KdaDesc(ctypes.Structure):
@@ -34,6 +34,12 @@ class KdaDesc(ctypes.Structure):
                 ("Dk", ctypes.c_int64), ("Dv", ctypes.c_int64), ("chunk", ctypes.c_int64),
                 ("dtype_qkv", ctypes.c_int32), ("dtype_beta", ctypes.c_int32),
                 ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class KdaGate(ctypes.Structure):
+    """The layer's decay / write gate inputs (include/kda_b200.h, KdaGate)."""
+    _fields_ = [("f", ctypes.c_void_p), ("A_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p),
+                ("b", ctypes.c_void_p), ("allow_neg_eigval", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class KdaError(RuntimeError):
@@ -69,6 +75,11 @@ def _declare(L):
     L.kda_bwd.argtypes = [D] + [P] * 15 + [P, S, P]
     L.kda_bwd_noalloc.restype = I
     L.kda_bwd_noalloc.argtypes = [D] + [P] * 15 + [P]
+    G = ctypes.POINTER(KdaGate)
+    L.kda_fwd_gated.restype = I
+    L.kda_fwd_gated.argtypes = [D, P, P, P, G, P, P, P, P, P, S, P]
+    L.kda_bwd_gated.restype = I
+    L.kda_bwd_gated.argtypes = [D, P, P, P, G] + [P] * 12 + [P, S, P]
 
 
 def lib(path: str | None = None):

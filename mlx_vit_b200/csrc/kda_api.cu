@@ -144,4 +144,62 @@ int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 
+static int check_gate(const KdaDesc *d, const KdaGate *gate) {
+  if (!gate || !gate->f || !gate->A_log || !gate->dt_bias || !gate->b) return KDA_ERR_INVALID_ARG;
+  if (!use_tc(d, 1)) return KDA_ERR_UNSUPPORTED;  // the gates are fused into the tensor-core kernels only
+  if (!aligned16(gate->f)) return KDA_ERR_MISALIGNED;
+  return KDA_OK;
+}
+
+static void set_gate(Params &p, const KdaGate *gate) {
+  p.gated = 1;
+  p.beta_scale = gate->allow_neg_eigval ? 2 : 1;
+  p.f = gate->f; p.A_log = gate->A_log; p.dt_bias = gate->dt_bias;
+  p.beta = gate->b;
+}
+
+int kda_fwd_gated(const KdaDesc *d, const void *q, const void *k, const void *v, const KdaGate *gate,
+                  const float *state0, void *o, float *stateT, void *saved, void *ws, size_t ws_bytes,
+                  void *stream) {
+  int s = kda_check_desc(d, 0);
+  if (s) return s;
+  if ((s = check_gate(d, gate))) return s;
+  if (!q || !k || !v || !o || !stateT) return KDA_ERR_INVALID_ARG;
+  const void *ptrs[] = {q, k, v, o, stateT};
+  for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
+  if ((state0 && !aligned16(state0)) || (saved && !aligned16(saved))) return KDA_ERR_MISALIGNED;
+  size_t need = kda_workspace_bytes(d, 0);
+  if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
+  Params p = make_params(d);
+  p.q = q; p.k = k; p.v = v; p.state0 = state0;
+  p.o = o; p.stateT = stateT; p.saved = saved; p.ws = ws;
+  set_gate(p, gate);
+  return kda::tc_fwd(p, d->dtype_beta, (cudaStream_t)stream);
+}
+
+int kda_bwd_gated(const KdaDesc *d, const void *q, const void *k, const void *v, const KdaGate *gate,
+                  const float *state0, const void *saved, const void *dO, const float *dstateT,
+                  void *dq, void *dk, void *dv, void *df, void *db, float *dA_log, float *ddt_bias,
+                  float *dstate0, void *ws, size_t ws_bytes, void *stream) {
+  int s = kda_check_desc(d, 1);
+  if (s) return s;
+  if ((s = check_gate(d, gate))) return s;
+  if (!q || !k || !v || !saved || !dO || !dq || !dk || !dv || !df || !db || !dA_log || !ddt_bias)
+    return KDA_ERR_INVALID_ARG;
+  const void *ptrs[] = {q, k, v, saved, dO, dq, dk, dv, df};
+  for (const void *ptr : ptrs) if (!aligned16(ptr)) return KDA_ERR_MISALIGNED;
+  if ((state0 && !aligned16(state0)) || (dstateT && !aligned16(dstateT)) ||
+      (dstate0 && !aligned16(dstate0)))
+    return KDA_ERR_MISALIGNED;
+  size_t need = kda_workspace_bytes(d, 1);
+  if (need && (!ws || ws_bytes < need || !aligned16(ws))) return KDA_ERR_WORKSPACE;
+  Params p = make_params(d);
+  p.q = q; p.k = k; p.v = v; p.state0 = state0;
+  p.saved_in = saved; p.dO = dO; p.dstateT = dstateT; p.ws = ws;
+  p.dq = dq; p.dk = dk; p.dv = dv; p.dbeta = db; p.dstate0 = dstate0;
+  set_gate(p, gate);
+  p.df = df; p.dA_log = dA_log; p.ddt_bias = ddt_bias;
+  return kda::tc_bwd(p, d->dtype_beta, (cudaStream_t)stream);
+}
+
 }  // extern "C"

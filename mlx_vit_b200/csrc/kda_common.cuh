@@ -26,7 +26,21 @@ struct Params {
   float *stateT, *dg, *dstate0;
   void *saved;                 // forward: per-chunk record for the backward (may be null)
   int *err;                    // optional device error word
+  // fused gates (kda_fwd_gated / kda_bwd_gated): g and beta come from f (dtype_qkv) and the
+  // logits in `beta`; the backward writes df, the logit gradient in `dbeta`, dA_log, ddt_bias
+  int gated, beta_scale;       // beta_scale: 2 with allow_neg_eigval, else 1
+  const void *f;
+  const float *A_log, *dt_bias;
+  void *df;
+  float *dA_log, *ddt_bias;
 };
+
+// softplus as the reference's (nope_gdn_mlx.py:83-86): log1p(e^{-|x|}) + max(x, 0)
+// softplus(x) = max(x, 0) + log(1 + e^-|x|) with the fast intrinsics: the log argument is in
+// (1, 2], where __logf's absolute error is about 2^-21, so g = -A softplus(.) carries an absolute
+// error of a few 1e-7 A (the terms below 2^-24 that 1 + e^-|x| drops are smaller still)
+__device__ __forceinline__ float softplus_f(float x) { return __logf(1.f + __expf(-fabsf(x))) + fmaxf(x, 0.f); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // Per-chunk record the tensor-core forward saves for the tensor-core backward (D = C = 64):
 // S0^T = transposed chunk-entry state [d][j], Unew [t][j], the decay-weighted P = Q K^T (lower incl.) and

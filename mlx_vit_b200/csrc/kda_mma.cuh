@@ -169,4 +169,51 @@ __device__ __forceinline__ void bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;\n" :: "r"(id), "r"(n) : "memory");
 }
 
+// Gate parameters staged once per CTA in shared memory (after the kernel's own layout, 16-byte
+// aligned): dt_bias [H][64] then A_log [H].  Above kGateSmemMaxH heads they stay in global memory.
+constexpr int kGateSmemMaxH = 64;
+__host__ __device__ inline int gate_smem_bytes(int gated, int H) {
+  return gated && H <= kGateSmemMaxH ? H * 65 * 4 : 0;
+}
+// Returns the dt_bias base (A_log follows at +H*64 when staged); the caller syncs the CTA.
+template <typename P>
+__device__ __forceinline__ const float *stage_gate_params(float *gs, const P &p, int tid, int nt,
+                                                          const float **A_log) {
+  if (!p.gated || p.H > kGateSmemMaxH) {
+    *A_log = p.A_log;
+    return p.dt_bias;
+  }
+  for (int i = tid; i < p.H * 65; i += nt) gs[i] = i < p.H * 64 ? p.dt_bias[i] : p.A_log[i - p.H * 64];
+  *A_log = gs + p.H * 64;
+  return gs;
+}
+
+// Fused decay gate: the bf16 tile of the gate pre-activation f (64 rows, 128-byte swizzle) at
+// `raw` becomes g = -exp(A_log[h]) softplus(f + dt_bias[h, d]) in fp32 over `G` (gsw layout;
+// `in_place`: the first half of G is `raw` itself).  Rows from `nvalid` on (past the sequence
+// end) get g = 0.  Thread `tid` < 512 converts 8 elements; the caller synchronises the CTA after
+// the call.
+__device__ __forceinline__ void gate_to_g(const uint8_t *raw, float *G, const float *A_log,
+                                          const float *dt_bias, int h, int nvalid, int tid,
+                                          bool in_place) {
+  const int t = tid >> 3, c0 = (tid & 7) * 8;
+  const uint4 u = *reinterpret_cast<const uint4 *>(raw + sw64(t, c0));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  const float A = __expf(A_log[h]);
+  const float *db = dt_bias + h * 64 + c0;
+  float g[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = unpack_bf16(w[e]);
+    g[2 * e] = -A * softplus_f(f.x + db[2 * e]);
+    g[2 * e + 1] = -A * softplus_f(f.y + db[2 * e + 1]);
+  }
+  if (t >= nvalid)  // rows past the sequence end carry no decay (their f is the TMA zero fill)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) g[e] = 0.f;
+  if (in_place) __syncthreads();  // every thread has read its f before G overwrites the tile
+  *reinterpret_cast<float4 *>(G + gsw(t, c0)) = make_float4(g[0], g[1], g[2], g[3]);
+  *reinterpret_cast<float4 *>(G + gsw(t, c0 + 4)) = make_float4(g[4], g[5], g[6], g[7]);
+}
+
 }  // namespace kda

@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
   const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
   __nv_bfloat16 *ds_exit = (__nv_bfloat16 *)p.ws;
+  if (p.gated && bh == 0)  // the gate-parameter gradients are accumulated by the chunk kernel,
+    for (int i = tid; i < p.H * 65; i += SC_NT)  // which runs after this one on the stream
+      (i < p.H * 64 ? p.ddt_bias[i] : p.dA_log[i - p.H * 64]) = 0.f;
   if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_MISALIGNED);
     return;
@@ -177,13 +180,15 @@ constexpr int O_S0 = 49152, O_UN = 57344, O_PB = 65536, O_MK = 73728, O_TF = 819
 constexpr int O_DS = 90112;                                         // dS1 [j][d]
 constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
 constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
-constexpr int O_VEC = 155648;
+constexpr int O_FS = 155648;                                        // fused gates: raw f tile (bf16)
+constexpr int O_VEC = 163840;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
               V_EG = 2368, V_PDB = 2432, V_PDG = 3200, V_FLAG = 3968;
 // partial sums, each slot written by exactly one thread (no atomics): dbeta rows from P5, P6, P7
 // [3][4 column warps][64], dGamma_C columns from the state term [8] and P6 [4] ([12][64])
 constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // three mbarriers
 constexpr int CK_SMEM = O_MBAR + 24;
+constexpr int CK_SMEM_GP = (CK_SMEM + 15) & ~15;                  // staged gate parameters
 
 template <typename Tb>
 __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
@@ -222,9 +227,12 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       bulk_g2s(s_base + O_PB, rec_ + kSavedP, 8192, mb);
       bulk_g2s(s_base + O_TF, rec_ + kSavedTinv, 8192, mb);
     } else if (stage == 1) {
-      mbar_expect_tx(mb, 5 * 8192 + 16384);
+      mbar_expect_tx(mb, 5 * 8192 + (p.gated ? 8192 : 16384));
       tma_load_rows(s_base + O_DO, &tm.m[3], h_, t0_, b_, mb);
-      tma_load_rows_f32(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
+      if (p.gated)  // the gate pre-activation f (bf16) into the first half of GS
+        tma_load_rows(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
+      else
+        tma_load_rows_f32(s_base + O_GS, &tm.m[4], h_, t0_, b_, mb);
       bulk_g2s(s_base + O_S0, rec_ + kSavedS0, 2 * 8192, mb);
       bulk_g2s(s_base + O_MK, rec_ + kSavedMkk, 8192, mb);
       bulk_g2s(s_base + O_DS, (const __nv_bfloat16 *)p.ws + (int64_t)i * D * D, 8192, mb);
@@ -243,6 +251,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     for (int i = 0; i < 3; ++i) mbar_init(mbar + 8 * i, 1);
     mbar_fence_init();
   }
+  const float *gA_log;
+  const float *gdtb = stage_gate_params(reinterpret_cast<float *>(sm + CK_SMEM_GP), p, tid, CK_NT, &gA_log);
   __syncthreads();
   int idx = blockIdx.x;
   if (idx < nchunks)
@@ -259,8 +269,14 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
     break;
   }
-  if (tid < C) {
-    bet[tid] = to_f(beta_next);
+  const int nvalid = min(C, T - t0);
+  if (tid < C)
+    bet[tid] = !p.gated ? to_f(beta_next) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_next)) : 0.f;
+  if (p.gated) {  // keep the raw f tile for the gate's VJP, then g over GS
+    const uint32_t o = sw64(tid >> 3, (tid & 7) * 8);
+    *reinterpret_cast<uint4 *>(sm + O_FS + o) = *reinterpret_cast<const uint4 *>(sm + O_GS + o);
+    gate_to_g(sm + O_GS, GS, gA_log, gdtb, h, nvalid, tid, true);
+    __syncthreads();
   }
   if (inext < nchunks && tid < C) beta_next = load_beta(inext);
   // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
@@ -710,23 +726,59 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
     for (int s2 = 0; s2 < 12; ++s2) acc += pdg[s2 * 64 + d];
     for (int s2 = seg + 1; s2 < 8; ++s2) acc += part[s2 * 64 + d];
+    if (!p.gated) {
 #pragma unroll
-    for (int r = 7; r >= 0; --r) {
-      const int t = seg * 8 + r;
-      acc += DG[gsw(t, d)];
-      DG[gsw(t, d)] = acc;
+      for (int r = 7; r >= 0; --r) {
+        const int t = seg * 8 + r;
+        acc += DG[gsw(t, d)];
+        DG[gsw(t, d)] = acc;
+      }
+    } else {  // through the gate: df = dg (-A) sigmoid(x), dA_log += dg g, ddt_bias += df
+      const float A = __expf(gA_log[h]), xb = gdtb[h * 64 + d];
+      float pa = 0.f, pt = 0.f;
+#pragma unroll
+      for (int r = 7; r >= 0; --r) {
+        const int t = seg * 8 + r;
+        acc += DG[gsw(t, d)];
+        const float x = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_FS + sw64(t, d))) + xb;
+        const float df = t0 + t < T ? -A * acc * sigmoid_f(x) : 0.f;
+        pa += t0 + t < T ? -A * acc * softplus_f(x) : 0.f;
+        pt += df;
+        *reinterpret_cast<__nv_bfloat16 *>(sm + O_DR + sw64(t, d)) = __float2bfloat16_rn(df);
+      }
+      __syncthreads();  // every thread has read pdg and part
+      pdg[seg * 64 + d] = pt;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) pa += __shfl_xor_sync(0xffffffffu, pa, o);
+      if (lane == 0) part[warp] = pa;
+      __syncthreads();
+      if (tid < 64) {
+        float sdt = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) sdt += pdg[s2 * 64 + tid];
+        atomicAdd(p.ddt_bias + h * 64 + tid, sdt);
+      }
+      if (tid == 0) {
+        float sa = 0.f;
+        for (int w = 0; w < CK_NT / 32; ++w) sa += part[w];
+        atomicAdd(p.dA_log + h, sa);
+      }
     }
     if (tid < 64 && t0 + tid < T) {
       float db = 0.f;
 #pragma unroll
       for (int s2 = 0; s2 < 12; ++s2) db += pdb[s2 * 64 + tid];
+      if (p.gated) db *= bet[tid] * (1.f - bet[tid] / p.beta_scale);  // through beta = s sigmoid(b)
       ((Tb *)p.dbeta)[((int64_t)b * T + t0 + tid) * H + h] = from_f<Tb>(db);
     }
   }
   fence_proxy_async_smem();
   __syncthreads();
   if (tid == 0) {
-    tma_store_rows_f32(&tm.m[7], s_base + O_KF, h, t0, b);
+    if (p.gated)
+      tma_store_rows(&tm.m[7], s_base + O_DR, h, t0, b);  // df (bf16)
+    else
+      tma_store_rows_f32(&tm.m[7], s_base + O_KF, h, t0, b);
     bulk_commit();
   }
   }  // chunk loop
@@ -736,9 +788,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
   TmaMaps tm;  // 0 q, 1 k, 2 v, 3 dO, 4 g (loads); 5 dq, 6 dk, 7 dg (stores)
-  const void *base[8] = {p.q, p.k, p.v, p.dO, p.g, p.dq, p.dk, p.dg};
+  const void *base[8] = {p.q, p.k, p.v, p.dO, p.gated ? p.f : (const void *)p.g, p.dq, p.dk,
+                         p.gated ? p.df : (void *)p.dg};
   for (int i = 0; i < 8; ++i)
-    if (int e = tma_map_bthd(&tm.m[i], base[i], p.B, p.T, p.H, D, i == 4 || i == 7)) return e;
+    if (int e = tma_map_bthd(&tm.m[i], base[i], p.B, p.T, p.H, D, (i == 4 || i == 7) && !p.gated)) return e;
   TmaMaps tms;
   tms.m[0] = tm.m[3];
   if (cudaFuncSetAttribute(kda_bwd_state_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM))
@@ -746,13 +799,14 @@ int launch(const Params &p, cudaStream_t st) {
   kda_bwd_state_scan_kernel<<<p.B * p.H, SC_NT, SC_SMEM, st>>>(p, tms);
   count_launch();
   auto kern = kda_bwd_chunks_kernel<Tb>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_SMEM)) return KDA_ERR_CUDA;
+  const int ck_smem = CK_SMEM_GP + gate_smem_bytes(p.gated, p.H);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ck_smem)) return KDA_ERR_CUDA;
   const int n = p.B * p.H * p.nc;
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return KDA_ERR_CUDA;
-  kern<<<n < nsm ? n : nsm, CK_NT, CK_SMEM, st>>>(p, tm);
+  kern<<<n < nsm ? n : nsm, CK_NT, ck_smem, st>>>(p, tm);
   count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }

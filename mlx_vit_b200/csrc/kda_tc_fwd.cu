@@ -71,6 +71,9 @@ constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V
               V_FLAG = 2368;
 constexpr int OFF_MBAR1 = OFF_VEC + (2368 + 4) * 4;      // mbarrier of the TMA loads
 constexpr int SMEM1 = OFF_MBAR1 + 8;
+// fused gates only: the raw f tile (TMA, bf16), then the staged gate parameters
+constexpr int OFF_FS1 = (SMEM1 + 1023) & ~1023;
+constexpr int SMEM1_GP = OFF_FS1 + 8192;
 
 __device__ __forceinline__ int ki_index(int i, int j) { return i * (i + 1) / 2 + j; }
 
@@ -156,15 +159,20 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     mbar_init(mbar, 1);
     mbar_fence_init();
   }
+  const float *gA_log;
+  const float *gdtb = stage_gate_params(reinterpret_cast<float *>(sm + SMEM1_GP), p, tid, NT1, &gA_log);
   __syncthreads();
   auto issue_loads = [&](int i) {  // q, k, v tiles (swizzled) and g (fp32) of chunk i
     if (tid == 0) {
       const int bh_ = i / nc, t0_ = (i % nc) * C, b_ = bh_ / H, h_ = bh_ % H;
-      mbar_expect_tx(mbar, 3 * 8192 + 16384);
+      mbar_expect_tx(mbar, 3 * 8192 + (p.gated ? 8192 : 16384));
       tma_load_rows(s_base + OFF_QS, &tm.m[0], h_, t0_, b_, mbar);
       tma_load_rows(s_base + OFF_KS, &tm.m[1], h_, t0_, b_, mbar);
       tma_load_rows(s_base + OFF_VS, &tm.m[2], h_, t0_, b_, mbar);
-      tma_load_rows_f32(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
+      if (p.gated)  // the gate pre-activation f (bf16), converted into GS
+        tma_load_rows(s_base + OFF_FS1, &tm.m[3], h_, t0_, b_, mbar);
+      else
+        tma_load_rows_f32(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
     }
   };
   // beta of the next chunk, kept raw until its use so that the load does not stall anyone
@@ -188,7 +196,10 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
     break;
   }
-  if (tid < C) bet[tid] = to_f(beta_next);
+  const int nvalid = min(C, T - (idx % nc) * C);
+  if (tid < C)
+    bet[tid] = !p.gated ? to_f(beta_next) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_next)) : 0.f;
+  if (p.gated) gate_to_g(sm + OFF_FS1, GS, gA_log, gdtb, idx / nc % H, nvalid, tid, false);
   __syncthreads();
 
   // ---- (1a) gamma = cumsum(g): 8 segments of 8 rows per channel ----
@@ -753,17 +764,18 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
 template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
   auto k1 = kda_fwd_chunks_kernel<Tb>;
-  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1)) return KDA_ERR_CUDA;
+  const int smem1 = p.gated ? SMEM1_GP + gate_smem_bytes(p.gated, p.H) : SMEM1;
+  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1)) return KDA_ERR_CUDA;
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return KDA_ERR_CUDA;
   const int nchunks = p.B * p.H * p.nc;
   TmaMaps tm;
-  const void *srcs[4] = {p.q, p.k, p.v, p.g};
+  const void *srcs[4] = {p.q, p.k, p.v, p.gated ? p.f : (const void *)p.g};
   for (int i = 0; i < 4; ++i)
-    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3)) return e;
-  k1<<<nchunks < nsm ? nchunks : nsm, NT1, SMEM1, st>>>(p, tm);
+    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3 && !p.gated)) return e;
+  k1<<<nchunks < nsm ? nchunks : nsm, NT1, smem1, st>>>(p, tm);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
     return KDA_ERR_CUDA;

@@ -192,3 +192,119 @@ def cuda_kda(q, k, v, g, beta, state: Optional[torch.Tensor] = None, chunk_size:
         return CudaKdaFunction.apply(q, k, v, g, beta, state, chunk_size, flags)
     o, S_T, _ = kda_forward(q, k, v, g, beta, state, chunk_size, save_states=False, flags=flags)
     return o, S_T
+
+
+def _gate_struct(f, A_log, dt_bias, b, allow_neg_eigval):
+    return _lib.KdaGate(ctypes.c_void_p(f.data_ptr()), ctypes.c_void_p(A_log.data_ptr()),
+                        ctypes.c_void_p(dt_bias.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                        int(bool(allow_neg_eigval)), 0)
+
+
+def kda_forward_gated(q, k, v, f, A_log, dt_bias, b, state=None, chunk_size=64,
+                      allow_neg_eigval=False, save_states=False):
+    """One ``kda_fwd_gated`` call: the decay gate g = -exp(A_log) softplus(f + dt_bias) and
+    the write gate beta = s sigmoid(b) are computed inside the chunk kernel
+    (nope_gdn_mlx.py:802-816).  Returns (o, S_T, saved | None)."""
+    L = _lib.lib()
+    desc = _desc(q, b, chunk_size, 0)
+    o = torch.empty_like(q)
+    B, T, H, D = q.shape
+    S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
+    cs = None
+    if save_states:
+        cs = torch.empty(L.kda_saved_bytes(ctypes.byref(desc)), dtype=torch.uint8, device=q.device)
+    ws, nws = _workspace(desc, 0, q.device)
+    gate = _gate_struct(f, A_log, dt_bias, b, allow_neg_eigval)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream().cuda_stream
+        st = L.kda_fwd_gated(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), ctypes.byref(gate),
+                             _ptr(state), _ptr(o), _ptr(S_T), _ptr(cs), _ptr(ws), nws,
+                             ctypes.c_void_p(stream))
+    _lib.check(st, "kda_fwd_gated")
+    return o, S_T, cs
+
+
+def kda_backward_gated(q, k, v, f, A_log, dt_bias, b, state, saved, do, dstate=None,
+                       chunk_size=64, allow_neg_eigval=False, want_dstate0=True):
+    """One ``kda_bwd_gated`` call.  Returns (dq, dk, dv, df, db, dA_log, ddt_bias,
+    dstate0 | None): the VJP of the recurrence chained through both gates."""
+    L = _lib.lib()
+    desc = _desc(q, b, chunk_size, 0)
+    B, T, H, D = q.shape
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    df = torch.empty_like(f)
+    db = torch.empty_like(b)
+    dA = torch.empty((H,), dtype=torch.float32, device=q.device)
+    ddtb = torch.empty((H * D,), dtype=torch.float32, device=q.device)
+    ds0 = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device) if want_dstate0 else None
+    ws, nws = _workspace(desc, 1, q.device)
+    gate = _gate_struct(f, A_log, dt_bias, b, allow_neg_eigval)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream().cuda_stream
+        st = L.kda_bwd_gated(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), ctypes.byref(gate),
+                             _ptr(state), _ptr(saved), _ptr(do), _ptr(dstate), _ptr(dq), _ptr(dk),
+                             _ptr(dv), _ptr(df), _ptr(db), _ptr(dA), _ptr(ddtb), _ptr(ds0),
+                             _ptr(ws), nws, ctypes.c_void_p(stream))
+    _lib.check(st, "kda_bwd_gated")
+    return dq, dk, dv, df, db, dA, ddtb, ds0
+
+
+class CudaKdaGatedFunction(torch.autograd.Function):
+    """Autograd wiring of ``kda_fwd_gated`` / ``kda_bwd_gated``: the gate lines of
+    ``GatedDeltaLayer.__call__`` (nope_gdn_mlx.py:802-816) and the recurrence as one op."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, f, A_log, dt_bias, b, state, chunk_size, allow_neg_eigval):
+        o, S_T, cs = kda_forward_gated(q, k, v, f, A_log, dt_bias, b, state, chunk_size,
+                                       allow_neg_eigval, save_states=True)
+        ctx.save_for_backward(q, k, v, f, A_log, dt_bias, b, state, cs)
+        ctx.chunk_size, ctx.allow_neg = chunk_size, allow_neg_eigval
+        ctx.has_state = state is not None
+        return o, S_T
+
+    @staticmethod
+    def backward(ctx, do, dS_T):
+        q, k, v, f, A_log, dt_bias, b, state, cs = ctx.saved_tensors
+        do = torch.zeros_like(q) if do is None else do.to(q.dtype).contiguous()
+        dS_T = None if dS_T is None else dS_T.float().contiguous()
+        dq, dk, dv, df, db, dA, ddtb, ds0 = kda_backward_gated(
+            q, k, v, f, A_log, dt_bias, b, state, cs, do, dS_T, ctx.chunk_size, ctx.allow_neg,
+            want_dstate0=ctx.has_state)
+        return dq, dk, dv, df, dA, ddtb, db, ds0, None, None
+
+
+def cuda_kda_gated(q, k, v, f, A_log, dt_bias, b, state: Optional[torch.Tensor] = None,
+                   chunk_size: int = 64, allow_neg_eigval: bool = False
+                   ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Channel-wise KDA with both gates fused into the chunk kernels.
+
+    ``f`` is the decay projection output (B, L, H, D) in q's dtype (bf16), ``A_log`` (H,)
+    and ``dt_bias`` (H*D,) are float32 parameters, ``b`` is the write-gate projection
+    output (B, L, H).  Equivalent to ``cuda_kda(q, k, v, g, beta, state)`` with
+    g = -exp(A_log) softplus(f + dt_bias) and beta = (2 if allow_neg_eigval else 1) sigmoid(b)
+    (nope_gdn_mlx.py:802-816), without materialising g or beta.  bf16 q/k/v/f only.
+    """
+    q, k, v, f, A_log, dt_bias, b, state = (
+        _as_torch(x, n) for x, n in ((q, "q"), (k, "k"), (v, "v"), (f, "f"), (A_log, "A_log"),
+                                     (dt_bias, "dt_bias"), (b, "b"), (state, "state")))
+    if q.dim() != 4:
+        raise ValueError(f"q must be (B, L, H, D), got {tuple(q.shape)}")
+    B, T, H, D = q.shape
+    _check_shapes(q, k, v, f, b, state)
+    if q.dtype != torch.bfloat16 or f.dtype != torch.bfloat16:
+        raise ValueError("cuda_kda_gated needs bf16 q, k, v and f")
+    if tuple(A_log.shape) != (H,) or tuple(dt_bias.shape) not in ((H * D,), (H, D)):
+        raise ValueError(f"A_log must be ({H},) and dt_bias ({H * D},)")
+    q, k, v, f, b = (x.contiguous() for x in (q, k, v, f, b))
+    A_log = A_log.to(torch.float32).contiguous()
+    dt_bias = dt_bias.to(torch.float32).reshape(H * D).contiguous()
+    if state is not None:
+        state = state.to(torch.float32).contiguous()
+    need_grad = torch.is_grad_enabled() and any(
+        x is not None and x.requires_grad for x in (q, k, v, f, A_log, dt_bias, b, state))
+    if need_grad:
+        return CudaKdaGatedFunction.apply(q, k, v, f, A_log, dt_bias, b, state, chunk_size,
+                                          allow_neg_eigval)
+    o, S_T, _ = kda_forward_gated(q, k, v, f, A_log, dt_bias, b, state, chunk_size,
+                                  allow_neg_eigval)
+    return o, S_T

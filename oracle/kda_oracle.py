@@ -165,3 +165,41 @@ def chunkwise_forward(q, k, v, g, beta, state=None, chunk=64, dtype=np.float64):
         S = np.exp(gam[:, :, -1, :])[..., None, :] * S + np.swapaxes(U, -1, -2) @ Kb
         o[:, sl] = O.transpose(0, 2, 1, 3)
     return o[:, :T], S, states
+
+
+def softplus(x):
+    """Stable softplus log(1 + e^x) = log1p(e^-|x|) + max(x, 0) (nope_gdn_mlx.py:83-86)."""
+    return np.log1p(np.exp(-np.abs(x))) + np.maximum(x, 0.0)
+
+
+def _sigmoid(x):
+    return 0.5 * (1.0 + np.tanh(0.5 * x))
+
+
+def gates(f, A_log, dt_bias, b, allow_neg_eigval=False, dtype=np.float64):
+    """Decay and write gates of the channel-wise layer (nope_gdn_mlx.py:802-816):
+    g = -exp(A_log[h]) * softplus(f + dt_bias[h, :]),  beta = s * sigmoid(b), s = 2 if
+    allow_neg_eigval else 1.  f: (B, T, H, D); A_log: (H,); dt_bias: (H*D,); b: (B, T, H)."""
+    B, T, H, D = f.shape
+    x = f.astype(dtype) + dt_bias.astype(dtype).reshape(H, D)
+    g = -np.exp(A_log.astype(dtype)).reshape(1, 1, H, 1) * softplus(x)
+    beta = (2.0 if allow_neg_eigval else 1.0) * _sigmoid(b.astype(dtype))
+    return g, beta
+
+
+def gates_vjp(f, A_log, dt_bias, b, dg, dbeta, allow_neg_eigval=False, dtype=np.float64):
+    """Chain rule through ``gates``: returns (df, dA_log, ddt_bias, db).
+
+    d g / d x = -exp(A_log) * sigmoid(x) (softplus' = sigmoid), d g / d A_log = g,
+    d beta / d b = beta * (1 - beta / s)."""
+    B, T, H, D = f.shape
+    x = f.astype(dtype) + dt_bias.astype(dtype).reshape(H, D)
+    A = np.exp(A_log.astype(dtype)).reshape(1, 1, H, 1)
+    g = -A * softplus(x)
+    df = dg.astype(dtype) * (-A) * _sigmoid(x)
+    dA_log = (dg.astype(dtype) * g).sum(axis=(0, 1, 3))
+    ddt_bias = df.sum(axis=(0, 1)).reshape(H * D)
+    s = 2.0 if allow_neg_eigval else 1.0
+    beta = s * _sigmoid(b.astype(dtype))
+    db = dbeta.astype(dtype) * beta * (1.0 - beta / s)
+    return df, dA_log, ddt_bias, db
