@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace kda {
@@ -191,23 +192,43 @@ __device__ __forceinline__ const float *stage_gate_params(float *gs, const P &p,
 // Fused decay gate: the bf16 tile of the gate pre-activation f (64 rows, 128-byte swizzle) at
 // `raw` becomes g = -exp(A_log[h]) softplus(f + dt_bias[h, d]) in fp32 over `G` (gsw layout;
 // `in_place`: the first half of G is `raw` itself).  Rows from `nvalid` on (past the sequence
-// end) get g = 0.  Thread `tid` < 512 converts 8 elements; the caller synchronises the CTA after
-// the call.
+// end) get g = 0.  With `sg` (the backward), {sigmoid(x), softplus(x)} of x = f + dt_bias go there
+// as half2, row-major [t][d], for the gate's VJP.  Thread `tid` < 512 converts 8 elements; the
+// caller synchronises the CTA after the call.
 __device__ __forceinline__ void gate_to_g(const uint8_t *raw, float *G, const float *A_log,
                                           const float *dt_bias, int h, int nvalid, int tid,
-                                          bool in_place) {
+                                          bool in_place, __half2 *sg = nullptr) {
   const int t = tid >> 3, c0 = (tid & 7) * 8;
   const uint4 u = *reinterpret_cast<const uint4 *>(raw + sw64(t, c0));
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
   const float A = __expf(A_log[h]);
   const float *db = dt_bias + h * 64 + c0;
-  float g[8];
+  float g[8], sig[8];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const float2 f = unpack_bf16(w[e]);
-    g[2 * e] = -A * softplus_f(f.x + db[2 * e]);
-    g[2 * e + 1] = -A * softplus_f(f.y + db[2 * e + 1]);
+    const float x[2] = {f.x + db[2 * e], f.y + db[2 * e + 1]};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {  // softplus(x) = max(x, 0) + log(1 + e^-|x|), sigmoid from e^-|x|
+      const float ex = __expf(-fabsf(x[j])), r = __fdividef(1.f, 1.f + ex);
+      const float sp = __logf(1.f + ex) + fmaxf(x[j], 0.f);
+      g[2 * e + j] = sp;
+      sig[2 * e + j] = x[j] >= 0.f ? r : ex * r;
+    }
   }
+  if (sg) {
+    uint32_t hw[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const __half2 v = __floats2half2_rn(sig[e], g[e]);
+      hw[e] = *reinterpret_cast<const uint32_t *>(&v);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(sg + t * 64 + c0);
+    dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) g[e] *= -A;
   if (t >= nvalid)  // rows past the sequence end carry no decay (their f is the TMA zero fill)
 #pragma unroll
     for (int e = 0; e < 8; ++e) g[e] = 0.f;

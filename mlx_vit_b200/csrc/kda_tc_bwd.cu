@@ -180,10 +180,11 @@ constexpr int O_S0 = 49152, O_UN = 57344, O_PB = 65536, O_MK = 73728, O_TF = 819
 constexpr int O_DS = 90112;                                         // dS1 [j][d]
 constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
 constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
-constexpr int O_FS = 155648;                                        // fused gates: raw f tile (bf16)
-constexpr int O_VEC = 163840;
+constexpr int O_SG = 155648;                                        // fused gates: {sigmoid, softplus}(x) half2 [t][d]
+constexpr int O_VEC = 172032;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
-              V_EG = 2368, V_PDB = 2432, V_PDG = 3200, V_FLAG = 3968;
+              V_EG = 2368, V_PDB = 2432, V_PDG = 3200, V_GPT = 3968, V_GPA = 4480,
+              V_FLAG = 4496;
 // partial sums, each slot written by exactly one thread (no atomics): dbeta rows from P5, P6, P7
 // [3][4 column warps][64], dGamma_C columns from the state term [8] and P6 [4] ([12][64])
 constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // three mbarriers
@@ -272,10 +273,8 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   const int nvalid = min(C, T - t0);
   if (tid < C)
     bet[tid] = !p.gated ? to_f(beta_next) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_next)) : 0.f;
-  if (p.gated) {  // keep the raw f tile for the gate's VJP, then g over GS
-    const uint32_t o = sw64(tid >> 3, (tid & 7) * 8);
-    *reinterpret_cast<uint4 *>(sm + O_FS + o) = *reinterpret_cast<const uint4 *>(sm + O_GS + o);
-    gate_to_g(sm + O_GS, GS, gA_log, gdtb, h, nvalid, tid, true);
+  if (p.gated) {  // g over GS; sigmoid and softplus of the gate input kept for the VJP
+    gate_to_g(sm + O_GS, GS, gA_log, gdtb, h, nvalid, tid, true, reinterpret_cast<__half2 *>(sm + O_SG));
     __syncthreads();
   }
   if (inext < nchunks && tid < C) beta_next = load_beta(inext);
@@ -734,35 +733,24 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
         DG[gsw(t, d)] = acc;
       }
     } else {  // through the gate: df = dg (-A) sigmoid(x), dA_log += dg g, ddt_bias += df
-      const float A = __expf(gA_log[h]), xb = gdtb[h * 64 + d];
+      // (partials into their own slots; summed after the barrier below)
+      const __half2 *sgt = reinterpret_cast<const __half2 *>(sm + O_SG);
+      const float A = __expf(gA_log[h]);
       float pa = 0.f, pt = 0.f;
 #pragma unroll
       for (int r = 7; r >= 0; --r) {
         const int t = seg * 8 + r;
         acc += DG[gsw(t, d)];
-        const float x = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + O_FS + sw64(t, d))) + xb;
-        const float df = t0 + t < T ? -A * acc * sigmoid_f(x) : 0.f;
-        pa += t0 + t < T ? -A * acc * softplus_f(x) : 0.f;
+        const float2 ss = __half22float2(sgt[t * 64 + d]);
+        const float df = t0 + t < T ? -A * acc * ss.x : 0.f;
+        pa += t0 + t < T ? acc * ss.y : 0.f;
         pt += df;
         *reinterpret_cast<__nv_bfloat16 *>(sm + O_DR + sw64(t, d)) = __float2bfloat16_rn(df);
       }
-      __syncthreads();  // every thread has read pdg and part
-      pdg[seg * 64 + d] = pt;
+      vec[V_GPT + seg * 64 + d] = pt;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) pa += __shfl_xor_sync(0xffffffffu, pa, o);
-      if (lane == 0) part[warp] = pa;
-      __syncthreads();
-      if (tid < 64) {
-        float sdt = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < 8; ++s2) sdt += pdg[s2 * 64 + tid];
-        atomicAdd(p.ddt_bias + h * 64 + tid, sdt);
-      }
-      if (tid == 0) {
-        float sa = 0.f;
-        for (int w = 0; w < CK_NT / 32; ++w) sa += part[w];
-        atomicAdd(p.dA_log + h, sa);
-      }
+      if (lane == 0) vec[V_GPA + warp] = -A * pa;
     }
     if (tid < 64 && t0 + tid < T) {
       float db = 0.f;
@@ -780,6 +768,19 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     else
       tma_store_rows_f32(&tm.m[7], s_base + O_KF, h, t0, b);
     bulk_commit();
+  }
+  if (p.gated) {  // this chunk's shares of ddt_bias and dA_log
+    if (tid >= 64 && tid < 128) {
+      float sdt = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) sdt += vec[V_GPT + s2 * 64 + tid - 64];
+      atomicAdd(p.ddt_bias + h * 64 + tid - 64, sdt);
+    } else if (tid == 128) {
+      float sa = 0.f;
+#pragma unroll
+      for (int w = 0; w < CK_NT / 32; ++w) sa += vec[V_GPA + w];
+      atomicAdd(p.dA_log + h, sa);
+    }
   }
   }  // chunk loop
   if (tid == 0) bulk_wait_all();  // shared memory stays valid until the stores have read it
