@@ -1,14 +1,14 @@
 // Tensor-core KDA forward for D = 64, chunk = 64, bf16 q/k/v, in two kernels.
 //
-//  kda_fwd_chunks  one CTA per (b, h, chunk), all independent (fills all SMs): every
-//                  state-independent quantity of the chunk, written as a per-chunk record
+//  kda_fwd_chunks  one persistent CTA per SM walking all (b, h, chunk), which are independent:
+//                  every state-independent quantity of the chunk, written as a per-chunk record
 //                  (-W, U, Qd, Kb, P as bf16 tiles, e^{gamma_C}) to the forward workspace,
 //                  and, for training, the state-independent part of the backward's record
 //                  (P, M, Tinv = (I+A)^{-1}, Mneg = -Kb^T W, Qt = Qd - P W).
-//  kda_fwd_scan    one CTA of 4 warps per (b, h): streams the chunk records (bulk copies, two
-//                  chunks ahead) and advances the fp32 state, which each warp keeps as 16 rows of
-//                  mma accumulator registers:
-//                    Unew^T = U^T - S W^T;  O^T = S Qd^T + Unew^T P^T;  S <- S diag(e^{gamma_C}) + Unew^T Kb
+//  kda_fwd_scan    one CTA of 5 warps per (b, h): streams the chunk records (bulk copies, two
+//                  chunks ahead) and advances the state with two tcgen05 MMAs per chunk into one
+//                  M = 128 TMEM accumulator (the fp32 state itself stays in registers):
+//                    Unew = U - W S^T;  O = Qd S^T + P Unew;  S^T <- diag(e^{gamma_C}) S^T + Kb^T Unew
 //
 // Chunk quantities (gamma = cumsum(g) inside the chunk, rows t, 16-row blocks b(t), r_i = gamma
 // at the middle row of block i):
