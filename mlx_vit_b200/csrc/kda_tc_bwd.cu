@@ -24,6 +24,7 @@
 // kSpanMax across half a 16-row block in some channel) take exact per-element decay factors in
 // the same kernel.
 #include <mutex>
+#include <type_traits>
 
 #include "kda_common.cuh"
 #include "kda_mma.cuh"
@@ -39,6 +40,7 @@ static __device__ int g_bwd_status;
 
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
+constexpr float kLog2e = 1.4426950408889634f;  // the big-chunk copy of gamma is kept in log2 units
 
 // workspace: the exit cotangent of every chunk (bf16 [j][d], swizzled)
 __host__ __device__ inline size_t ws_bytes(int64_t nchunks) { return (size_t)nchunks * 8192; }
@@ -181,7 +183,8 @@ constexpr int O_DS = 90112;                                         // dS1 [j][d
 constexpr int O_KD = 98304, O_QD = 106496, O_KF = 114688, O_KB = 122880;
 constexpr int O_DR = 131072, O_DP = 139264, O_DK = 147456;
 constexpr int O_SG = 155648;                                        // fused gates: {sigmoid, softplus}(x) half2 [t][d]
-constexpr int O_VEC = 172032;
+constexpr int O_GB = 172032;                                        // big chunks: gamma (fp32, gsw) for P8
+constexpr int O_VEC = 188416;
 constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
               V_EG = 2368, V_PDB = 2432, V_PDG = 3200, V_GPT = 3968, V_GPA = 4480,
               V_FLAG = 4496;
@@ -319,6 +322,11 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + 8, d)]) : (j == i ? 1.f : 0.f);
+    } else if (slot < 4) {  // big: G_ij = e^{gamma(start of i) - gamma(end of j)} <= 1, j < i
+      const int i = slot;
+      const float si = GS[gsw(i * 16, d)];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gij[(i * 4 + j) * 64 + d] = j < i ? __expf(si - GS[gsw(j * 16 + 15, d)]) : 0.f;
     } else if (slot == 4) {
       eG[d] = __expf(GS[gsw(63, d)]);
     }
@@ -326,26 +334,39 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   if (tid == 0) bulk_wait_read_all();  // the previous chunk's output stores have read KD, QD, KF
   __syncthreads();
 
-  // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma};
-  //      a big chunk builds KB only, with exact factors, and keeps a copy of gamma over the KD
-  //      and QD tiles for P8 (GS is reloaded before P8) ----
-  float *GB = reinterpret_cast<float *>(sm + O_KD);
+  // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma}.
+  //      A big chunk factors e^{gamma_t - gamma_s} (t in block i > j, the block of s) as
+  //      A_t G_ij B_s, every factor <= 1: KD = k A, QD = q A with A_t = e^{gamma_t - gamma(start
+  //      of t's block)}, KF = k B with B_s = e^{gamma(end of s's block) - gamma_s}; its diagonal
+  //      blocks take exact factors in P8 from a copy of gamma (GS is reloaded before P8) ----
+  float *GB = reinterpret_cast<float *>(sm + O_GB);
   if (big) {
     for (int u = tid; u < 512; u += CK_NT) {
-      const int t = u >> 3, ch = u & 7, d0 = ch * 8;
+      const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
       const uint32_t off = sw64(t, d0);
       const uint4 kq = *reinterpret_cast<const uint4 *>(sm + O_KS + off);
-      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w};
-      uint32_t okb[4];
+      const uint4 qq = *reinterpret_cast<const uint4 *>(sm + O_QS + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+      uint32_t okd[4], oqd[4], okf[4], okb[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float2 kf = unpack_bf16(kw[e]);
+        const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
         const int d = d0 + 2 * e;
         const float2 gm = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
         const float2 gc = *reinterpret_cast<const float2 *>(GS + gsw(63, d));
-        *reinterpret_cast<float2 *>(GB + gsw(t, d)) = gm;
+        const float2 gs = *reinterpret_cast<const float2 *>(GS + gsw(16 * blk, d));
+        const float2 ge = *reinterpret_cast<const float2 *>(GS + gsw(16 * blk + 15, d));
+        *reinterpret_cast<float2 *>(GB + gsw(t, d)) = make_float2(gm.x * kLog2e, gm.y * kLog2e);
+        const float a0 = __expf(gm.x - gs.x), a1 = __expf(gm.y - gs.y);
+        const float b0 = __expf(ge.x - gm.x), b1 = __expf(ge.y - gm.y);
+        okd[e] = pack_bf16(kf.x * a0, kf.y * a1);
+        oqd[e] = pack_bf16(qf.x * a0, qf.y * a1);
+        okf[e] = pack_bf16(kf.x * b0, kf.y * b1);
         okb[e] = pack_bf16(kf.x * __expf(gc.x - gm.x), kf.y * __expf(gc.y - gm.y));
       }
+      *reinterpret_cast<uint4 *>(sm + O_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
+      *reinterpret_cast<uint4 *>(sm + O_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
+      *reinterpret_cast<uint4 *>(sm + O_KF + off) = make_uint4(okf[0], okf[1], okf[2], okf[3]);
       *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
     }
   } else
@@ -491,7 +512,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
             f = fg;
             eg = f * (x ? er.y : er.x);
             eb = __fdividef(x ? eq.y : eq.x, f);
-          } else {
+          } else {  // (A_t is applied in P8 from the copy of gamma)
             f = 1.f;
             eg = __expf(fg);
             eb = __expf(GS[gsw(63, d + x)] - fg);  // gamma_C - gamma_t
@@ -565,71 +586,13 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   __syncthreads();
   if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
-  // ---- P8: decayed products ----
-  if (big) {  // exact per-element factors e^{gamma_t - gamma_s} (gamma kept over KD | QD)
-    float gm[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const float2 v = *reinterpret_cast<const float2 *>(GB + gsw(16 * mt + g4 + 8 * hh, n0 + 8 * nt + 2 * c4));
-        gm[nt][2 * hh] = v.x;
-        gm[nt][2 * hh + 1] = v.y;
-      }
-    auto bf = [&](int tile, int r, int c) {
-      return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
-    };
-    for (int s2 = 0; s2 < 16 * mt + 16; ++s2) {  // dq, dk rows: sum over s <= t
-      float dp[2], dk[2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int t = 16 * mt + g4 + 8 * hh;
-        dp[hh] = s2 <= t ? bf(O_DP, t, s2) : 0.f;
-        dk[hh] = s2 <= t ? bf(O_DK, t, s2) : 0.f;
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int d = n0 + 8 * nt + 2 * c4;
-        const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s2, d));
-        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s2, d)));
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int e = 2 * hh + x;
-            const float w = (x ? ks.y : ks.x) * __expf(fminf(gm[nt][e] - (x ? gs.y : gs.x), 0.f));
-            DQ[nt][e] = fmaf(dp[hh], w, DQ[nt][e]);
-            DKp[nt][e] = fmaf(dk[hh], w, DKp[nt][e]);
-          }
-      }
-    }
-    for (int t2 = 16 * mt; t2 < 64; ++t2) {  // dk columns: sum over t >= s
-      float dp[2], dk[2];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int s_ = 16 * mt + g4 + 8 * hh;
-        dp[hh] = t2 >= s_ ? bf(O_DP, t2, s_) : 0.f;
-        dk[hh] = t2 >= s_ ? bf(O_DK, t2, s_) : 0.f;
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int d = n0 + 8 * nt + 2 * c4;
-        const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t2, d));
-        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t2, d)));
-        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t2, d)));
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int e = 2 * hh + x;
-            const float w = __expf(fminf((x ? gt.y : gt.x) - gm[nt][e], 0.f));
-            DKm[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, DKm[nt][e]);
-          }
-      }
-    }
-  } else {
+  // ---- P8: decayed products.  Block pairs go through the tensor cores with the factors of P2;
+  //      a big chunk's diagonal block (mt, mt) is summed here with exact factors ----
+  // block pairs; compiled once per case (`Big`: without the diagonal block, B_s for the columns)
+  auto p8_pairs = [&](auto big_tag) {
+    constexpr bool Big = decltype(big_tag)::value;
     float Q2[2][4] = {}, K2[2][4] = {}, M2[2][4] = {};
-    for (int j = 0; j <= mt; ++j) {  // rows t in block mt, columns s in block j
+    for (int j = 0; j < mt + (Big ? 0 : 1); ++j) {  // rows t in block mt, columns s in block j
       float T1[2][4] = {}, T2[2][4] = {};
       uint32_t aP[4], aK[4], bK[4];
       ldsm_x4(a_frag_addr(s_base + O_DP, 16 * mt, 16 * j, lane), aP);
@@ -651,7 +614,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
         }
       }
     }
-    for (int i = mt; i < 4; ++i) {  // rows s in block mt, sum over t in block i
+    for (int i = mt + (Big ? 1 : 0); i < 4; ++i) {  // rows s in block mt, sum over t in block i
       float T3[2][4] = {};
       uint32_t aKt[4], aPt[4], bK[4], bQ[4];
       ldsm_x4_t(ct_frag_addr(s_base + O_DK, 16 * i, 16 * mt, lane), aKt);
@@ -670,14 +633,83 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
         for (int e = 0; e < 4; ++e) M2[nt][e] += ((e & 1) ? g2.y : g2.x) * T3[nt][e];
       }
     }
+    if (!Big) {
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        DQ[nt][e] += Fv[nt][e] * Q2[nt][e];
-        DKp[nt][e] += Fv[nt][e] * K2[nt][e];
-        DKm[nt][e] += __fdividef(M2[nt][e], Fv[nt][e]);
+        for (int e = 0; e < 4; ++e) {
+          DQ[nt][e] += Fv[nt][e] * Q2[nt][e];
+          DKp[nt][e] += Fv[nt][e] * K2[nt][e];
+          DKm[nt][e] += __fdividef(M2[nt][e], Fv[nt][e]);
+        }
+    } else {  // A_t = e^{gamma_t - gamma(start of block mt)}, B_s = e^{gamma(end of it) - gamma_s}
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = n0 + 8 * nt + 2 * c4 + (e & 1);
+          const float b = exp2f(GB[gsw(16 * mt + 15, d)] - GB[gsw(16 * mt + g4 + 8 * (e >> 1), d)]);
+          DKm[nt][e] += M2[nt][e] * b;
+        }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = n0 + 8 * nt + 2 * c4 + (e & 1);
+          const float a = exp2f(GB[gsw(16 * mt + g4 + 8 * (e >> 1), d)] - GB[gsw(16 * mt, d)]);
+          DQ[nt][e] += a * Q2[nt][e];
+          DKp[nt][e] += a * K2[nt][e];
+        }
+    }
+  };
+  if (big) {
+    // this thread's own gamma, re-read from shared memory where used (register pressure)
+    auto gown = [&](int nt, int e) { return GB[gsw(16 * mt + g4 + 8 * (e >> 1), n0 + 8 * nt + 2 * c4 + (e & 1))]; };
+    // The DP / DK tiles are zero above the diagonal, so the sums run over whole row / column
+    // ranges; the clamp only keeps e^{gamma_t - gamma_s} finite where s > t.
+    auto bf = [&](int tile, int r, int c) {
+      return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
+    };
+    const int r0 = 16 * mt + g4, r1 = r0 + 8;  // this thread's two rows
+    for (int s = 16 * mt; s <= r1; ++s) {  // dq, dk rows: sum over s <= t
+      const float dp[2] = {bf(O_DP, r0, s), bf(O_DP, r1, s)}, dk[2] = {bf(O_DK, r0, s), bf(O_DK, r1, s)};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int d = n0 + 8 * nt + 2 * c4;
+        const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s, d));
+        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s, d)));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int e = 2 * hh + x;
+            const float w = (x ? ks.y : ks.x) * exp2f(fminf(gown(nt, e) - (x ? gs.y : gs.x), 0.f));
+            DQ[nt][e] = fmaf(dp[hh], w, DQ[nt][e]);
+            DKp[nt][e] = fmaf(dk[hh], w, DKp[nt][e]);
+          }
       }
+    }
+    for (int t2 = r0; t2 < 16 * mt + 16; ++t2) {  // dk columns: sum over t >= s
+      const float dp[2] = {bf(O_DP, t2, r0), bf(O_DP, t2, r1)}, dk[2] = {bf(O_DK, t2, r0), bf(O_DK, t2, r1)};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int d = n0 + 8 * nt + 2 * c4;
+        const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t2, d));
+        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t2, d)));
+        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t2, d)));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int e = 2 * hh + x;
+            const float w = exp2f(fminf((x ? gt.y : gt.x) - gown(nt, e), 0.f));
+            DKm[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, DKm[nt][e]);
+          }
+      }
+    }
+    p8_pairs(std::true_type{});
+  } else {
+    p8_pairs(std::false_type{});
   }
   // ---- P9: dgamma, dg = reverse cumsum, outputs ----
   // ---- P9: dgamma = q dq + k (dk_row - dk_col) in registers while q, k are still resident ----
