@@ -220,8 +220,10 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     __syncthreads();
   }
   // guard: factored decay stays within e^{kSpanMax} unless gamma moves more than that across
-  // half a 16-row block; such a "big" chunk uses block-start references (every off-diagonal
-  // factor <= 1) and computes its diagonal blocks exactly.
+  // half a 16-row block.  Such a "big" chunk factors e^{gamma_t - gamma_s} (t in block i > j,
+  // the block of s) as A_t G_ij B_s with A_t = e^{gamma_t - gamma(start of i)},
+  // G_ij = e^{gamma(start of i) - gamma(end of j)}, B_s = e^{gamma(end of j) - gamma_s}, every
+  // factor <= 1, and computes its diagonal blocks exactly.
   if (tid < 64) {
     float span = 0.f;
 #pragma unroll
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       egr[i * 64 + d] = __expf(gC - ri);
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + ro, d)]) : (j == i ? 1.f : 0.f);
+        gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + (big ? 15 : ro), d)]) : (j == i ? 1.f : 0.f);
     } else if (slot == 4) {
       eG[d] = __expf(gC);
     }
@@ -267,7 +269,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const float4 ga4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0));
     const float4 gb4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0 + 4));
     const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
-    uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[4][4];
+    uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[1][4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
@@ -299,16 +301,9 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       okb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
       if (!big) {  // Kinc of the diagonal block only: k / F (the GEMMs rescale it per block pair)
         oki[0][e] = pack_bf16(kf.x * iF[0], kf.y * iF[1]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float s0 = 0.f, s1 = 0.f;
-          if (i >= blk) {
-            s0 = __expf(refs[i * 64 + d] - gam[2 * e]);
-            s1 = __expf(refs[i * 64 + d + 1] - gam[2 * e + 1]);
-          }
-          oki[i][e] = pack_bf16(kf.x * s0, kf.y * s1);
-        }
+      } else {  // k B_s
+        const float ge0 = GS[gsw(16 * blk + 15, d)], ge1 = GS[gsw(16 * blk + 15, d + 1)];
+        oki[0][e] = pack_bf16(kf.x * __expf(ge0 - gam[2 * e]), kf.y * __expf(ge1 - gam[2 * e + 1]));
       }
     }
     *reinterpret_cast<uint4 *>(sm + OFF_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
@@ -317,38 +312,46 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
     *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
     *reinterpret_cast<uint4 *>(sm + OFF_KBS + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
-    if (!big) {
-      *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(blk, blk) * 2048 + sw64(t & 15, d0)) =
-          make_uint4(oki[0][0], oki[0][1], oki[0][2], oki[0][3]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (i >= blk)
-          *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(i, blk) * 2048 + sw64(t & 15, d0)) =
-              make_uint4(oki[i][0], oki[i][1], oki[i][2], oki[i][3]);
-    }
+    *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(blk, blk) * 2048 + sw64(t & 15, d0)) =
+        make_uint4(oki[0][0], oki[0][1], oki[0][2], oki[0][3]);
   }
   __syncthreads();
 
-  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors)
+  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors): the 136
+  // pairs s <= t of each block, each summed over d by four adjacent lanes (16 channels each);
+  // the pair's lane for channels 0-15 also zeroes the mirror entry above the diagonal
   if (big) {
-    for (int e = tid; e < 1024; e += NT1) {
-      const int i = e >> 8, tl = (e >> 4) & 15, sl = e & 15, t = 16 * i + tl, s = 16 * i + sl;
+    for (int item = tid; item < 4 * 136 * 4; item += NT1) {
+      const int qd = item & 3, pr = item >> 2, i = pr / 136, pi = pr - i * 136;
+      int tl = (int)((sqrtf(8.f * pi + 1.f) - 1.f) * 0.5f);
+      tl += (tl + 1) * (tl + 2) / 2 <= pi;
+      tl -= tl * (tl + 1) / 2 > pi;
+      const int sl = pi - tl * (tl + 1) / 2, t = 16 * i + tl, s = 16 * i + sl;
       float mk = 0.f, mq = 0.f;
-      if (s <= t) {
-        for (int d = 0; d < 64; d += 2) {
-          const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
-          const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
-          const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
-          const float e0 = __expf(GS[gsw(t, d)] - GS[gsw(s, d)]);
-          const float e1 = __expf(GS[gsw(t, d + 1)] - GS[gsw(s, d + 1)]);
-          mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
-          mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
-        }
+#pragma unroll 4
+      for (int d = 16 * qd; d < 16 * qd + 16; d += 2) {
+        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
+        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
+        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
+        const float2 gt = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
+        const float2 gs = *reinterpret_cast<const float2 *>(GS + gsw(s, d));
+        const float e0 = __expf(gt.x - gs.x), e1 = __expf(gt.y - gs.y);
+        mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
+        mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
       }
-      AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
-      *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
-      *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(s <= t ? mq : 0.f);
+      mk += __shfl_xor_sync(0xffffffffu, mk, 1);
+      mq += __shfl_xor_sync(0xffffffffu, mq, 1);
+      mk += __shfl_xor_sync(0xffffffffu, mk, 2);
+      mq += __shfl_xor_sync(0xffffffffu, mq, 2);
+      if (qd == 0) {
+        AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
+        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
+        *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(mq);
+      } else if (qd == 1 && sl < tl) {  // the mirror (sl, tl) above the diagonal
+        AD[i * 256 + sl * 16 + tl] = 0.f;
+        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(s, t)) = __float2bfloat16_rn(0.f);
+        *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(s, t)) = __float2bfloat16_rn(0.f);
+      }
     }
     __syncthreads();
   }
@@ -365,9 +368,9 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   //      blocks and the 6 off-diagonal M blocks. ----
   auto mp_block = [&](int mat, int i, int j) {
     float acc[2][4] = {};
-    // a big chunk has every Kinc tile; otherwise only the diagonal ones (k / F) and the block
-    // pair's factor e^{r_i - r_j} scales the A operand along d
-    const bool scale = !big && j < i;
+    // only the diagonal Kinc tiles exist (k / F, or k B for a big chunk); the block pair's
+    // factor (e^{r_i - r_j}, or G_ij) scales the A operand along d
+    const bool scale = j < i;
     const uint32_t kib = s_base + OFF_KI + ki_index(scale ? j : i, j) * 2048;
     const float *G = gij + (i * 4 + j) * 64;
 #pragma unroll
