@@ -18,6 +18,10 @@ int tc_fwd_device_status(bool reset);
 int tc_bwd_device_status(bool reset);
 int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st);
 int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st);
+bool tc128_supported(const KdaDesc *d);
+size_t tc128_workspace_bytes(const KdaDesc *d);
+int tc128_fwd(const Params &p, int dtype_beta, cudaStream_t st);
+int tc128_fwd_device_status(bool reset);
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 }  // namespace kda
@@ -44,6 +48,11 @@ static bool use_tc(const KdaDesc *d, int backward) {
   if (d->flags & KDA_FLAG_FORCE_GENERIC) return false;
   return kda::tc_supported(d, backward);
 }
+// D = 128: tensor-core forward without saved states (streaming inference)
+static bool use_tc128(const KdaDesc *d, int backward) {
+  if (backward || (d->flags & KDA_FLAG_FORCE_GENERIC)) return false;
+  return kda::tc128_supported(d);
+}
 
 extern "C" {
 
@@ -52,7 +61,8 @@ int kda_abi_version(void) { return KDA_ABI_VERSION; }
 int kda_device_status(int reset) {
   const int f = kda::tc_fwd_device_status(reset != 0);
   const int b = kda::tc_bwd_device_status(reset != 0);
-  return f ? f : b;
+  const int f128 = kda::tc128_fwd_device_status(reset != 0);
+  return f ? f : b ? b : f128;
 }
 
 uint64_t kda_launch_counter(void) { return kda::g_launches.load(std::memory_order_relaxed); }
@@ -75,13 +85,14 @@ const char *kda_strerror(int s) {
 int kda_check_desc(const KdaDesc *d, int backward) {
   int s = check_desc_shape(d);
   if (s) return s;
-  if (use_tc(d, backward)) return KDA_OK;
+  if (use_tc(d, backward) || use_tc128(d, backward)) return KDA_OK;
   if (!backward) return kda::generic_fwd_split((int)d->Dk, (int)d->chunk) ? KDA_OK : KDA_ERR_UNSUPPORTED;
   return kda::generic_bwd_smem((int)d->Dk, (int)d->chunk) <= 227 * 1024 ? KDA_OK : KDA_ERR_UNSUPPORTED;
 }
 
 size_t kda_workspace_bytes(const KdaDesc *d, int backward) {
   if (kda_check_desc(d, backward)) return 0;
+  if (use_tc128(d, backward)) return kda::tc128_workspace_bytes(d);
   return use_tc(d, backward) ? kda::tc_workspace_bytes(d, backward) : 0;
 }
 
@@ -117,6 +128,7 @@ int kda_fwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   p.o = o; p.stateT = stateT; p.saved = saved; p.ws = ws;
   cudaStream_t st = (cudaStream_t)stream;
   if (use_tc(d, 0) && (!saved || use_tc(d, 1))) return kda::tc_fwd(p, d->dtype_beta, st);
+  if (use_tc128(d, 0) && !saved) return kda::tc128_fwd(p, d->dtype_beta, st);
   return kda::generic_fwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 

@@ -50,7 +50,7 @@ int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64
   const int64_t es = fp32 ? 4 : 2;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(H * D * es), (cuuint64_t)(T * H * D * es)};
-  const cuuint32_t box[4] = {(cuuint32_t)(fp32 ? 32 : D), 1, 64, 1};  // 128 bytes per box row
+  const cuuint32_t box[4] = {(cuuint32_t)(fp32 ? 32 : 64), 1, 64, 1};  // 128 bytes per box row
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                         const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

@@ -17,11 +17,11 @@ struct alignas(64) TmaMaps {
   CUtensorMap m[8];
 };
 
-// Encodes the map of a [B, T, H, D] tensor (bf16 or fp32, D = 64) with a box of 64 rows of
-// one head (all D columns for bf16, 32 for fp32).  Returns 0 on success, a KDA_ERR_* code otherwise.
+// Encodes the map of a [B, T, H, D] tensor (bf16 or fp32) with a box of 64 rows of one head
+// and 128 bytes of columns (64 for bf16, 32 for fp32; x selects the first column).  Returns 0 on success, a KDA_ERR_* code otherwise.
 int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32);
 
-// x: first column of the box (0, or 32 for the second half of an fp32 tile)
+// x: first column of the box (a multiple of 64 for bf16, of 32 for fp32)
 __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap *map, int h, int t0, int b,
                                               uint32_t mbar, int x = 0) {
   asm volatile(
