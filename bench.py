@@ -238,6 +238,56 @@ def fused_gates_leg(args, L, dev, q, k, v, S0, do, dst, desc, saved, ws, nws, ws
     return out
 
 
+def streaming_d128_leg(args, L, dev, flush):
+    """cfg4 (streaming inference): B1 H16 D128 chunk 64, T = 16384 as 4 segments of 4096 with
+    the state carried, heads sharded over 8 GPUs; this leg runs one GPU's share (2 heads),
+    forward only, each segment one kda_fwd call.  CUDA-graph replayed, L2 flushed per step."""
+    import ctypes
+    import torch
+    from mlx_vit_b200 import _lib
+    from mlx_vit_b200.kda import _desc, _ptr
+    from mlx_vit_b200.synthetic import make_inputs_torch
+    Bs, Hs, Ts, Ds, nseg = 1, 2, 4096, 128, 4
+    inp = make_inputs_torch(Bs, Ts * nseg, Hs, Ds, seed=77, device=dev, dtype=torch.bfloat16)
+    seg = [{n: inp[n][:, Ts * i:Ts * (i + 1)].contiguous() for n in ("q", "k", "v", "g", "beta")}
+           for i in range(nseg)]
+    desc = _desc(seg[0]["q"], seg[0]["beta"], CHUNK, 0)
+    nws = L.kda_workspace_bytes(ctypes.byref(desc), 0)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=dev)
+    states = [inp["state"].clone()] + [torch.empty_like(inp["state"]) for _ in range(nseg)]
+    outs = [torch.empty_like(x["q"]) for x in seg]
+    stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def step():
+        for i, x in enumerate(seg):
+            _lib.check(L.kda_fwd(ctypes.byref(desc), _ptr(x["q"]), _ptr(x["k"]), _ptr(x["v"]), _ptr(x["g"]),
+                                 _ptr(x["beta"]), _ptr(states[i]), _ptr(outs[i]), _ptr(states[i + 1]),
+                                 None, _ptr(ws), nws, stream()), "kda_fwd")
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    c0 = L.kda_launch_counter()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        step()
+    launches = L.kda_launch_counter() - c0
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    ms = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gr.replay()
+        e1.record()
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    t = statistics.mean(ms)
+    return {"workload": "cfg4 share of one GPU: B1 H2 D128 chunk64, 4 x 4096 tokens with the state "
+                        "carried (bf16 I/O, fp32 g/state), forward", "ms_per_step": round(t, 4),
+            "tokens_per_s": round(Bs * Ts * nseg / (t / 1e3), 1), "gpu_launches_per_step": int(launches)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -328,6 +378,7 @@ def run_ours(args, rank, world, local_rank):
 
     fused = fused_gates_leg(args, L, dev, q, k, v, S0, do, dst, desc, saved, ws, nws, wsf, nwsf,
                             dq, dk, dv, flush, o, S_T)
+    streaming = streaming_d128_leg(args, L, dev, flush)
 
     # ---- e2e through the public API with host buffers (pinned), copies inside timing ----
     host = {n: x.cpu().pin_memory() for n, x in inp.items()}
@@ -392,6 +443,7 @@ def run_ours(args, rank, world, local_rank):
                      "traffic": None},
         "gpu_launches": int(launches),
         "fused_gates": fused,
+        "streaming_d128": streaming,
         "clocks": clocks,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
