@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 2
+#define KDA_ABI_VERSION 3
 
 enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
 
@@ -125,6 +125,15 @@ KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const voi
             const void *saved, const void *dO, const float *dstateT,
             void *dq, void *dk, void *dv, float *dg, void *dbeta, float *dstate0,
             void *ws, size_t ws_bytes, void *stream);
+
+/* Token-by-token forward: the step form, exact in fp32, one launch, no chunk padding; for
+ * decoding and short segments (the state carried between calls).  Dk == Dv in {16, 32, 64, 128};
+ * desc->chunk is validated but unused.  No saved record (inference only).
+ * Replaces: the step path _kda_step_fused looped by _loop_compiled_kda / _loop_naive_kda
+ * (nope_gdn_mlx.py:616-638, :890-917, :2870-2892) and the step kernels (:2946-3036). */
+KDA_API int kda_fwd_recurrent(const KdaDesc *desc, const void *q, const void *k, const void *v,
+                              const float *g, const void *beta, const float *state0, void *o,
+                              float *stateT, void *stream);
 
 /* The layer's decay and write gates, fused into the kernels' load path (channel-wise KDA,
  * GatedDeltaLayer.__call__, nope_gdn_mlx.py:802-816):

@@ -12,7 +12,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkda_b200.so")
 
-KDA_ABI_VERSION = 2
+KDA_ABI_VERSION = 3
 KDA_F32, KDA_BF16, KDA_F16 = 0, 1, 2
 KDA_FLAG_FORCE_GENERIC = 0x1
 
@@ -26,7 +26,7 @@ KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 # every symbol include/kda_b200.h declares
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
            "kda_saved_bytes", "kda_launch_counter", "kda_device_status", "kda_fwd", "kda_bwd",
-           "kda_bwd_noalloc", "kda_fwd_gated", "kda_bwd_gated")
+           "kda_bwd_noalloc", "kda_fwd_gated", "kda_bwd_gated", "kda_fwd_recurrent")
 
 
 class KdaDesc(ctypes.Structure):
@@ -80,6 +80,8 @@ def _declare(L):
     L.kda_fwd_gated.argtypes = [D, P, P, P, G, P, P, P, P, P, S, P]
     L.kda_bwd_gated.restype = I
     L.kda_bwd_gated.argtypes = [D, P, P, P, G] + [P] * 12 + [P, S, P]
+    L.kda_fwd_recurrent.restype = I
+    L.kda_fwd_recurrent.argtypes = [D] + [P] * 9
 
 
 def lib(path: str | None = None):

@@ -19,6 +19,8 @@ int tc_bwd_device_status(bool reset);
 int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st);
 int tc_bwd(const Params &p, int dtype_beta, cudaStream_t st);
 bool tc128_supported(const KdaDesc *d);
+bool recurrent_supported(int D);
+int recurrent_fwd(const Params &p, int dq, int db, cudaStream_t st);
 size_t tc128_workspace_bytes(const KdaDesc *d);
 int tc128_fwd(const Params &p, int dtype_beta, cudaStream_t st);
 int tc128_fwd_device_status(bool reset);
@@ -154,6 +156,18 @@ int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   cudaStream_t st = (cudaStream_t)stream;
   if (use_tc(d, 1)) return kda::tc_bwd(p, d->dtype_beta, st);
   return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
+}
+
+int kda_fwd_recurrent(const KdaDesc *d, const void *q, const void *k, const void *v, const float *g,
+                      const void *beta, const float *state0, void *o, float *stateT, void *stream) {
+  int s = check_desc_shape(d);
+  if (s) return s;
+  if (!kda::recurrent_supported((int)d->Dk)) return KDA_ERR_UNSUPPORTED;
+  if (!q || !k || !v || !g || !beta || !o || !stateT) return KDA_ERR_INVALID_ARG;
+  Params p = make_params(d);
+  p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
+  p.o = o; p.stateT = stateT;
+  return kda::recurrent_fwd(p, d->dtype_qkv, d->dtype_beta, (cudaStream_t)stream);
 }
 
 static int check_gate(const KdaDesc *d, const KdaGate *gate) {

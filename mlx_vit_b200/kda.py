@@ -144,6 +144,25 @@ def kda_backward(q, k, v, g, beta, state, saved, do, dstate=None, chunk_size=64,
     return dq, dk, dv, dg, db, ds0
 
 
+RECURRENT_MAX_T = 16  # cuda_kda without gradients steps token by token up to this length
+
+
+def kda_recurrent(q, k, v, g, beta, state=None):
+    """One ``kda_fwd_recurrent`` call: the step form token by token (exact fp32 arithmetic, one
+    launch), for decoding and short segments.  Returns (o, S_T); no gradients."""
+    L = _lib.lib()
+    B, T, H, D = q.shape
+    desc = _desc(q, beta, 64, 0)
+    o = torch.empty_like(q)
+    S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream().cuda_stream
+        st = L.kda_fwd_recurrent(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta),
+                                 _ptr(state), _ptr(o), _ptr(S_T), ctypes.c_void_p(stream))
+    _lib.check(st, "kda_fwd_recurrent")
+    return o, S_T
+
+
 class CudaKdaFunction(torch.autograd.Function):
     """Autograd wiring of the forward/VJP pair (the torch counterpart of the reference's
     ``mx.custom_function`` + ``.vjp`` at nope_gdn_mlx.py:2734-2809).  The forward saves one
@@ -190,6 +209,8 @@ def cuda_kda(q, k, v, g, beta, state: Optional[torch.Tensor] = None, chunk_size:
         x is not None and x.requires_grad for x in (q, k, v, g, beta, state))
     if need_grad:
         return CudaKdaFunction.apply(q, k, v, g, beta, state, chunk_size, flags)
+    if q.shape[1] <= RECURRENT_MAX_T and q.shape[3] in (16, 32, 64, 128) and not force_generic:
+        return kda_recurrent(q, k, v, g, beta, state)
     o, S_T, _ = kda_forward(q, k, v, g, beta, state, chunk_size, save_states=False, flags=flags)
     return o, S_T
 

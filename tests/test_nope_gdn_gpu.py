@@ -1,0 +1,65 @@
+"""The NoPE-GDN model around the fused-gate op (GPU): the layer agrees with the same layer whose
+gates are evaluated in torch around plain ``cuda_kda``, and a small model trains (finite
+gradients everywhere, loss going down over a few steps)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kda_testutil import rel_err
+from mlx_vit_b200 import cuda_kda
+from mlx_vit_b200.nope_gdn import GatedDeltaLayer, NoPEGDNVideo
+
+pytestmark = pytest.mark.gpu
+
+
+def unfused_forward(layer, x):
+    """The layer's forward with g and beta evaluated in torch (nope_gdn_mlx.py:802-816)."""
+    B, L, _ = x.shape
+    H, D = layer.H, layer.D
+    bf = torch.bfloat16
+    q = F.silu(layer.q_conv1d(layer.q_proj(x))).view(B, L, H, D)
+    k = F.silu(layer.k_conv1d(layer.k_proj(x))).view(B, L, H, D)
+    v = F.silu(layer.v_conv1d(layer.v_proj(x))).view(B, L, H, D)
+    q = (F.normalize(q.float(), dim=-1) * layer.scale).to(bf)
+    k = F.normalize(k.float(), dim=-1).to(bf)
+    f = layer.f_proj_2(layer.f_proj_1(x)).view(B, L, H, D).to(bf)
+    g = -torch.exp(layer.A_log).view(1, 1, H, 1) * F.softplus(f.float() + layer.dt_bias.view(H, D))
+    beta = torch.sigmoid(layer.b_proj(x).to(bf).float())
+    o, _ = cuda_kda(q, k, v.to(bf).contiguous(), g, beta, None, layer.chunk)
+    gate = layer.g_proj_2(layer.g_proj_1(x)).view(B, L, H, D)
+    return layer.o_proj(layer.o_norm(o, gate).reshape(B, L, H * D))
+
+
+def test_layer_fused_gates_equal_unfused(cuda):
+    torch.manual_seed(0)
+    layer = GatedDeltaLayer(256, 4, 64).to(cuda)
+    x = torch.randn(2, 200, 256, device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y1, _ = layer(x)
+    g1 = torch.autograd.grad(y1.float().square().sum(), list(layer.parameters()))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y2 = unfused_forward(layer, x)
+    g2 = torch.autograd.grad(y2.float().square().sum(), list(layer.parameters()))
+    assert rel_err(y1.detach().float().cpu().numpy(), y2.detach().float().cpu().numpy()) <= 2e-2
+    for (n, _), a, b in zip(layer.named_parameters(), g1, g2):
+        assert torch.isfinite(a).all(), n
+        assert rel_err(a.float().cpu().numpy(), b.float().cpu().numpy()) <= 5e-2, n
+
+
+def test_small_model_trains(cuda):
+    torch.manual_seed(1)
+    model = NoPEGDNVideo(img_size=64, frames=8, dim=128, depth=2, heads=2, num_classes=10).to(cuda)
+    clips = torch.rand(2, 8, 64, 64, 3, device=cuda)
+    labels = torch.tensor([3, 7], device=cuda)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+    losses = []
+    for _ in range(6):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = F.cross_entropy(model(clips).float(), labels)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        for n, p in model.named_parameters():
+            assert p.grad is not None and torch.isfinite(p.grad).all(), n
+        opt.step()
+        losses.append(loss.item())
+    assert losses[-1] < losses[0], losses
