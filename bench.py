@@ -473,6 +473,14 @@ def kernel_only(args):
     from mlx_vit_b200 import kda_forward, kda_backward
     from mlx_vit_b200.synthetic import make_inputs_torch
     dev = torch.device("cuda", 0)
+    if args.kernel_only == "stream":  # the D = 128 streaming forward: cfg4's share of one GPU
+        x = make_inputs_torch(1, 4096, 2, 128, seed=77, device=dev, dtype=torch.bfloat16)
+        st = x["state"]
+        for _ in range(args.warmup + args.steps):
+            for _ in range(4):
+                _, st, _ = kda_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], st, CHUNK)
+        torch.cuda.synchronize()
+        return 0
     inp = make_inputs_torch(B, T, H, D, seed=1234, device=dev, dtype=torch.bfloat16, state_std=0.1)
     q, k, v, g, beta, S0, do, dst = (inp[n] for n in ("q", "k", "v", "g", "beta", "state", "do", "dst"))
     _, _, cs = kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=True)
@@ -572,7 +580,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=("cfg2", "cfg3"), default="cfg2",
                     help="cfg2: the KDA op (the headline line); cfg3: full-model DP training step")
-    ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both"), default=None,
+    ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both", "stream"), default=None,
                     help="profiling driver: run only the kda_fwd/kda_bwd launches (steps+warmup "
                          "times), no timing, no e2e, no JSON line")
     args = ap.parse_args()
