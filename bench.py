@@ -544,11 +544,13 @@ def run_cfg3(args, rank, world, local_rank):
     total = max_over_ranks(e0.elapsed_time(e1), dev)
     ms = total / args.steps
     share = None
+    # every rank runs the profiled step (DDP's all-reduce needs all of them); rank 0 records it
+    import contextlib
+    from torch.profiler import profile, ProfilerActivity
+    with (profile(activities=[ProfilerActivity.CUDA]) if rank == 0 else contextlib.nullcontext()) as prof:
+        step()
+        torch.cuda.synchronize()
     if rank == 0:
-        from torch.profiler import profile, ProfilerActivity
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            step()
-            torch.cuda.synchronize()
         kda_us = all_us = 0.0
         for ev in prof.key_averages():
             t = getattr(ev, "device_time_total", None) or getattr(ev, "cuda_time_total", 0.0)
@@ -613,7 +615,10 @@ def main():
         return kernel_only(args)
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        import datetime
+        # a short collective timeout: a rank that falls out ends the others' next collective
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=120))
     line = run_cfg3(args, rank, world, local_rank) if args.workload == "cfg3" else run_ours(args, rank, world, local_rank)
     if line is not None:
         print(json.dumps(line))
