@@ -44,9 +44,41 @@ static PFN_cuTensorMapEncodeTiled encode_fn() {
   return fn;
 }
 
+// The tensor-map encoder is a driver call: it needs a current context on the calling thread.  A
+// host thread that has made no runtime call yet (e.g. an autograd worker thread on device 0, where
+// the runtime's default device already matches and nothing binds a context) has none, so bind the
+// current device's primary context first.  Host-only and allowed during stream capture.
+static bool ensure_context() {
+  static PFN_cuCtxGetCurrent get_cur = nullptr;
+  static PFN_cuCtxSetCurrent set_cur = nullptr;
+  static PFN_cuDevicePrimaryCtxRetain retain = nullptr;
+  static PFN_cuDeviceGet dev_get = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<PFN_cuCtxGetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxSetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      set_cur = reinterpret_cast<PFN_cuCtxSetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuDevicePrimaryCtxRetain", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      retain = reinterpret_cast<PFN_cuDevicePrimaryCtxRetain>(p);
+    if (cudaGetDriverEntryPoint("cuDeviceGet", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      dev_get = reinterpret_cast<PFN_cuDeviceGet>(p);
+  });
+  if (!get_cur || !set_cur || !retain || !dev_get) return false;
+  CUcontext ctx = nullptr;
+  if (get_cur(&ctx) == CUDA_SUCCESS && ctx) return true;
+  int dev = 0;
+  CUdevice cu = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev_get(&cu, dev) != CUDA_SUCCESS) return false;
+  // one reference to the primary context is kept until exit (the runtime holds one as well)
+  return retain(&ctx, cu) == CUDA_SUCCESS && set_cur(ctx) == CUDA_SUCCESS;
+}
+
 int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32) {
   PFN_cuTensorMapEncodeTiled fn = encode_fn();
-  if (!fn) return KDA_ERR_CUDA;
+  if (!fn || !ensure_context()) return KDA_ERR_CUDA;
   const int64_t es = fp32 ? 4 : 2;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   const cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(H * D * es), (cuuint64_t)(T * H * D * es)};

@@ -149,3 +149,27 @@ def test_no_device_wait_timed_out(cuda):
     """Every bounded device-side wait in the runs above completed (status word still 0)."""
     from mlx_vit_b200 import _lib
     assert _lib.lib().kda_device_status(0) == 0
+
+
+def test_fresh_host_thread(cuda):
+    """A host thread that has made no CUDA call yet (as autograd's worker thread on device 0)
+    can run the tensor-core forward and backward: the library binds the device's context for
+    its driver-side tensor-map encoding."""
+    import threading
+    inp = make_inputs(2, 100, 3, 64, seed=7, state_std=0.1)
+    out = {}
+
+    def work():
+        try:
+            t = to_dev(inp, cuda, torch.bfloat16)
+            out["r"] = run_fwd_bwd(t, 64)
+        except Exception as e:  # reported below
+            out["e"] = e
+
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert "e" not in out, out.get("e")
+    ref = O.fwd_bwd(rounded_inputs(inp, torch.bfloat16), dtype=np.float64)
+    for k in OUT_KEYS:
+        assert rel_err(out["r"][k], ref[k]) <= TOL_BF16, k

@@ -49,7 +49,8 @@ def test_layer_fused_gates_equal_unfused(cuda):
     # bf16 paths differ in them by more (about 15 % here); the op-level tests pin them against
     # the oracle with the dg bound carried through the chain rule.  Every other gradient: 5e-2.
     loose = {"A_log": 0.25, "dt_bias": 0.25}
-    assert all(e <= loose.get(n, 5e-2) for n, e in errs.items()), errs
+    bad = {n: e for n, e in errs.items() if e > loose.get(n, 5e-2)}
+    assert not bad, bad
 
 
 def test_small_model_trains(cuda):
