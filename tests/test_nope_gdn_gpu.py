@@ -1,6 +1,7 @@
 """The NoPE-GDN model around the fused-gate op (GPU): the layer agrees with the same layer whose
 gates are evaluated in torch around plain ``cuda_kda``, and a small model trains (finite
 gradients everywhere, loss going down over a few steps)."""
+import numpy as np
 import pytest
 import torch
 import torch.nn.functional as F
@@ -33,6 +34,10 @@ def unfused_forward(layer, x):
 def test_layer_fused_gates_equal_unfused(cuda):
     torch.manual_seed(0)
     layer = GatedDeltaLayer(256, 4, 64).to(cuda)
+    # mild decays (A = 1.5): this checks the layer's wiring; strong-decay parity of the gate
+    # gradients (df amplified by A) is the op-level tests' subject
+    with torch.no_grad():
+        layer.A_log.fill_(float(np.log(1.5)))
     x = torch.randn(2, 200, 256, device=cuda)
     with torch.autocast("cuda", dtype=torch.bfloat16):
         y1, _ = layer(x)
