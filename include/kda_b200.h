@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 3
+#define KDA_ABI_VERSION 4
 
 enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
 
@@ -134,6 +134,22 @@ KDA_API int kda_bwd(const KdaDesc *desc, const void *q, const void *k, const voi
 KDA_API int kda_fwd_recurrent(const KdaDesc *desc, const void *q, const void *k, const void *v,
                               const float *g, const void *beta, const float *state0, void *o,
                               float *stateT, void *stream);
+
+/* The layer's row operations around the recurrence, one fused pass each (bf16 I/O, fp32
+ * arithmetic, rows of D = 64 or 128 contiguous elements, 16-byte aligned pointers):
+ *   kda_l2norm_silu_fwd:  y = l2norm(silu(x)) * scale   (q: scale = D^-1/2, k: 1)
+ *   kda_gated_rmsnorm_fwd: y = rmsnorm(o) * w * sigmoid(gate), w float32 [D]
+ * and their VJPs (dw float32 [D], overwritten).
+ * Replaces: GatedDeltaLayer.__call__'s "SiLU + L2 norm + scale" lines (nope_gdn_mlx.py:797-799,
+ * l2_normalize :76-79) and its output RMSNormGated (:340-371, applied at :880-885). */
+KDA_API int kda_l2norm_silu_fwd(int64_t rows, int D, const void *x, void *y, float scale, void *stream);
+KDA_API int kda_l2norm_silu_bwd(int64_t rows, int D, const void *x, const void *dy, void *dx, float scale,
+                                void *stream);
+KDA_API int kda_gated_rmsnorm_fwd(int64_t rows, int D, const void *o, const void *gate, const float *w,
+                                  void *y, float eps, void *stream);
+KDA_API int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, const float *w,
+                                  const void *dy, void *dout, void *dgate, float *dw, float eps,
+                                  void *stream);
 
 /* The layer's decay and write gates, fused into the kernels' load path (channel-wise KDA,
  * GatedDeltaLayer.__call__, nope_gdn_mlx.py:802-816):

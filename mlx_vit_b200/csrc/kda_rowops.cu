@@ -1,0 +1,242 @@
+// The GDN layer's per-head row operations around the recurrence, fused into one pass each
+// (bf16 I/O, fp32 arithmetic, one warp per row of D = 64 or 128 elements):
+//
+//   prologue  y = l2norm(silu(x)) * scale     q and k after the short convolutions
+//             (nope_gdn_mlx.py:797-799 with l2_normalize :76-79: x / max(||x||, 1e-12))
+//   epilogue  y = rmsnorm(o) * w * sigmoid(gate)   the output's gated RMSNorm
+//             (RMSNormGated / _gated_rms_norm :340-371, applied at :880-885)
+//
+// and their VJPs.  The backward of the prologue recomputes silu(x) and the norm from x; the
+// backward of the epilogue recomputes the RMS from o and reduces dw over rows with one atomic
+// per channel per CTA.
+#include <initializer_list>
+
+#include "kda_common.cuh"
+
+namespace kda {
+namespace rowops {
+
+constexpr int kWarps = 8;  // rows per CTA pass
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// E = elements per lane (D / 32): lane l holds columns l*E .. l*E+E-1
+template <int E>
+__device__ __forceinline__ void load_row(const __nv_bfloat16 *p, int lane, float (&x)[E]) {
+  const __nv_bfloat162 *q = reinterpret_cast<const __nv_bfloat162 *>(p + lane * E);
+#pragma unroll
+  for (int i = 0; i < E / 2; ++i) {
+    const float2 f = __bfloat1622float2(q[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+template <int E>
+__device__ __forceinline__ void store_row(__nv_bfloat16 *p, int lane, const float (&x)[E]) {
+  __nv_bfloat162 *q = reinterpret_cast<__nv_bfloat162 *>(p + lane * E);
+#pragma unroll
+  for (int i = 0; i < E / 2; ++i) q[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+}
+
+template <int E>
+__global__ void __launch_bounds__(32 * kWarps) l2norm_silu_fwd_kernel(int64_t rows, const __nv_bfloat16 *x,
+                                                                      __nv_bfloat16 *y, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    float v[E];
+    load_row<E>(x + r * 32 * E, lane, v);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      v[i] *= sigm(v[i]);
+      ss += v[i] * v[i];
+    }
+    const float inv = scale / fmaxf(sqrtf(warp_sum(ss)), 1e-12f);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] *= inv;
+    store_row<E>(y + r * 32 * E, lane, v);
+  }
+}
+
+// y = scale s / max(n, eps), s = silu(x), n = ||s||:
+//   ds = scale (dy - s (s . dy) / n^2) / n  (n > eps; else scale dy / eps);  dx = ds silu'(x)
+template <int E>
+__global__ void __launch_bounds__(32 * kWarps) l2norm_silu_bwd_kernel(int64_t rows, const __nv_bfloat16 *x,
+                                                                      const __nv_bfloat16 *dy,
+                                                                      __nv_bfloat16 *dx, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    float v[E], g[E], s[E];
+    load_row<E>(x + r * 32 * E, lane, v);
+    load_row<E>(dy + r * 32 * E, lane, g);
+    float ss = 0.f, sg = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      s[i] = v[i] * sigm(v[i]);
+      ss += s[i] * s[i];
+      sg += s[i] * g[i];
+    }
+    ss = warp_sum(ss);
+    sg = warp_sum(sg);
+    const float n = sqrtf(ss);
+    const bool clamp = !(n > 1e-12f);
+    const float inv = scale / (clamp ? 1e-12f : n), proj = clamp ? 0.f : sg / ss;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float sgm = sigm(v[i]);
+      const float ds = inv * (g[i] - s[i] * proj);
+      g[i] = ds * sgm * (1.f + v[i] * (1.f - sgm));
+    }
+    store_row<E>(dx + r * 32 * E, lane, g);
+  }
+}
+
+template <int E>
+__global__ void __launch_bounds__(32 * kWarps) gated_rmsnorm_fwd_kernel(int64_t rows, const __nv_bfloat16 *o,
+                                                                        const __nv_bfloat16 *gate, const float *w,
+                                                                        __nv_bfloat16 *y, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  float wl[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) wl[i] = w[lane * E + i];
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    float v[E], g[E];
+    load_row<E>(o + r * 32 * E, lane, v);
+    load_row<E>(gate + r * 32 * E, lane, g);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss += v[i] * v[i];
+    const float rr = rsqrtf(warp_sum(ss) / (32 * E) + eps);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = v[i] * rr * wl[i] * sigm(g[i]);
+    store_row<E>(y + r * 32 * E, lane, v);
+  }
+}
+
+// n = o r, r = rsqrt(mean(o^2) + eps), y = n w sigmoid(gate):
+//   dgate = dy n w s (1 - s);  dw += dy n s;  dn = dy w s;  do = r (dn - n mean(dn n))
+template <int E>
+__global__ void __launch_bounds__(32 * kWarps) gated_rmsnorm_bwd_kernel(int64_t rows, const __nv_bfloat16 *o,
+                                                                        const __nv_bfloat16 *gate, const float *w,
+                                                                        const __nv_bfloat16 *dy, __nv_bfloat16 *dout,
+                                                                        __nv_bfloat16 *dgate, float *dw, float eps) {
+  __shared__ float red[kWarps][32 * E];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  float wl[E], dwl[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    wl[i] = w[lane * E + i];
+    dwl[i] = 0.f;
+  }
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + wp; r < rows; r += stride) {
+    float v[E], g[E], d[E];
+    load_row<E>(o + r * 32 * E, lane, v);
+    load_row<E>(gate + r * 32 * E, lane, g);
+    load_row<E>(dy + r * 32 * E, lane, d);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) ss += v[i] * v[i];
+    const float rr = rsqrtf(warp_sum(ss) / (32 * E) + eps);
+    float dnn = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float n = v[i] * rr, s = sigm(g[i]);
+      dwl[i] += d[i] * n * s;
+      const float dn = d[i] * wl[i] * s;
+      g[i] = d[i] * n * wl[i] * s * (1.f - s);  // dgate
+      v[i] = n;
+      d[i] = dn;
+      dnn += dn * n;
+    }
+    const float m = warp_sum(dnn) / (32 * E);
+#pragma unroll
+    for (int i = 0; i < E; ++i) d[i] = rr * (d[i] - v[i] * m);
+    store_row<E>(dout + r * 32 * E, lane, d);
+    store_row<E>(dgate + r * 32 * E, lane, g);
+  }
+#pragma unroll
+  for (int i = 0; i < E; ++i) red[wp][lane * E + i] = dwl[i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < 32 * E; c += 32 * kWarps) {
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) a += red[k][c];
+    atomicAdd(dw + c, a);
+  }
+}
+
+static int grid_for(int64_t rows) {
+  static int nsm = 0;
+  if (!nsm) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      nsm = 148;
+  }
+  const int64_t need = (rows + kWarps - 1) / kWarps;
+  return (int)(need < 8LL * nsm ? need : 8LL * nsm);
+}
+
+}  // namespace rowops
+}  // namespace kda
+
+using namespace kda::rowops;
+
+static bool row_args_ok(int64_t rows, int D, std::initializer_list<const void *> ptrs) {
+  if (rows <= 0 || !(D == 64 || D == 128)) return false;
+  for (const void *p : ptrs)
+    if (!p || ((uintptr_t)p & 15u)) return false;
+  return true;
+}
+
+#define KDA_ROW_LAUNCH(kern, rows, D, st, ...)                                                 \
+  do {                                                                                         \
+    const int g = grid_for(rows);                                                              \
+    if (D == 64) kern<2><<<g, 32 * kWarps, 0, st>>>(rows, __VA_ARGS__);                        \
+    else kern<4><<<g, 32 * kWarps, 0, st>>>(rows, __VA_ARGS__);                                \
+    kda::count_launch();                                                                       \
+  } while (0)
+
+extern "C" {
+
+int kda_l2norm_silu_fwd(int64_t rows, int D, const void *x, void *y, float scale, void *stream) {
+  if (!row_args_ok(rows, D, {x, y})) return KDA_ERR_INVALID_ARG;
+  KDA_ROW_LAUNCH(l2norm_silu_fwd_kernel, rows, D, (cudaStream_t)stream, (const __nv_bfloat16 *)x,
+                 (__nv_bfloat16 *)y, scale);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+int kda_l2norm_silu_bwd(int64_t rows, int D, const void *x, const void *dy, void *dx, float scale, void *stream) {
+  if (!row_args_ok(rows, D, {x, dy, dx})) return KDA_ERR_INVALID_ARG;
+  KDA_ROW_LAUNCH(l2norm_silu_bwd_kernel, rows, D, (cudaStream_t)stream, (const __nv_bfloat16 *)x,
+                 (const __nv_bfloat16 *)dy, (__nv_bfloat16 *)dx, scale);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+int kda_gated_rmsnorm_fwd(int64_t rows, int D, const void *o, const void *gate, const float *w, void *y,
+                          float eps, void *stream) {
+  if (!row_args_ok(rows, D, {o, gate, w, y})) return KDA_ERR_INVALID_ARG;
+  KDA_ROW_LAUNCH(gated_rmsnorm_fwd_kernel, rows, D, (cudaStream_t)stream, (const __nv_bfloat16 *)o,
+                 (const __nv_bfloat16 *)gate, w, (__nv_bfloat16 *)y, eps);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, const float *w, const void *dy,
+                          void *dout, void *dgate, float *dw, float eps, void *stream) {
+  if (!row_args_ok(rows, D, {o, gate, w, dy, dout, dgate, dw})) return KDA_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(dw, 0, sizeof(float) * D, st) != cudaSuccess) return KDA_ERR_CUDA;
+  KDA_ROW_LAUNCH(gated_rmsnorm_bwd_kernel, rows, D, st, (const __nv_bfloat16 *)o, (const __nv_bfloat16 *)gate, w,
+                 (const __nv_bfloat16 *)dy, (__nv_bfloat16 *)dout, (__nv_bfloat16 *)dgate, dw, eps);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -7,7 +7,8 @@ g = -e^{A_log} softplus(f_proj_2(f_proj_1(x)) + dt_bias) and the write gate beta
 the recurrence, the low-rank output gate with gated RMSNorm, and the output projection), the
 pre-norm block with a GELU MLP (``HybridBlock``, :4009-4090), a tubelet embedding and a
 classification head.  The recurrence and both gates run in the library's fused kernels
-(``cuda_kda_gated``); everything else is PyTorch (cuBLAS GEMMs, elementwise kernels).
+(``cuda_kda_gated``), the q / k prologue (SiLU + L2 norm) and the output's gated RMSNorm in its
+one-pass row kernels (``rowops``); everything else is PyTorch (cuBLAS GEMMs, elementwise kernels).
 
 Parameters follow the reference's initialisation where it sets one: A ~ U[1, 16] as A_log,
 dt_bias = 0, RMSNorm weight 1, conv weights ~ U(+-1/sqrt(K)) with zero bias.
@@ -21,6 +22,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .kda import cuda_kda_gated
+from .rowops import gated_rmsnorm, l2norm_silu
 
 
 class ShortCausalConv1d(nn.Module):
@@ -46,8 +48,11 @@ class RMSNormGated(nn.Module):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(dim))
         self.eps = eps
+        self.fused = True  # the library's one-pass kernel (kda_gated_rmsnorm_*); False: torch ops
 
     def forward(self, x, gate):
+        if self.fused and x.is_cuda and x.shape[-1] in (64, 128):
+            return gated_rmsnorm(x.to(torch.bfloat16), gate.to(torch.bfloat16), self.weight, self.eps)
         xf = x.float()
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
         return (y * torch.sigmoid(gate.float())).to(x.dtype)
@@ -80,16 +85,21 @@ class GatedDeltaLayer(nn.Module):
         self.g_proj_2 = nn.Linear(D, tot, bias=True)
         self.o_norm = RMSNormGated(D)
         self.o_proj = nn.Linear(tot, hidden, bias=False)
+        self.fused_rows = True  # q/k prologue in the library's fused kernel; False: torch ops
 
     def forward(self, x, state=None):
         B, L, _ = x.shape
         H, D = self.H, self.D
         bf = torch.bfloat16
-        q = F.silu(self.q_conv1d(self.q_proj(x))).view(B, L, H, D)
-        k = F.silu(self.k_conv1d(self.k_proj(x))).view(B, L, H, D)
         v = F.silu(self.v_conv1d(self.v_proj(x))).view(B, L, H, D)
-        q = (F.normalize(q.float(), dim=-1) * self.scale).to(bf)
-        k = F.normalize(k.float(), dim=-1).to(bf)
+        qr = self.q_conv1d(self.q_proj(x)).view(B, L, H, D)
+        kr = self.k_conv1d(self.k_proj(x)).view(B, L, H, D)
+        if self.fused_rows:  # one pass each: the library's kda_l2norm_silu_* kernels
+            q = l2norm_silu(qr.to(bf), self.scale)
+            k = l2norm_silu(kr.to(bf), 1.0)
+        else:
+            q = (F.normalize(F.silu(qr).float(), dim=-1) * self.scale).to(bf)
+            k = F.normalize(F.silu(kr).float(), dim=-1).to(bf)
         f = self.f_proj_2(self.f_proj_1(x)).view(B, L, H, D).to(bf)
         b = self.b_proj(x).to(bf)
         o, new_state = cuda_kda_gated(q, k, v.to(bf).contiguous(), f.contiguous(), self.A_log,

@@ -1,0 +1,93 @@
+"""Fused row operations of the GDN layer around the recurrence (bf16, D = 64 or 128), with
+autograd: ``l2norm_silu`` is the q / k prologue y = l2norm(silu(x)) * scale
+(nope_gdn_mlx.py:797-799, l2_normalize :76-79) and ``gated_rmsnorm`` the output's
+y = rmsnorm(o) * w * sigmoid(gate) (RMSNormGated, :340-371).  One CUDA pass each way
+(``kda_l2norm_silu_*`` / ``kda_gated_rmsnorm_*`` in include/kda_b200.h); no CPU path."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _ptr(x):
+    return ctypes.c_void_p(x.data_ptr())
+
+
+def _stream(x):
+    return ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+
+
+def _check_rows(*xs):
+    for x in xs:
+        if not x.is_cuda or x.dtype != torch.bfloat16:
+            raise ValueError("fused row ops take bf16 CUDA tensors")
+    D = xs[0].shape[-1]
+    if D not in (64, 128):
+        raise ValueError(f"fused row ops need D = 64 or 128, got {D}")
+    return xs[0].numel() // D, D
+
+
+class L2NormSiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, scale):
+        x = x.contiguous()
+        rows, D = _check_rows(x)
+        y = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.lib().kda_l2norm_silu_fwd(rows, D, _ptr(x), _ptr(y), float(scale), _stream(x)),
+                       "kda_l2norm_silu_fwd")
+        ctx.save_for_backward(x)
+        ctx.scale = scale
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        rows, D = _check_rows(x, dy)
+        dx = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.lib().kda_l2norm_silu_bwd(rows, D, _ptr(x), _ptr(dy), _ptr(dx), float(ctx.scale),
+                                                      _stream(x)), "kda_l2norm_silu_bwd")
+        return dx, None
+
+
+class GatedRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, o, gate, w, eps):
+        o, gate = o.contiguous(), gate.contiguous()
+        rows, D = _check_rows(o, gate)
+        w32 = w.to(torch.float32).contiguous()
+        y = torch.empty_like(o)
+        with torch.cuda.device(o.device):
+            _lib.check(_lib.lib().kda_gated_rmsnorm_fwd(rows, D, _ptr(o), _ptr(gate), _ptr(w32), _ptr(y),
+                                                        float(eps), _stream(o)), "kda_gated_rmsnorm_fwd")
+        ctx.save_for_backward(o, gate, w32)
+        ctx.eps, ctx.w_dtype = eps, w.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        o, gate, w32 = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16).contiguous()
+        rows, D = _check_rows(o, gate, dy)
+        do, dg = torch.empty_like(o), torch.empty_like(gate)
+        dw = torch.empty(D, dtype=torch.float32, device=o.device)
+        with torch.cuda.device(o.device):
+            _lib.check(_lib.lib().kda_gated_rmsnorm_bwd(rows, D, _ptr(o), _ptr(gate), _ptr(w32), _ptr(dy), _ptr(do),
+                                                        _ptr(dg), _ptr(dw), float(ctx.eps), _stream(o)),
+                       "kda_gated_rmsnorm_bwd")
+        return do, dg, dw.to(ctx.w_dtype), None
+
+
+def l2norm_silu(x: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
+    """y = silu(x) / max(||silu(x)||, 1e-12) * scale over the last dim (bf16 in and out)."""
+    return L2NormSiLU.apply(x, scale)
+
+
+def gated_rmsnorm(o: torch.Tensor, gate: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """y = o * rsqrt(mean(o^2) + eps) * w * sigmoid(gate) over the last dim (bf16 in and out)."""
+    return GatedRMSNorm.apply(o, gate, w, eps)

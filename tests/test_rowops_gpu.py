@@ -1,0 +1,59 @@
+"""GPU parity of the fused row kernels (kda_l2norm_silu_*, kda_gated_rmsnorm_*) against fp32
+torch references on the same bf16 inputs: forward and every gradient, max|delta|/max|ref|
+<= 2e-2 (bf16 I/O)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from kda_testutil import rel_err
+from mlx_vit_b200.rowops import gated_rmsnorm, l2norm_silu
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def np_(x):
+    return x.detach().float().cpu().numpy()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("scale", [1.0, 0.125])
+def test_l2norm_silu(cuda, D, scale):
+    torch.manual_seed(D)
+    x = (torch.randn(3, 37, 5, D, device=cuda) * 2).to(torch.bfloat16)
+    x[0, 0, 0] = 0  # a zero row: the norm clamps at 1e-12
+    dy = torch.randn_like(x)
+    xa = x.clone().requires_grad_(True)
+    y = l2norm_silu(xa, scale)
+    y.backward(dy)
+    xr = x.float().requires_grad_(True)
+    yr = F.normalize(F.silu(xr), dim=-1, eps=1e-12) * scale
+    yr.backward(dy.float())
+    assert torch.isfinite(y).all() and torch.isfinite(xa.grad).all()
+    assert rel_err(np_(y), np_(yr)) <= TOL
+    assert rel_err(np_(xa.grad), np_(xr.grad)) <= TOL
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_gated_rmsnorm(cuda, D):
+    torch.manual_seed(D + 1)
+    o = torch.randn(2, 50, 3, D, device=cuda).to(torch.bfloat16)
+    g = torch.randn_like(o)
+    w = torch.randn(D, device=cuda) * 0.5 + 1
+    dy = torch.randn_like(o)
+    oa, ga, wa = o.clone().requires_grad_(True), g.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    y = gated_rmsnorm(oa, ga, wa, 1e-5)
+    y.backward(dy)
+    orf, grf, wrf = o.float().requires_grad_(True), g.float().requires_grad_(True), w.clone().requires_grad_(True)
+    yr = orf * torch.rsqrt(orf.pow(2).mean(-1, keepdim=True) + 1e-5) * wrf * torch.sigmoid(grf)
+    yr.backward(dy.float())
+    assert rel_err(np_(y), np_(yr)) <= TOL
+    for a, b in ((oa.grad, orf.grad), (ga.grad, grf.grad), (wa.grad, wrf.grad)):
+        assert rel_err(np_(a), np_(b)) <= TOL
+
+
+def test_rowops_reject_bad_input(cuda):
+    with pytest.raises(ValueError):
+        l2norm_silu(torch.randn(4, 48, device=cuda).to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        l2norm_silu(torch.randn(4, 64, device=cuda))
