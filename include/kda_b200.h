@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 4
+#define KDA_ABI_VERSION 5
 
 enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
 
@@ -147,6 +147,16 @@ KDA_API int kda_l2norm_silu_bwd(int64_t rows, int D, const void *x, const void *
                                 void *stream);
 KDA_API int kda_gated_rmsnorm_fwd(int64_t rows, int D, const void *o, const void *gate, const float *w,
                                   void *y, float eps, void *stream);
+/* The layer's short causal depthwise convolution (kernel 4) with SiLU, and for q / k the L2 norm and
+ * scale (norm != 0), in one pass: x, y [B, T, H*D] bf16, w [H*D][4] and bias [H*D] float32.  The
+ * VJP writes dx (bf16) and dw, db (float32, overwritten) and needs a float32 [B, T, H*D] scratch.
+ * Replaces: ShortCausalConv1d (nope_gdn_mlx.py:400-431) applied at :793-795 and followed by the
+ * SiLU / L2 norm of :797-799. */
+KDA_API int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w,
+                              const float *bias, void *y, int norm, float scale, void *stream);
+KDA_API int kda_conv_silu_bwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w,
+                              const float *bias, const void *dy, void *dx, float *dw, float *db,
+                              int norm, float scale, float *dz_scratch, void *stream);
 KDA_API int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, const float *w,
                                   const void *dy, void *dout, void *dgate, float *dw, float eps,
                                   void *stream);

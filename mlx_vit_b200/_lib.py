@@ -12,7 +12,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkda_b200.so")
 
-KDA_ABI_VERSION = 4
+KDA_ABI_VERSION = 5
 KDA_F32, KDA_BF16, KDA_F16 = 0, 1, 2
 KDA_FLAG_FORCE_GENERIC = 0x1
 
@@ -27,7 +27,8 @@ KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_bytes",
            "kda_saved_bytes", "kda_launch_counter", "kda_device_status", "kda_fwd", "kda_bwd",
            "kda_bwd_noalloc", "kda_fwd_gated", "kda_bwd_gated", "kda_fwd_recurrent",
-           "kda_l2norm_silu_fwd", "kda_l2norm_silu_bwd", "kda_gated_rmsnorm_fwd", "kda_gated_rmsnorm_bwd")
+           "kda_l2norm_silu_fwd", "kda_l2norm_silu_bwd", "kda_gated_rmsnorm_fwd", "kda_gated_rmsnorm_bwd",
+           "kda_conv_silu_fwd", "kda_conv_silu_bwd")
 
 
 class KdaDesc(ctypes.Structure):
@@ -87,7 +88,9 @@ def _declare(L):
     for n, a in (("kda_l2norm_silu_fwd", [i64, I, P, P, f32, P]),
                  ("kda_l2norm_silu_bwd", [i64, I, P, P, P, f32, P]),
                  ("kda_gated_rmsnorm_fwd", [i64, I, P, P, P, P, f32, P]),
-                 ("kda_gated_rmsnorm_bwd", [i64, I, P, P, P, P, P, P, P, f32, P])):
+                 ("kda_gated_rmsnorm_bwd", [i64, I, P, P, P, P, P, P, P, f32, P]),
+                 ("kda_conv_silu_fwd", [i64, i64, I, I, P, P, P, P, I, f32, P]),
+                 ("kda_conv_silu_bwd", [i64, i64, I, I, P, P, P, P, P, P, P, I, f32, P, P])):
         getattr(L, n).restype = I
         getattr(L, n).argtypes = a
 

@@ -174,6 +174,131 @@ __global__ void __launch_bounds__(32 * kWarps) gated_rmsnorm_bwd_kernel(int64_t 
   }
 }
 
+// Short causal depthwise convolution (kernel 4, the reference's ShortCausalConv1d,
+// nope_gdn_mlx.py:400-431: z[t, c] = b[c] + sum_j w[c, j] x[t - 3 + j, c], zeros before t = 0)
+// followed by SiLU, and for q / k by the L2 norm and scale: one warp per (b, t, head) row, the
+// four input rows it reads come through L1.  x, y: [B, T, C] bf16 with C = H D; w [C][4], b [C] fp32.
+template <int E, bool NORM>
+__global__ void __launch_bounds__(32 * kWarps) conv_silu_fwd_kernel(int64_t rows, int T, int C, const __nv_bfloat16 *x,
+                                                                    const float *w, const float *bias,
+                                                                    __nv_bfloat16 *y, float scale) {
+  const int lane = threadIdx.x & 31, D = 32 * E, Hh = C / D;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    const int h = (int)(r % Hh);
+    const int64_t bt = r / Hh;
+    const int t = (int)(bt % T);
+    const int c0 = h * D + lane * E;
+    float z[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) z[i] = bias[c0 + i];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int ts = t - 3 + j;
+      if (ts < 0) continue;
+      float xv[E];
+      load_row<E>(x + (bt - 3 + j) * C + h * D, lane, xv);
+#pragma unroll
+      for (int i = 0; i < E; ++i) z[i] = fmaf(w[(c0 + i) * 4 + j], xv[i], z[i]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      z[i] *= sigm(z[i]);
+      ss += z[i] * z[i];
+    }
+    if (NORM) {
+      const float inv = scale / fmaxf(sqrtf(warp_sum(ss)), 1e-12f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) z[i] *= inv;
+    }
+    store_row<E>(y + bt * C + h * D, lane, z);
+  }
+}
+
+// backward, part 1: per row, dz = d/dz of silu (and the L2 norm) at z = conv(x), into fp32 dz
+template <int E, bool NORM>
+__global__ void __launch_bounds__(32 * kWarps) conv_silu_bwd_rows_kernel(int64_t rows, int T, int C,
+                                                                         const __nv_bfloat16 *x, const float *w,
+                                                                         const float *bias, const __nv_bfloat16 *dy,
+                                                                         float *dz, float scale) {
+  const int lane = threadIdx.x & 31, D = 32 * E, Hh = C / D;
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    const int h = (int)(r % Hh);
+    const int64_t bt = r / Hh;
+    const int t = (int)(bt % T);
+    const int c0 = h * D + lane * E;
+    float z[E], g[E], s[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) z[i] = bias[c0 + i];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (t - 3 + j < 0) continue;
+      float xv[E];
+      load_row<E>(x + (bt - 3 + j) * C + h * D, lane, xv);
+#pragma unroll
+      for (int i = 0; i < E; ++i) z[i] = fmaf(w[(c0 + i) * 4 + j], xv[i], z[i]);
+    }
+    load_row<E>(dy + bt * C + h * D, lane, g);
+    float ss = 0.f, sg = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      s[i] = z[i] * sigm(z[i]);
+      ss += s[i] * s[i];
+      sg += s[i] * g[i];
+    }
+    float inv = 1.f, proj = 0.f;
+    if (NORM) {
+      ss = warp_sum(ss);
+      sg = warp_sum(sg);
+      const float n = sqrtf(ss);
+      const bool clamp = !(n > 1e-12f);
+      inv = scale / (clamp ? 1e-12f : n);
+      proj = clamp ? 0.f : sg / ss;
+    }
+    float *out = dz + bt * C + c0;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const float sgm = sigm(z[i]);
+      out[i] = inv * (g[i] - s[i] * proj) * sgm * (1.f + z[i] * (1.f - sgm));
+    }
+  }
+}
+
+// backward, part 2: dx[t, c] = sum_j w[c, j] dz[t + 3 - j, c]; dw[c, j] += sum_t dz[t, c] x[t - 3 + j, c];
+// db[c] += sum_t dz[t, c].  Thread = channel, walking a segment of t with sliding windows.
+__global__ void __launch_bounds__(128) conv_bwd_cols_kernel(int B, int T, int C, int seg, const __nv_bfloat16 *x,
+                                                            const float *w, const float *dz, __nv_bfloat16 *dx,
+                                                            float *dw, float *db) {
+  const int c = blockIdx.x * 128 + threadIdx.x;
+  const int b = blockIdx.z, t0 = blockIdx.y * seg, t1 = min(T, t0 + seg);
+  if (c >= C || t0 >= T) return;
+  const float w0 = w[c * 4], w1 = w[c * 4 + 1], w2 = w[c * 4 + 2], w3 = w[c * 4 + 3];
+  const int64_t base = (int64_t)b * T * C + c;
+  auto X = [&](int t) { return t >= 0 ? __bfloat162float(x[base + (int64_t)t * C]) : 0.f; };
+  auto Z = [&](int t) { return t < T ? dz[base + (int64_t)t * C] : 0.f; };
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, ab = 0.f;
+  // window: dz[t .. t+3], x[t-3 .. t]
+  float z0 = Z(t0), z1 = Z(t0 + 1), z2 = Z(t0 + 2), z3 = Z(t0 + 3);
+  float xm3 = X(t0 - 3), xm2 = X(t0 - 2), xm1 = X(t0 - 1), x0 = X(t0);
+  for (int t = t0; t < t1; ++t) {
+    dx[base + (int64_t)t * C] = __float2bfloat16_rn(w3 * z0 + w2 * z1 + w1 * z2 + w0 * z3);
+    a0 = fmaf(z0, xm3, a0);
+    a1 = fmaf(z0, xm2, a1);
+    a2 = fmaf(z0, xm1, a2);
+    a3 = fmaf(z0, x0, a3);
+    ab += z0;
+    z0 = z1; z1 = z2; z2 = z3; z3 = Z(t + 4);
+    xm3 = xm2; xm2 = xm1; xm1 = x0; x0 = X(t + 1 < T ? t + 1 : -1);
+  }
+  atomicAdd(dw + c * 4, a0);
+  atomicAdd(dw + c * 4 + 1, a1);
+  atomicAdd(dw + c * 4 + 2, a2);
+  atomicAdd(dw + c * 4 + 3, a3);
+  atomicAdd(db + c, ab);
+}
+
 static int grid_for(int64_t rows) {
   static int nsm = 0;
   if (!nsm) {
@@ -236,6 +361,54 @@ int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, 
   if (cudaMemsetAsync(dw, 0, sizeof(float) * D, st) != cudaSuccess) return KDA_ERR_CUDA;
   KDA_ROW_LAUNCH(gated_rmsnorm_bwd_kernel, rows, D, st, (const __nv_bfloat16 *)o, (const __nv_bfloat16 *)gate, w,
                  (const __nv_bfloat16 *)dy, (__nv_bfloat16 *)dout, (__nv_bfloat16 *)dgate, dw, eps);
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+
+int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
+                      void *y, int norm, float scale, void *stream) {
+  const int64_t rows = B * T * H;
+  if (!row_args_ok(rows, D, {x, w, bias, y})) return KDA_ERR_INVALID_ARG;
+  const int C = H * D;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int g = grid_for(rows);
+  const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x;
+  __nv_bfloat16 *yb = (__nv_bfloat16 *)y;
+  if (D == 64) {
+    if (norm) conv_silu_fwd_kernel<2, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+    else conv_silu_fwd_kernel<2, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+  } else {
+    if (norm) conv_silu_fwd_kernel<4, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+    else conv_silu_fwd_kernel<4, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+  }
+  kda::count_launch();
+  return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
+}
+
+int kda_conv_silu_bwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
+                      const void *dy, void *dx, float *dw, float *db, int norm, float scale, float *dz_ws,
+                      void *stream) {
+  const int64_t rows = B * T * H;
+  if (!row_args_ok(rows, D, {x, w, bias, dy, dx, dw, db, dz_ws})) return KDA_ERR_INVALID_ARG;
+  const int C = H * D;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(dw, 0, sizeof(float) * C * 4, st) != cudaSuccess ||
+      cudaMemsetAsync(db, 0, sizeof(float) * C, st) != cudaSuccess)
+    return KDA_ERR_CUDA;
+  const int g = grid_for(rows);
+  const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x, *dyb = (const __nv_bfloat16 *)dy;
+  if (D == 64) {
+    if (norm) conv_silu_bwd_rows_kernel<2, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+    else conv_silu_bwd_rows_kernel<2, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+  } else {
+    if (norm) conv_silu_bwd_rows_kernel<4, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+    else conv_silu_bwd_rows_kernel<4, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+  }
+  kda::count_launch();
+  const int seg = 64;
+  dim3 grid((C + 127) / 128, (int)((T + seg - 1) / seg), (int)B);
+  conv_bwd_cols_kernel<<<grid, 128, 0, st>>>((int)B, (int)T, C, seg, xb, w, dz_ws, (__nv_bfloat16 *)dx, dw, db);
+  kda::count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
 

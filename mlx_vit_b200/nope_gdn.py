@@ -22,7 +22,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .kda import cuda_kda_gated
-from .rowops import gated_rmsnorm, l2norm_silu
+from .rowops import conv_silu, gated_rmsnorm
 
 
 class ShortCausalConv1d(nn.Module):
@@ -85,19 +85,21 @@ class GatedDeltaLayer(nn.Module):
         self.g_proj_2 = nn.Linear(D, tot, bias=True)
         self.o_norm = RMSNormGated(D)
         self.o_proj = nn.Linear(tot, hidden, bias=False)
-        self.fused_rows = True  # q/k prologue in the library's fused kernel; False: torch ops
+        self.fused_rows = True  # conv + SiLU (+ L2 norm) in the library's fused kernels; False: torch ops
 
     def forward(self, x, state=None):
         B, L, _ = x.shape
         H, D = self.H, self.D
         bf = torch.bfloat16
-        v = F.silu(self.v_conv1d(self.v_proj(x))).view(B, L, H, D)
-        qr = self.q_conv1d(self.q_proj(x)).view(B, L, H, D)
-        kr = self.k_conv1d(self.k_proj(x)).view(B, L, H, D)
-        if self.fused_rows:  # one pass each: the library's kda_l2norm_silu_* kernels
-            q = l2norm_silu(qr.to(bf), self.scale)
-            k = l2norm_silu(kr.to(bf), 1.0)
+        if self.fused_rows:  # conv + SiLU (+ L2 norm) in one pass each: kda_conv_silu_*
+            cv = lambda conv, t, norm, sc: conv_silu(t.to(bf), conv.weight, conv.bias, H, D, norm, sc)
+            q = cv(self.q_conv1d, self.q_proj(x), True, self.scale).view(B, L, H, D)
+            k = cv(self.k_conv1d, self.k_proj(x), True, 1.0).view(B, L, H, D)
+            v = cv(self.v_conv1d, self.v_proj(x), False, 1.0).view(B, L, H, D)
         else:
+            v = F.silu(self.v_conv1d(self.v_proj(x))).view(B, L, H, D)
+            qr = self.q_conv1d(self.q_proj(x)).view(B, L, H, D)
+            kr = self.k_conv1d(self.k_proj(x)).view(B, L, H, D)
             q = (F.normalize(F.silu(qr).float(), dim=-1) * self.scale).to(bf)
             k = F.normalize(F.silu(kr).float(), dim=-1).to(bf)
         f = self.f_proj_2(self.f_proj_1(x)).view(B, L, H, D).to(bf)

@@ -83,6 +83,47 @@ class GatedRMSNorm(torch.autograd.Function):
         return do, dg, dw.to(ctx.w_dtype), None
 
 
+class ConvSiLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, H, D, norm, scale):
+        x = x.contiguous()
+        if not x.is_cuda or x.dtype != torch.bfloat16 or D not in (64, 128) or x.shape[-1] != H * D:
+            raise ValueError("conv_silu takes a bf16 CUDA tensor [B, T, H*D] with D = 64 or 128")
+        B, T = x.shape[0], x.shape[1]
+        w32 = w.reshape(H * D, 4).to(torch.float32).contiguous()
+        b32 = b.to(torch.float32).contiguous()
+        y = torch.empty_like(x)
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.lib().kda_conv_silu_fwd(B, T, H, D, _ptr(x), _ptr(w32), _ptr(b32), _ptr(y), int(norm),
+                                                    float(scale), _stream(x)), "kda_conv_silu_fwd")
+        ctx.save_for_backward(x, w32, b32)
+        ctx.meta = (H, D, norm, scale, w.shape, w.dtype, b.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w32, b32 = ctx.saved_tensors
+        H, D, norm, scale, wshape, wdt, bdt = ctx.meta
+        dy = dy.to(torch.bfloat16).contiguous()
+        B, T = x.shape[0], x.shape[1]
+        dx = torch.empty_like(x)
+        dw = torch.empty_like(w32)
+        db = torch.empty_like(b32)
+        dz = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.lib().kda_conv_silu_bwd(B, T, H, D, _ptr(x), _ptr(w32), _ptr(b32), _ptr(dy), _ptr(dx),
+                                                    _ptr(dw), _ptr(db), int(norm), float(scale), _ptr(dz),
+                                                    _stream(x)), "kda_conv_silu_bwd")
+        return dx, dw.reshape(wshape).to(wdt), db.to(bdt), None, None, None, None
+
+
+def conv_silu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: int, head_dim: int,
+              norm: bool = False, scale: float = 1.0) -> torch.Tensor:
+    """silu(causal depthwise conv4(x)) over time for x [B, T, H*D] (bf16); with ``norm`` also the
+    per-head L2 norm and ``scale``.  ``weight`` is the conv's [C, 1, 4] (or [C, 4]) tensor."""
+    return ConvSiLU.apply(x, weight, bias, heads, head_dim, norm, scale)
+
+
 def l2norm_silu(x: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
     """y = silu(x) / max(||silu(x)||, 1e-12) * scale over the last dim (bf16 in and out)."""
     return L2NormSiLU.apply(x, scale)

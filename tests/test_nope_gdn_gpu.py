@@ -53,7 +53,9 @@ def test_layer_fused_gates_equal_unfused(cuda):
     # A_log and dt_bias gradients are sums over (B, T) of bf16 dg with cancellation, so two
     # bf16 paths differ in them by more (about 15 % here); the op-level tests pin them against
     # the oracle with the dg bound carried through the chain rule.  Every other gradient: 5e-2.
-    loose = {"A_log": 0.25, "dt_bias": 0.25}
+    # f_proj_1 / f_proj_2 receive df = dg (-A) sigmoid(x) summed over every token: the same
+    # bf16-dg noise, which the fused path's own bf16 roundings (conv, norms) move by a few %.
+    loose = {"A_log": 0.25, "dt_bias": 0.25, "f_proj_1.weight": 0.1, "f_proj_2.weight": 0.1}
     bad = {n: e for n, e in errs.items() if e > loose.get(n, 5e-2)}
     assert not bad, bad
 

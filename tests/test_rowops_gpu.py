@@ -57,3 +57,31 @@ def test_rowops_reject_bad_input(cuda):
         l2norm_silu(torch.randn(4, 48, device=cuda).to(torch.bfloat16))
     with pytest.raises(ValueError):
         l2norm_silu(torch.randn(4, 64, device=cuda))
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("norm", [False, True])
+def test_conv_silu(cuda, D, norm):
+    """Causal depthwise conv (kernel 4) + SiLU (+ L2 norm, scale) against F.conv1d in fp32."""
+    from mlx_vit_b200.rowops import conv_silu
+    torch.manual_seed(D + norm)
+    B, T, H = 2, 131, 3
+    C = H * D
+    x = torch.randn(B, T, C, device=cuda).to(torch.bfloat16)
+    w = torch.empty(C, 1, 4, device=cuda).uniform_(-0.5, 0.5)
+    b = torch.randn(C, device=cuda) * 0.1
+    dy = torch.randn_like(x)
+    scale = 0.125 if norm else 1.0
+    xa, wa, ba = x.clone().requires_grad_(True), w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    y = conv_silu(xa, wa, ba, H, D, norm, scale)
+    y.backward(dy)
+    xr, wr, br = x.float().requires_grad_(True), w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    z = F.conv1d(F.pad(xr.transpose(1, 2), (3, 0)), wr, br, groups=C).transpose(1, 2)
+    yr = F.silu(z)
+    if norm:
+        yr = (F.normalize(yr.view(B, T, H, D), dim=-1, eps=1e-12) * scale).view(B, T, C)
+    yr.backward(dy.float())
+    assert rel_err(np_(y), np_(yr)) <= TOL
+    for a, r in ((xa.grad, xr.grad), (wa.grad, wr.grad), (ba.grad, br.grad)):
+        assert torch.isfinite(a).all()
+        assert rel_err(np_(a), np_(r)) <= TOL
