@@ -208,6 +208,11 @@ def cuda_kda(q, k, v, g, beta, state: Optional[torch.Tensor] = None, chunk_size:
     need_grad = torch.is_grad_enabled() and any(
         x is not None and x.requires_grad for x in (q, k, v, g, beta, state))
     if need_grad:
+        # fail before the forward runs if no backward kernel covers the shape (e.g. D = 128)
+        st = _lib.lib().kda_check_desc(ctypes.byref(_desc(q, beta, chunk_size, flags)), 1)
+        if st:
+            raise ValueError(f"cuda_kda: gradients need a backward for this shape, which is not "
+                             f"available ({_lib.lib().kda_strerror(st).decode()})")
         return CudaKdaFunction.apply(q, k, v, g, beta, state, chunk_size, flags)
     if q.shape[1] <= RECURRENT_MAX_T and q.shape[3] in (16, 32, 64, 128) and not force_generic:
         return kda_recurrent(q, k, v, g, beta, state)

@@ -75,3 +75,12 @@ def test_d128_streaming_segments_equal_one_pass(cuda):
 
 def test_d128_no_device_wait_timed_out(cuda):
     assert _lib.lib().kda_device_status(0) == 0
+
+
+def test_d128_with_gradients_fails_before_running(cuda):
+    """No backward kernel covers D = 128: asking for gradients raises up front."""
+    inp = make_inputs(1, 64, 1, 128, seed=2, state_std=0.0, with_grads=False)
+    t = {k: torch.from_numpy(inp[k]).to(cuda) for k in ("q", "k", "v", "g", "beta")}
+    q = t["q"].to(torch.bfloat16).requires_grad_(True)
+    with pytest.raises(ValueError):
+        cuda_kda(q, t["k"].to(torch.bfloat16), t["v"].to(torch.bfloat16), t["g"], t["beta"].to(torch.bfloat16))
