@@ -10,6 +10,7 @@
 // backward of the epilogue recomputes the RMS from o and reduces dw over rows with one atomic
 // per channel per CTA.
 #include <initializer_list>
+#include <mutex>
 
 #include "kda_common.cuh"
 
@@ -299,13 +300,16 @@ __global__ void __launch_bounds__(128) conv_bwd_cols_kernel(int B, int T, int C,
   atomicAdd(db + c, ab);
 }
 
+// grid-stride launches: at most 8 CTAs per SM of the device current at the first call
 static int grid_for(int64_t rows) {
-  static int nsm = 0;
-  if (!nsm) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      nsm = 148;
-  }
+  static int nsm = 148;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      nsm = n;
+  });
   const int64_t need = (rows + kWarps - 1) / kWarps;
   return (int)(need < 8LL * nsm ? need : 8LL * nsm);
 }
