@@ -283,7 +283,45 @@ def streaming_d128_leg(args, L, dev, flush):
         e1.synchronize()
         ms.append(e0.elapsed_time(e1))
     t = statistics.mean(ms)
-    return {"workload": "cfg4 share of one GPU: B1 H2 D128 chunk64, 4 x 4096 tokens with the state "
+
+    # decoding: one token per call with the state carried, the step kernel (kda_fwd_recurrent)
+    # against the chunked forward (one padded chunk per call); 64 tokens per timed graph
+    ndec = 64
+    xd = {n: inp[n][:, :ndec].contiguous() for n in ("q", "k", "v", "g", "beta")}
+    tok = [{n: xd[n][:, i:i + 1] for n in xd} for i in range(ndec)]
+    sd = [inp["state"].clone()] + [torch.empty_like(inp["state"]) for _ in range(ndec)]
+    od = [torch.empty_like(x["q"]) for x in tok]
+    d1 = _desc(tok[0]["q"], tok[0]["beta"], CHUNK, 0)
+    nws1 = L.kda_workspace_bytes(ctypes.byref(d1), 0)
+    ws1 = torch.empty(max(nws1, 16), dtype=torch.uint8, device=dev)
+
+    def decode(recurrent):
+        for i, x in enumerate(tok):
+            args = (ctypes.byref(d1), _ptr(x["q"]), _ptr(x["k"]), _ptr(x["v"]), _ptr(x["g"]), _ptr(x["beta"]),
+                    _ptr(sd[i]), _ptr(od[i]), _ptr(sd[i + 1]))
+            if recurrent:
+                _lib.check(L.kda_fwd_recurrent(*args, stream()), "kda_fwd_recurrent")
+            else:
+                _lib.check(L.kda_fwd(*args, None, _ptr(ws1), nws1, stream()), "kda_fwd")
+    dec = {}
+    for name, rec in (("recurrent", True), ("chunked", False)):
+        for _ in range(2):
+            decode(rec)
+        torch.cuda.synchronize()
+        gd = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gd):
+            decode(rec)
+        for _ in range(3):
+            gd.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(max(1, args.steps // 4)):
+            gd.replay()
+        e1.record()
+        e1.synchronize()
+        dec[name + "_us_per_token"] = round(e0.elapsed_time(e1) * 1e3 / (max(1, args.steps // 4) * ndec), 2)
+    return {"decode_d128": dict(dec, workload="one token per call, B1 H2 D128, state carried (CUDA graph of 64 calls)"),
+            "workload": "cfg4 share of one GPU: B1 H2 D128 chunk64, 4 x 4096 tokens with the state "
                         "carried (bf16 I/O, fp32 g/state), forward", "ms_per_step": round(t, 4),
             "tokens_per_s": round(Bs * Ts * nseg / (t / 1e3), 1), "gpu_launches_per_step": int(launches)}
 
