@@ -22,9 +22,11 @@
  * Conventions
  *   - All pointers are device pointers; buffers are owned by the caller; the library keeps no
  *     allocation of its own and writes only the listed outputs (and the caller's workspace).
- *   - Layouts are dense row-major:  q, k, g, dO, dq, dk, dg: [B, T, H, Dk];  v, o, dv: [B, T,
- *     H, Dv];  beta, dbeta: [B, T, H];  state0, stateT, dstateT, dstate0: [B, H, Dv, Dk]
- *     float32.  `saved` is an opaque device buffer of kda_saved_bytes() bytes that kda_fwd fills
+ *   - Layouts are row-major [B, T, H, D]:  q, k, g, dO, dq, dk, dg: [B, T, H, Dk];  v, o, dv:
+ *     [B, T, H, Dv];  beta, dbeta: [B, T, H];  state0, stateT, dstateT, dstate0: [B, H, Dv, Dk]
+ *     float32.  The inputs q, k, v, g, beta, dO may be strided views (KdaDesc strides, the
+ *     head dimension unit-stride; the reference's (B, L, H, D) arrays are read without the head
+ *     fold of nope_gdn_mlx.py:833-838); every output is dense.  `saved` is an opaque device buffer of kda_saved_bytes() bytes that kda_fwd fills
  *     and kda_bwd reads (per-chunk entry states and WY values); pass it between the two calls
  *     with the same descriptor.
  *   - dtype_qkv applies to q, k, v, o, dO, dq, dk, dv;  dtype_beta to beta and dbeta;
@@ -49,7 +51,7 @@
 extern "C" {
 #endif
 
-#define KDA_ABI_VERSION 5
+#define KDA_ABI_VERSION 6
 
 enum kda_dtype { KDA_F32 = 0, KDA_BF16 = 1, KDA_F16 = 2 };
 
@@ -68,6 +70,17 @@ enum kda_status {
 /* Flags for KdaDesc.flags */
 #define KDA_FLAG_FORCE_GENERIC 0x1  /* use the fp32 SIMT kernels even where a tensor-core
                                        kernel exists (testing / fp32-exact arithmetic) */
+#define KDA_FLAG_DEBUG_WAIT_TIMEOUT 0x2  /* testing only: the tensor-core forward's state scan
+                                       first waits (a few polls) on a barrier that nothing
+                                       completes, so its bounded-wait failure path runs: the
+                                       call returns 0, kda_device_status() then reports
+                                       KDA_ERR_TIMEOUT and the output is not written */
+
+/* Element strides of one input along batch, time and head; the last axis (D) is unit-stride.
+ * All three zero means the dense layout ([B, T, H, D]: T*H*D, H*D, D; [B, T, H]: T*H, H, 1). */
+typedef struct KdaStrides {
+  int64_t b, t, h;
+} KdaStrides;
 
 typedef struct KdaDesc {
   int64_t B, T, H;     /* batch, sequence length, heads                          */
@@ -77,6 +90,12 @@ typedef struct KdaDesc {
   int32_t dtype_beta;  /* enum kda_dtype                                         */
   int32_t flags;       /* KDA_FLAG_*                                             */
   int32_t reserved;
+  /* input views read in place (e.g. q, k, v as slices of one fused projection, time-major
+   * [B, T, H, D] with any b / t / h strides).  The tensor-core kernels read them by TMA, which
+   * needs every nonzero stride times the element size to be a multiple of 16 bytes (else
+   * KDA_ERR_MISALIGNED).  With the fused gates, f takes g's strides and b beta's.  Outputs,
+   * states and the saved record are always dense. */
+  KdaStrides q, k, v, g, beta, dO;
 } KdaDesc;
 
 /* ABI version of the loaded library (KDA_ABI_VERSION it was built with). */
@@ -136,20 +155,25 @@ KDA_API int kda_fwd_recurrent(const KdaDesc *desc, const void *q, const void *k,
                               float *stateT, void *stream);
 
 /* The layer's row operations around the recurrence, one fused pass each (bf16 I/O, fp32
- * arithmetic, rows of D = 64 or 128 contiguous elements, 16-byte aligned pointers):
- *   kda_l2norm_silu_fwd:  y = l2norm(silu(x)) * scale   (q: scale = D^-1/2, k: 1)
- *   kda_gated_rmsnorm_fwd: y = rmsnorm(o) * w * sigmoid(gate), w float32 [D]
+ * arithmetic, 16-byte aligned pointers):
+ *   kda_l2norm_silu_fwd:  y = l2norm(silu(x)) * scale over rows of n contiguous elements (n a
+ *                         multiple of 8, at most 8192).  In the layer a row is one token's whole
+ *                         H*D channel vector (q: scale = D^-1/2, k: 1), as the reference
+ *                         normalises before its head reshape (nope_gdn_mlx.py:797-799, :818-821).
+ *   kda_gated_rmsnorm_fwd: y = rmsnorm(o) * w * sigmoid(gate) over rows of D = 64 or 128 (one
+ *                         head), w float32 [D]
  * and their VJPs (dw float32 [D], overwritten).
  * Replaces: GatedDeltaLayer.__call__'s "SiLU + L2 norm + scale" lines (nope_gdn_mlx.py:797-799,
  * l2_normalize :76-79) and its output RMSNormGated (:340-371, applied at :880-885). */
-KDA_API int kda_l2norm_silu_fwd(int64_t rows, int D, const void *x, void *y, float scale, void *stream);
-KDA_API int kda_l2norm_silu_bwd(int64_t rows, int D, const void *x, const void *dy, void *dx, float scale,
+KDA_API int kda_l2norm_silu_fwd(int64_t rows, int n, const void *x, void *y, float scale, void *stream);
+KDA_API int kda_l2norm_silu_bwd(int64_t rows, int n, const void *x, const void *dy, void *dx, float scale,
                                 void *stream);
 KDA_API int kda_gated_rmsnorm_fwd(int64_t rows, int D, const void *o, const void *gate, const float *w,
                                   void *y, float eps, void *stream);
-/* The layer's short causal depthwise convolution (kernel 4) with SiLU, and for q / k the L2 norm and
- * scale (norm != 0), in one pass: x, y [B, T, H*D] bf16, w [H*D][4] and bias [H*D] float32.  The
- * VJP writes dx (bf16) and dw, db (float32, overwritten) and needs a float32 [B, T, H*D] scratch.
+/* The layer's short causal depthwise convolution (kernel 4) with SiLU, and for q / k the L2 norm
+ * over each token's whole H*D channel row and the scale (norm != 0), in one pass: x, y [B, T, H*D]
+ * bf16 (H*D a multiple of 8, at most 8192), w [H*D][4] and bias [H*D] float32.  The VJP writes dx
+ * (bf16) and dw, db (float32, overwritten) and needs a float32 [B, T, H*D] scratch.
  * Replaces: ShortCausalConv1d (nope_gdn_mlx.py:400-431) applied at :793-795 and followed by the
  * SiLU / L2 norm of :797-799. */
 KDA_API int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w,

@@ -12,15 +12,17 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libkda_b200.so")
 
-KDA_ABI_VERSION = 5
+KDA_ABI_VERSION = 6
 KDA_F32, KDA_BF16, KDA_F16 = 0, 1, 2
 KDA_FLAG_FORCE_GENERIC = 0x1
+KDA_FLAG_DEBUG_WAIT_TIMEOUT = 0x2
 
 STATUS = {
     0: "KDA_OK", -1: "KDA_ERR_INVALID_ARG", -2: "KDA_ERR_UNSUPPORTED", -3: "KDA_ERR_DTYPE",
     -4: "KDA_ERR_MISALIGNED", -5: "KDA_ERR_WORKSPACE", -6: "KDA_ERR_CUDA", -7: "KDA_ERR_TIMEOUT",
     -8: "KDA_ERR_SCRATCH_LIMIT",
 }
+STATUS_CODE = {v: k for k, v in STATUS.items()}
 KDA_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 # every symbol include/kda_b200.h declares
@@ -31,11 +33,18 @@ EXPORTS = ("kda_abi_version", "kda_strerror", "kda_check_desc", "kda_workspace_b
            "kda_conv_silu_fwd", "kda_conv_silu_bwd")
 
 
+class KdaStrides(ctypes.Structure):
+    """Element strides (b, t, h) of one input; all zero = dense (include/kda_b200.h)."""
+    _fields_ = [("b", ctypes.c_int64), ("t", ctypes.c_int64), ("h", ctypes.c_int64)]
+
+
 class KdaDesc(ctypes.Structure):
     _fields_ = [("B", ctypes.c_int64), ("T", ctypes.c_int64), ("H", ctypes.c_int64),
                 ("Dk", ctypes.c_int64), ("Dv", ctypes.c_int64), ("chunk", ctypes.c_int64),
                 ("dtype_qkv", ctypes.c_int32), ("dtype_beta", ctypes.c_int32),
-                ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("flags", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("q", KdaStrides), ("k", KdaStrides), ("v", KdaStrides), ("g", KdaStrides),
+                ("beta", KdaStrides), ("dO", KdaStrides)]
 
 
 class KdaGate(ctypes.Structure):

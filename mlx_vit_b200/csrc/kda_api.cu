@@ -32,6 +32,8 @@ using kda::Params;
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+static bool strides_ok(const KdaStrides &s) { return s.b >= 0 && s.t >= 0 && s.h >= 0; }
+
 static int dtype_ok(int dt) { return dt == KDA_F32 || dt == KDA_BF16 || dt == KDA_F16; }
 
 static int check_desc_shape(const KdaDesc *d) {
@@ -43,6 +45,9 @@ static int check_desc_shape(const KdaDesc *d) {
     return KDA_ERR_UNSUPPORTED;
   if (d->Dk != d->Dv) return KDA_ERR_UNSUPPORTED;  // the reference state is D x D
   if (d->chunk > 64 || d->Dk > 128) return KDA_ERR_UNSUPPORTED;
+  if (!strides_ok(d->q) || !strides_ok(d->k) || !strides_ok(d->v) || !strides_ok(d->g) ||
+      !strides_ok(d->beta) || !strides_ok(d->dO))
+    return KDA_ERR_INVALID_ARG;
   return KDA_OK;
 }
 
@@ -107,10 +112,31 @@ size_t kda_saved_bytes(const KdaDesc *d) {
   return (size_t)(d->B * d->H * nc * d->Dk * d->Dv) * sizeof(float);
 }
 
+// an input's strides: the descriptor's, or the dense layout when all three are zero
+static kda::Str input_strides(const KdaStrides &s, const KdaDesc *d, bool per_head_vector) {
+  if (s.b == 0 && s.t == 0 && s.h == 0) {
+    const int64_t D = per_head_vector ? d->Dk : 1;
+    return kda::Str{d->T * d->H * D, d->H * D, D};
+  }
+  return kda::Str{s.b, s.t, s.h};
+}
+
+// TMA reads need every stride of a tile-loaded input to span a multiple of 16 bytes
+static bool tma_strides_ok(const kda::Str &s, int elem_bytes) {
+  return (s.b * elem_bytes) % 16 == 0 && (s.t * elem_bytes) % 16 == 0 && (s.h * elem_bytes) % 16 == 0;
+}
+
 static Params make_params(const KdaDesc *d) {
   Params p = {};
   p.B = (int)d->B; p.T = (int)d->T; p.H = (int)d->H; p.D = (int)d->Dk; p.C = (int)d->chunk;
   p.nc = (int)((d->T + d->chunk - 1) / d->chunk);
+  p.sq = input_strides(d->q, d, true);
+  p.sk = input_strides(d->k, d, true);
+  p.sv = input_strides(d->v, d, true);
+  p.sg = input_strides(d->g, d, true);
+  p.sb = input_strides(d->beta, d, false);
+  p.sdo = input_strides(d->dO, d, true);
+  p.debug_wait_polls = (d->flags & KDA_FLAG_DEBUG_WAIT_TIMEOUT) ? 64 : 0;
   return p;
 }
 
@@ -129,8 +155,12 @@ int kda_fwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta; p.state0 = state0;
   p.o = o; p.stateT = stateT; p.saved = saved; p.ws = ws;
   cudaStream_t st = (cudaStream_t)stream;
-  if (use_tc(d, 0) && (!saved || use_tc(d, 1))) return kda::tc_fwd(p, d->dtype_beta, st);
-  if (use_tc128(d, 0) && !saved) return kda::tc128_fwd(p, d->dtype_beta, st);
+  const bool tc = use_tc(d, 0) && (!saved || use_tc(d, 1)), tc128 = !tc && use_tc128(d, 0) && !saved;
+  if ((tc || tc128) && !(tma_strides_ok(p.sq, 2) && tma_strides_ok(p.sk, 2) && tma_strides_ok(p.sv, 2) &&
+                         tma_strides_ok(p.sg, 4)))
+    return KDA_ERR_MISALIGNED;
+  if (tc) return kda::tc_fwd(p, d->dtype_beta, st);
+  if (tc128) return kda::tc128_fwd(p, d->dtype_beta, st);
   return kda::generic_fwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 
@@ -154,7 +184,12 @@ int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
   p.saved_in = saved; p.dO = dO; p.dstateT = dstateT; p.ws = ws;
   p.dq = dq; p.dk = dk; p.dv = dv; p.dg = dg; p.dbeta = dbeta; p.dstate0 = dstate0;
   cudaStream_t st = (cudaStream_t)stream;
-  if (use_tc(d, 1)) return kda::tc_bwd(p, d->dtype_beta, st);
+  if (use_tc(d, 1)) {
+    if (!(tma_strides_ok(p.sq, 2) && tma_strides_ok(p.sk, 2) && tma_strides_ok(p.sv, 2) &&
+          tma_strides_ok(p.sg, 4) && tma_strides_ok(p.sdo, 2)))
+      return KDA_ERR_MISALIGNED;
+    return kda::tc_bwd(p, d->dtype_beta, st);
+  }
   return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 
@@ -174,6 +209,10 @@ static int check_gate(const KdaDesc *d, const KdaGate *gate) {
   if (!gate || !gate->f || !gate->A_log || !gate->dt_bias || !gate->b) return KDA_ERR_INVALID_ARG;
   if (!use_tc(d, 1)) return KDA_ERR_UNSUPPORTED;  // the gates are fused into the tensor-core kernels only
   if (!aligned16(gate->f)) return KDA_ERR_MISALIGNED;
+  const Params p = make_params(d);
+  if (!(tma_strides_ok(p.sq, 2) && tma_strides_ok(p.sk, 2) && tma_strides_ok(p.sv, 2) &&
+        tma_strides_ok(p.sg, 2) && tma_strides_ok(p.sdo, 2)))
+    return KDA_ERR_MISALIGNED;
   return KDA_OK;
 }
 

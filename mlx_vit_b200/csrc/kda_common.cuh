@@ -13,9 +13,18 @@ namespace kda {
 // Kernel launch counter behind kda_launch_counter(); every launch site bumps it.
 void count_launch();
 
-// Kernel parameter block shared by every KDA kernel.  Element strides are those of the dense
-// [B, T, H, D] / [B, T, H] / [B, H, Dv, Dk] layouts of the C ABI.
+// Element strides (batch, time, head) of one input; the last axis is unit-stride.
+struct Str {
+  int64_t b, t, h;
+};
+__device__ __forceinline__ int64_t at(const Str &s, int b, int t, int h, int d = 0) {
+  return (int64_t)b * s.b + (int64_t)t * s.t + (int64_t)h * s.h + d;
+}
+
+// Kernel parameter block shared by every KDA kernel.  Outputs, states and records use the dense
+// [B, T, H, D] / [B, T, H] / [B, H, Dv, Dk] layouts of the C ABI; the inputs carry strides.
 struct Params {
+  Str sq, sk, sv, sg, sb, sdo;  // input strides (f uses sg, the gate logits sb)
   int B, T, H, D, C, nc;       // D = Dk = Dv, C = chunk, nc = ceil(T / C)
   const void *q, *k, *v, *beta;
   const float *g, *state0, *dstateT;
@@ -33,6 +42,9 @@ struct Params {
   const float *A_log, *dt_bias;
   void *df;
   float *dA_log, *ddt_bias;
+  // test hook (KDA_FLAG_DEBUG_WAIT_TIMEOUT): > 0 makes the forward's state scan first wait this
+  // many polls on a barrier that nothing completes, so that its bounded-wait failure path runs
+  int debug_wait_polls;
 };
 
 // softplus as the reference's (nope_gdn_mlx.py:83-86): log1p(e^{-|x|}) + max(x, 0)

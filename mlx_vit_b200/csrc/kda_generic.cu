@@ -54,18 +54,17 @@ kda_fwd_generic_kernel(Params p, int DVS) {
     for (int i = tid; i < C * D; i += nt) {
       int t = i / D, d = i % D, tt = t0 + t;
       bool in = tt < T;
-      int64_t o = off_bthd(b, tt, h, d, T, H, D);
-      K[i] = in ? to_f(k[o]) : 0.f;
-      Q[i] = in ? to_f(q[o]) : 0.f;
-      Gm[i] = in ? p.g[o] : 0.f;
+      K[i] = in ? to_f(k[at(p.sk, b, tt, h, d)]) : 0.f;
+      Q[i] = in ? to_f(q[at(p.sq, b, tt, h, d)]) : 0.f;
+      Gm[i] = in ? p.g[at(p.sg, b, tt, h, d)] : 0.f;
     }
     for (int i = tid; i < C * DVS; i += nt) {
       int t = i / DVS, j = i % DVS, tt = t0 + t;
-      V[i] = tt < T ? to_f(v[off_bthd(b, tt, h, j0 + j, T, H, D)]) : 0.f;
+      V[i] = tt < T ? to_f(v[at(p.sv, b, tt, h, j0 + j)]) : 0.f;
     }
     for (int t = tid; t < C; t += nt) {
       int tt = t0 + t;
-      bet[t] = tt < T ? to_f(beta[((int64_t)b * T + tt) * H + h]) : 0.f;
+      bet[t] = tt < T ? to_f(beta[at(p.sb, b, tt, h)]) : 0.f;
     }
     __syncthreads();
     for (int d = tid; d < D; d += nt) {  // gamma = cumsum(g) over the chunk
@@ -152,16 +151,15 @@ __device__ void bwd_chunk_body(const Params &p, float *sm, int bh, int c, bool u
   for (int i = tid; i < C * D; i += nt) {
     int t = i / D, d = i % D, tt = t0 + t;
     bool in = tt < T;
-    int64_t o = off_bthd(b, tt, h, d, T, H, D);
-    K[i] = in ? to_f(k[o]) : 0.f;
-    Q[i] = in ? to_f(q[o]) : 0.f;
-    Gm[i] = in ? p.g[o] : 0.f;
-    Y[i] = in ? to_f(v[o]) : 0.f;
-    dO[i] = in ? to_f(dOg[o]) : 0.f;
+    K[i] = in ? to_f(k[at(p.sk, b, tt, h, d)]) : 0.f;
+    Q[i] = in ? to_f(q[at(p.sq, b, tt, h, d)]) : 0.f;
+    Gm[i] = in ? p.g[at(p.sg, b, tt, h, d)] : 0.f;
+    Y[i] = in ? to_f(v[at(p.sv, b, tt, h, d)]) : 0.f;
+    dO[i] = in ? to_f(dOg[at(p.sdo, b, tt, h, d)]) : 0.f;
   }
   for (int t = tid; t < C; t += nt) {
     int tt = t0 + t;
-    bet[t] = tt < T ? to_f(beta[((int64_t)b * T + tt) * H + h]) : 0.f;
+    bet[t] = tt < T ? to_f(beta[at(p.sb, b, tt, h)]) : 0.f;
   }
   __syncthreads();
   for (int d = tid; d < D; d += nt) {

@@ -125,8 +125,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t mbar, uint32_t parity) {
 // records KDA_ERR_TIMEOUT and bails out) if it has not completed after kMbarSpinLimit polls,
 // each of which already blocks for a hardware-chosen interval.
 constexpr int kMbarSpinLimit = 1 << 22;
-__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
-  for (int i = 0; i < kMbarSpinLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, int limit = kMbarSpinLimit) {
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(mbar, parity)) return true;
   return false;
 }
@@ -159,12 +159,34 @@ __device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void *src, uin
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n"
                :: "r"(dst), "l"(src), "r"(bytes), "r"(mbar), "l"(pol) : "memory");
 }
+// one arrival of this thread (release: its earlier shared-memory writes are visible to the thread
+// that completes a wait on the phase)
+__device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n" :: "r"(mbar) : "memory");
+}
+// wait until at most N of this thread's bulk store groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" :: "n"(N) : "memory");
+}
+// hint: bring `bytes` (a multiple of 16) at a 16-byte aligned global address into L2
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" :: "l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 __device__ __forceinline__ void bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;\n" :: "r"(id), "r"(n) : "memory");
+}
+// named barrier over n threads that also returns whether c held for all of them
+__device__ __forceinline__ bool bar_and(int id, int n, bool c) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r) : "r"((uint32_t)c), "r"(id), "r"(n) : "memory");
+  return r != 0;
 }
 __device__ __forceinline__ void bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;\n" :: "r"(id), "r"(n) : "memory");

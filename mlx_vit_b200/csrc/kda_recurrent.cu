@@ -44,14 +44,13 @@ __global__ void __launch_bounds__((D < 32 ? D : 32) * (D > 64 ? 2 : 1)) kda_recu
     for (int m = 0; m < PER; ++m) {
       const int d = tid + NT * m;
       if (d < D) {
-        const int64_t off = off_bthd(b, t, h, d, T, H, D);
-        nk[m] = to_f(k[off]);
-        nq[m] = to_f(q[off]);
-        ng[m] = p.g[off];
+        nk[m] = to_f(k[at(p.sk, b, t, h, d)]);
+        nq[m] = to_f(q[at(p.sq, b, t, h, d)]);
+        ng[m] = p.g[at(p.sg, b, t, h, d)];
       }
     }
-    nv = to_f(v[off_bthd(b, t, h, j, T, H, D)]);
-    nb = to_f(beta[((int64_t)b * T + t) * H + h]);
+    nv = to_f(v[at(p.sv, b, t, h, j)]);
+    nb = to_f(beta[at(p.sb, b, t, h)]);
   };
   if (T > 0) load(0);
   for (int t = 0; t < T; ++t) {

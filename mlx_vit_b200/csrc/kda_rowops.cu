@@ -1,10 +1,13 @@
-// The GDN layer's per-head row operations around the recurrence, fused into one pass each
-// (bf16 I/O, fp32 arithmetic, one warp per row of D = 64 or 128 elements):
+// The GDN layer's row operations around the recurrence, fused into one pass each (bf16 I/O,
+// fp32 arithmetic):
 //
-//   prologue  y = l2norm(silu(x)) * scale     q and k after the short convolutions
-//             (nope_gdn_mlx.py:797-799 with l2_normalize :76-79: x / max(||x||, 1e-12))
-//   epilogue  y = rmsnorm(o) * w * sigmoid(gate)   the output's gated RMSNorm
-//             (RMSNormGated / _gated_rms_norm :340-371, applied at :880-885)
+//   prologue  y = l2norm(silu(x)) * scale     q and k after the short convolutions, the norm
+//             taken over the whole H*D channel row as the reference does before its head
+//             reshape (nope_gdn_mlx.py:797-799 with l2_normalize :76-79: x / max(||x||, 1e-12);
+//             reshape :818-821); one CTA per row, a block reduction
+//   epilogue  y = rmsnorm(o) * w * sigmoid(gate)   the output's gated RMSNorm over each head's
+//             D channels (RMSNormGated(D) / _gated_rms_norm :340-371 on the (B, L, H, D)
+//             output, :880-885); one warp per row
 //
 // and their VJPs.  The backward of the prologue recomputes silu(x) and the norm from x; the
 // backward of the epilogue recomputes the RMS from o and reduces dw over rows with one atomic
@@ -44,58 +47,126 @@ __device__ __forceinline__ void store_row(__nv_bfloat16 *p, int lane, const floa
   for (int i = 0; i < E / 2; ++i) q[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
 }
 
-template <int E>
-__global__ void __launch_bounds__(32 * kWarps) l2norm_silu_fwd_kernel(int64_t rows, const __nv_bfloat16 *x,
+// ---- row-wide L2 norm: one CTA of kRowThreads per row of n channels (the layer's whole H*D
+// row, which the reference normalises before its head reshape, nope_gdn_mlx.py:797-799 then
+// :818-821).  A thread owns chunks of 8 consecutive channels (16-byte loads), chunk
+// tid + kRowThreads * k for k < KC, so n <= 8 * kRowThreads * KC. ----
+constexpr int kRowThreads = 128;
+constexpr int kRowMaxChunks = 8;  // n <= 8192
+
+// sum over the CTA; `red` holds two slots per warp so that consecutive rows need one barrier each
+__device__ __forceinline__ float2 block_sum2(float2 v, float2 (*red)[kRowThreads / 32], int parity) {
+  v.x = warp_sum(v.x);
+  v.y = warp_sum(v.y);
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  if (lane == 0) red[parity][wp] = v;
+  __syncthreads();
+  float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; ++i) {
+    s.x += red[parity][i].x;
+    s.y += red[parity][i].y;
+  }
+  return s;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
+    x[2 * e] = f.x;
+    x[2 * e + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16 *p, const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
+    w[e] = *reinterpret_cast<uint32_t *>(&v);
+  }
+  *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int KC>
+__global__ void __launch_bounds__(kRowThreads) l2norm_silu_fwd_kernel(int64_t rows, int n, const __nv_bfloat16 *x,
                                                                       __nv_bfloat16 *y, float scale) {
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
-    float v[E];
-    load_row<E>(x + r * 32 * E, lane, v);
+  __shared__ float2 red[2][kRowThreads / 32];
+  const int nch = n >> 3;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    float v[KC][8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      v[i] *= sigm(v[i]);
-      ss += v[i] * v[i];
-    }
-    const float inv = scale / fmaxf(sqrtf(warp_sum(ss)), 1e-12f);
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+        load8(x + r * n + 8 * c, v[k]);
 #pragma unroll
-    for (int i = 0; i < E; ++i) v[i] *= inv;
-    store_row<E>(y + r * 32 * E, lane, v);
+        for (int i = 0; i < 8; ++i) {
+          v[k][i] *= sigm(v[k][i]);
+          ss += v[k][i] * v[k][i];
+        }
+      }
+    }
+    const float inv = scale / fmaxf(sqrtf(block_sum2(make_float2(ss, 0.f), red, parity).x), 1e-12f);
+#pragma unroll
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[k][i] *= inv;
+        store8(y + r * n + 8 * c, v[k]);
+      }
+    }
   }
 }
 
-// y = scale s / max(n, eps), s = silu(x), n = ||s||:
-//   ds = scale (dy - s (s . dy) / n^2) / n  (n > eps; else scale dy / eps);  dx = ds silu'(x)
-template <int E>
-__global__ void __launch_bounds__(32 * kWarps) l2norm_silu_bwd_kernel(int64_t rows, const __nv_bfloat16 *x,
+// y = scale s / max(N, eps), s = silu(x), N = ||s|| over the row:
+//   ds = scale (dy - s (s . dy) / N^2) / N  (N > eps; else scale dy / eps);  dx = ds silu'(x)
+template <int KC>
+__global__ void __launch_bounds__(kRowThreads) l2norm_silu_bwd_kernel(int64_t rows, int n, const __nv_bfloat16 *x,
                                                                       const __nv_bfloat16 *dy,
                                                                       __nv_bfloat16 *dx, float scale) {
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
-    float v[E], g[E], s[E];
-    load_row<E>(x + r * 32 * E, lane, v);
-    load_row<E>(dy + r * 32 * E, lane, g);
+  __shared__ float2 red[2][kRowThreads / 32];
+  const int nch = n >> 3;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    float v[KC][8], g[KC][8];
     float ss = 0.f, sg = 0.f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      s[i] = v[i] * sigm(v[i]);
-      ss += s[i] * s[i];
-      sg += s[i] * g[i];
-    }
-    ss = warp_sum(ss);
-    sg = warp_sum(sg);
-    const float n = sqrtf(ss);
-    const bool clamp = !(n > 1e-12f);
-    const float inv = scale / (clamp ? 1e-12f : n), proj = clamp ? 0.f : sg / ss;
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+        load8(x + r * n + 8 * c, v[k]);
+        load8(dy + r * n + 8 * c, g[k]);
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      const float sgm = sigm(v[i]);
-      const float ds = inv * (g[i] - s[i] * proj);
-      g[i] = ds * sgm * (1.f + v[i] * (1.f - sgm));
+        for (int i = 0; i < 8; ++i) {
+          const float s = v[k][i] * sigm(v[k][i]);
+          ss += s * s;
+          sg += s * g[k][i];
+        }
+      }
     }
-    store_row<E>(dx + r * 32 * E, lane, g);
+    const float2 red2 = block_sum2(make_float2(ss, sg), red, parity);
+    const float N = sqrtf(red2.x);
+    const bool clamp = !(N > 1e-12f);
+    const float inv = scale / (clamp ? 1e-12f : N), proj = clamp ? 0.f : red2.y / red2.x;
+#pragma unroll
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float sgm = sigm(v[k][i]), s = v[k][i] * sgm;
+          const float ds = inv * (g[k][i] - s * proj);
+          g[k][i] = ds * sgm * (1.f + v[k][i] * (1.f - sgm));
+        }
+        store8(dx + r * n + 8 * c, g[k]);
+      }
+    }
   }
 }
 
@@ -177,92 +248,125 @@ __global__ void __launch_bounds__(32 * kWarps) gated_rmsnorm_bwd_kernel(int64_t 
 
 // Short causal depthwise convolution (kernel 4, the reference's ShortCausalConv1d,
 // nope_gdn_mlx.py:400-431: z[t, c] = b[c] + sum_j w[c, j] x[t - 3 + j, c], zeros before t = 0)
-// followed by SiLU, and for q / k by the L2 norm and scale: one warp per (b, t, head) row, the
-// four input rows it reads come through L1.  x, y: [B, T, C] bf16 with C = H D; w [C][4], b [C] fp32.
-template <int E, bool NORM>
-__global__ void __launch_bounds__(32 * kWarps) conv_silu_fwd_kernel(int64_t rows, int T, int C, const __nv_bfloat16 *x,
-                                                                    const float *w, const float *bias,
-                                                                    __nv_bfloat16 *y, float scale) {
-  const int lane = threadIdx.x & 31, D = 32 * E, Hh = C / D;
-  const int64_t stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
-    const int h = (int)(r % Hh);
-    const int64_t bt = r / Hh;
-    const int t = (int)(bt % T);
-    const int c0 = h * D + lane * E;
-    float z[E];
+// followed by SiLU, and for q / k by the L2 norm over the whole C = H D channel row (the
+// reference normalises before its head reshape, :797-799 then :818-821) and the scale: one CTA
+// per (b, t) row, the four input rows it reads come through L1.  x, y: [B, T, C] bf16;
+// w [C][4], b [C] fp32.
+template <int KC>
+__device__ __forceinline__ void conv_row(int64_t r, int t, int C, const __nv_bfloat16 *x, const float *w,
+                                         const float *bias, float (&z)[KC][8]) {
+  const int nch = C >> 3;
 #pragma unroll
-    for (int i = 0; i < E; ++i) z[i] = bias[c0 + i];
+  for (int k = 0; k < KC; ++k) {
+    const int c = threadIdx.x + kRowThreads * k;
+    if (c >= nch) continue;
+    const int c0 = 8 * c;
+    const float4 b0 = *reinterpret_cast<const float4 *>(bias + c0);
+    const float4 b1 = *reinterpret_cast<const float4 *>(bias + c0 + 4);
+    z[k][0] = b0.x; z[k][1] = b0.y; z[k][2] = b0.z; z[k][3] = b0.w;
+    z[k][4] = b1.x; z[k][5] = b1.y; z[k][6] = b1.z; z[k][7] = b1.w;
+    float wt[8][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int ts = t - 3 + j;
-      if (ts < 0) continue;
-      float xv[E];
-      load_row<E>(x + (bt - 3 + j) * C + h * D, lane, xv);
-#pragma unroll
-      for (int i = 0; i < E; ++i) z[i] = fmaf(w[(c0 + i) * 4 + j], xv[i], z[i]);
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = *reinterpret_cast<const float4 *>(w + (c0 + i) * 4);
+      wt[i][0] = q.x; wt[i][1] = q.y; wt[i][2] = q.z; wt[i][3] = q.w;
     }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < E; ++i) {
-      z[i] *= sigm(z[i]);
-      ss += z[i] * z[i];
-    }
-    if (NORM) {
-      const float inv = scale / fmaxf(sqrtf(warp_sum(ss)), 1e-12f);
-#pragma unroll
-      for (int i = 0; i < E; ++i) z[i] *= inv;
-    }
-    store_row<E>(y + bt * C + h * D, lane, z);
-  }
-}
-
-// backward, part 1: per row, dz = d/dz of silu (and the L2 norm) at z = conv(x), into fp32 dz
-template <int E, bool NORM>
-__global__ void __launch_bounds__(32 * kWarps) conv_silu_bwd_rows_kernel(int64_t rows, int T, int C,
-                                                                         const __nv_bfloat16 *x, const float *w,
-                                                                         const float *bias, const __nv_bfloat16 *dy,
-                                                                         float *dz, float scale) {
-  const int lane = threadIdx.x & 31, D = 32 * E, Hh = C / D;
-  const int64_t stride = (int64_t)gridDim.x * kWarps;
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
-    const int h = (int)(r % Hh);
-    const int64_t bt = r / Hh;
-    const int t = (int)(bt % T);
-    const int c0 = h * D + lane * E;
-    float z[E], g[E], s[E];
-#pragma unroll
-    for (int i = 0; i < E; ++i) z[i] = bias[c0 + i];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (t - 3 + j < 0) continue;
-      float xv[E];
-      load_row<E>(x + (bt - 3 + j) * C + h * D, lane, xv);
+      float xv[8];
+      load8(x + (r - 3 + j) * C + c0, xv);
 #pragma unroll
-      for (int i = 0; i < E; ++i) z[i] = fmaf(w[(c0 + i) * 4 + j], xv[i], z[i]);
+      for (int i = 0; i < 8; ++i) z[k][i] = fmaf(wt[i][j], xv[i], z[k][i]);
     }
-    load_row<E>(dy + bt * C + h * D, lane, g);
+  }
+}
+
+template <int KC, bool NORM>
+__global__ void __launch_bounds__(kRowThreads) conv_silu_fwd_kernel(int64_t rows, int T, int C, const __nv_bfloat16 *x,
+                                                                    const float *w, const float *bias,
+                                                                    __nv_bfloat16 *y, float scale) {
+  __shared__ float2 red[2][kRowThreads / 32];
+  const int nch = C >> 3;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    const int t = (int)(r % T);
+    float z[KC][8];
+    conv_row<KC>(r, t, C, x, w, bias, z);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < KC; ++k)
+      if (threadIdx.x + kRowThreads * k < nch)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          z[k][i] *= sigm(z[k][i]);
+          ss += z[k][i] * z[k][i];
+        }
+    float inv = 1.f;
+    if (NORM) inv = scale / fmaxf(sqrtf(block_sum2(make_float2(ss, 0.f), red, parity).x), 1e-12f);
+#pragma unroll
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+        if (NORM)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) z[k][i] *= inv;
+        store8(y + r * C + 8 * c, z[k]);
+      }
+    }
+  }
+}
+
+// backward, part 1: per (b, t) row, dz = d/dz of silu (and the row-wide L2 norm) at z = conv(x),
+// into fp32 dz
+template <int KC, bool NORM>
+__global__ void __launch_bounds__(kRowThreads) conv_silu_bwd_rows_kernel(int64_t rows, int T, int C,
+                                                                         const __nv_bfloat16 *x, const float *w,
+                                                                         const float *bias, const __nv_bfloat16 *dy,
+                                                                         float *dz, float scale) {
+  __shared__ float2 red[2][kRowThreads / 32];
+  const int nch = C >> 3;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    const int t = (int)(r % T);
+    float z[KC][8], g[KC][8];
+    conv_row<KC>(r, t, C, x, w, bias, z);
     float ss = 0.f, sg = 0.f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      s[i] = z[i] * sigm(z[i]);
-      ss += s[i] * s[i];
-      sg += s[i] * g[i];
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+        load8(dy + r * C + 8 * c, g[k]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float s = z[k][i] * sigm(z[k][i]);
+          ss += s * s;
+          sg += s * g[k][i];
+        }
+      }
     }
     float inv = 1.f, proj = 0.f;
     if (NORM) {
-      ss = warp_sum(ss);
-      sg = warp_sum(sg);
-      const float n = sqrtf(ss);
-      const bool clamp = !(n > 1e-12f);
-      inv = scale / (clamp ? 1e-12f : n);
-      proj = clamp ? 0.f : sg / ss;
+      const float2 s2 = block_sum2(make_float2(ss, sg), red, parity);
+      const float N = sqrtf(s2.x);
+      const bool clamp = !(N > 1e-12f);
+      inv = scale / (clamp ? 1e-12f : N);
+      proj = clamp ? 0.f : s2.y / s2.x;
     }
-    float *out = dz + bt * C + c0;
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      const float sgm = sigm(z[i]);
-      out[i] = inv * (g[i] - s[i] * proj) * sgm * (1.f + z[i] * (1.f - sgm));
+    for (int k = 0; k < KC; ++k) {
+      const int c = threadIdx.x + kRowThreads * k;
+      if (c < nch) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float sgm = sigm(z[k][i]), s = z[k][i] * sgm;
+          o[i] = inv * (g[k][i] - s * proj) * sgm * (1.f + z[k][i] * (1.f - sgm));
+        }
+        float4 *out = reinterpret_cast<float4 *>(dz + r * C + 8 * c);
+        out[0] = make_float4(o[0], o[1], o[2], o[3]);
+        out[1] = make_float4(o[4], o[5], o[6], o[7]);
+      }
     }
   }
 }
@@ -336,17 +440,41 @@ static bool row_args_ok(int64_t rows, int D, std::initializer_list<const void *>
 
 extern "C" {
 
-int kda_l2norm_silu_fwd(int64_t rows, int D, const void *x, void *y, float scale, void *stream) {
-  if (!row_args_ok(rows, D, {x, y})) return KDA_ERR_INVALID_ARG;
-  KDA_ROW_LAUNCH(l2norm_silu_fwd_kernel, rows, D, (cudaStream_t)stream, (const __nv_bfloat16 *)x,
-                 (__nv_bfloat16 *)y, scale);
+// row-wide kernels: chunks of 8 channels per thread, KC chunks at most
+static int row_chunks(int n) {
+  const int per = (n / 8 + kRowThreads - 1) / kRowThreads;
+  return per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : per <= kRowMaxChunks ? 8 : 0;
+}
+static bool wide_row_ok(int64_t rows, int n, std::initializer_list<const void *> ptrs) {
+  if (rows <= 0 || n <= 0 || (n & 7) || !row_chunks(n)) return false;
+  for (const void *p : ptrs)
+    if (!p || ((uintptr_t)p & 15u)) return false;
+  return true;
+}
+static int wide_grid(int64_t rows) { return (int)(rows < 8LL * 148 * 4 ? rows : 8LL * 148 * 4); }
+
+#define KDA_WIDE_LAUNCH(kern, kc, g, st, ...)                                     \
+  do {                                                                            \
+    switch (kc) {                                                                 \
+      case 1: kern<1><<<g, kRowThreads, 0, st>>>(__VA_ARGS__); break;             \
+      case 2: kern<2><<<g, kRowThreads, 0, st>>>(__VA_ARGS__); break;             \
+      case 4: kern<4><<<g, kRowThreads, 0, st>>>(__VA_ARGS__); break;             \
+      default: kern<8><<<g, kRowThreads, 0, st>>>(__VA_ARGS__); break;            \
+    }                                                                             \
+    kda::count_launch();                                                          \
+  } while (0)
+
+int kda_l2norm_silu_fwd(int64_t rows, int n, const void *x, void *y, float scale, void *stream) {
+  if (!wide_row_ok(rows, n, {x, y})) return KDA_ERR_INVALID_ARG;
+  KDA_WIDE_LAUNCH(l2norm_silu_fwd_kernel, row_chunks(n), wide_grid(rows), (cudaStream_t)stream, rows, n,
+                  (const __nv_bfloat16 *)x, (__nv_bfloat16 *)y, scale);
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
 
-int kda_l2norm_silu_bwd(int64_t rows, int D, const void *x, const void *dy, void *dx, float scale, void *stream) {
-  if (!row_args_ok(rows, D, {x, dy, dx})) return KDA_ERR_INVALID_ARG;
-  KDA_ROW_LAUNCH(l2norm_silu_bwd_kernel, rows, D, (cudaStream_t)stream, (const __nv_bfloat16 *)x,
-                 (const __nv_bfloat16 *)dy, (__nv_bfloat16 *)dx, scale);
+int kda_l2norm_silu_bwd(int64_t rows, int n, const void *x, const void *dy, void *dx, float scale, void *stream) {
+  if (!wide_row_ok(rows, n, {x, dy, dx})) return KDA_ERR_INVALID_ARG;
+  KDA_WIDE_LAUNCH(l2norm_silu_bwd_kernel, row_chunks(n), wide_grid(rows), (cudaStream_t)stream, rows, n,
+                  (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)dy, (__nv_bfloat16 *)dx, scale);
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
 
@@ -371,20 +499,23 @@ int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, 
 
 int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
                       void *y, int norm, float scale, void *stream) {
-  const int64_t rows = B * T * H;
-  if (!row_args_ok(rows, D, {x, w, bias, y})) return KDA_ERR_INVALID_ARG;
+  const int64_t rows = B * T;
   const int C = H * D;
+  if (H <= 0 || D <= 0 || !wide_row_ok(rows, C, {x, w, bias, y})) return KDA_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const int g = grid_for(rows);
+  const int g = wide_grid(rows), kc = row_chunks(C);
   const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x;
   __nv_bfloat16 *yb = (__nv_bfloat16 *)y;
-  if (D == 64) {
-    if (norm) conv_silu_fwd_kernel<2, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
-    else conv_silu_fwd_kernel<2, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
-  } else {
-    if (norm) conv_silu_fwd_kernel<4, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
-    else conv_silu_fwd_kernel<4, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+#define KDA_CONV_FWD(KC)                                                                                       \
+  if (norm) conv_silu_fwd_kernel<KC, true><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale); \
+  else conv_silu_fwd_kernel<KC, false><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
+  switch (kc) {
+    case 1: KDA_CONV_FWD(1) break;
+    case 2: KDA_CONV_FWD(2) break;
+    case 4: KDA_CONV_FWD(4) break;
+    default: KDA_CONV_FWD(8) break;
   }
+#undef KDA_CONV_FWD
   kda::count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
@@ -392,22 +523,25 @@ int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const f
 int kda_conv_silu_bwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
                       const void *dy, void *dx, float *dw, float *db, int norm, float scale, float *dz_ws,
                       void *stream) {
-  const int64_t rows = B * T * H;
-  if (!row_args_ok(rows, D, {x, w, bias, dy, dx, dw, db, dz_ws})) return KDA_ERR_INVALID_ARG;
+  const int64_t rows = B * T;
   const int C = H * D;
+  if (H <= 0 || D <= 0 || !wide_row_ok(rows, C, {x, w, bias, dy, dx, dw, db, dz_ws})) return KDA_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(dw, 0, sizeof(float) * C * 4, st) != cudaSuccess ||
       cudaMemsetAsync(db, 0, sizeof(float) * C, st) != cudaSuccess)
     return KDA_ERR_CUDA;
-  const int g = grid_for(rows);
+  const int g = wide_grid(rows), kc = row_chunks(C);
   const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x, *dyb = (const __nv_bfloat16 *)dy;
-  if (D == 64) {
-    if (norm) conv_silu_bwd_rows_kernel<2, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
-    else conv_silu_bwd_rows_kernel<2, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
-  } else {
-    if (norm) conv_silu_bwd_rows_kernel<4, true><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
-    else conv_silu_bwd_rows_kernel<4, false><<<g, 32 * kWarps, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+#define KDA_CONV_BWD(KC)                                                                                          \
+  if (norm) conv_silu_bwd_rows_kernel<KC, true><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale); \
+  else conv_silu_bwd_rows_kernel<KC, false><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+  switch (kc) {
+    case 1: KDA_CONV_BWD(1) break;
+    case 2: KDA_CONV_BWD(2) break;
+    case 4: KDA_CONV_BWD(4) break;
+    default: KDA_CONV_BWD(8) break;
   }
+#undef KDA_CONV_BWD
   kda::count_launch();
   const int seg = 64;
   dim3 grid((C + 127) / 128, (int)((T + seg - 1) / seg), (int)B);

@@ -76,12 +76,17 @@ static bool ensure_context() {
   return retain(&ctx, cu) == CUDA_SUCCESS && set_cur(ctx) == CUDA_SUCCESS;
 }
 
-int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32) {
+int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32,
+                 const Str *st) {
   PFN_cuTensorMapEncodeTiled fn = encode_fn();
   if (!fn || !ensure_context()) return KDA_ERR_CUDA;
   const int64_t es = fp32 ? 4 : 2;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(H * D * es), (cuuint64_t)(T * H * D * es)};
+  const Str dense = {T * H * D, H * D, D};
+  const Str &s = st ? *st : dense;
+  const cuuint64_t strides[3] = {(cuuint64_t)(s.h * es), (cuuint64_t)(s.t * es), (cuuint64_t)(s.b * es)};
+  for (int i = 0; i < 3; ++i)
+    if (strides[i] % 16) return KDA_ERR_MISALIGNED;
   const cuuint32_t box[4] = {(cuuint32_t)(fp32 ? 32 : 64), 1, 64, 1};  // 128 bytes per box row
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,

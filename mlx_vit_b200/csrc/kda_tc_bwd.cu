@@ -40,6 +40,11 @@ static __device__ int g_bwd_status;
 
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
+// the block-pair factors e^{r_i - r_j} of a chunk that is not "big" stay above fp32's smallest
+// normal (e^-87) only if gamma moves at most this much between the middle rows of the first and
+// the last block; beyond it the factor would flush to zero while the decay it stands for
+// (e^{gamma_t - gamma_s} for t, s close to the block boundary) is not negligible
+constexpr float kMidGapMax = 80.f;
 constexpr float kLog2e = 1.4426950408889634f;  // the big-chunk copy of gamma is kept in log2 units
 
 // workspace: the exit cotangent of every chunk (bf16 [j][d], swizzled)
@@ -82,9 +87,11 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
   __syncthreads();
   // dO tile by TMA; Mneg, Qt, e^{gamma_C} (one contiguous, already swizzled span of the saved
   // record) by one bulk copy; both complete on the buffer's mbarrier
+  int issued = 0;  // thread 0: steps whose loads are issued
   auto issue = [&](int c, int buf) {
     const uint8_t *rec = (const uint8_t *)p.saved_in + ((int64_t)bh * nc + c) * kSavedChunk;
     if (tid == 0) {
+      issued = nc - c;
       mbar_expect_tx(mbar + buf * 8, 8192 + kSavedChunk - kSavedM);
       tma_load_rows(s_base + SC_DO + buf * 8192, &tm.m[0], h, c * C, b, mbar + buf * 8);
       bulk_g2s(s_base + SC_RC + buf * SC_RCB, rec + kSavedM, kSavedChunk - kSavedM, mbar + buf * 8);
@@ -114,7 +121,11 @@ __global__ void __launch_bounds__(SC_NT, 1) kda_bwd_state_scan_kernel(Params p, 
     const int c = nc - 1 - i, buf = i % SC_NB;
     if (tid == 0) bulk_wait_read_all();  // the exit-cotangent store of step i - 2 has read its staging
     if (__syncthreads_or(!mbar_wait(mbar + buf * 8, (i / SC_NB) & 1))) {
-      if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+      if (tid == 0) {  // (bounded) the loads in flight land and the stores read their staging
+        atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+        for (int s2 = i; s2 < issued; ++s2) mbar_wait(mbar + (s2 % SC_NB) * 8, (s2 / SC_NB) & 1);
+        bulk_wait_all();
+      }
       return;
     }
     if (i + 2 < nc) issue(c - 2, (i + 2) % SC_NB);
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   // beta of the next chunk, kept raw until its use so that the load does not stall anyone
   auto load_beta = [&](int i) -> Tb {
     const int bh_ = i / nc, t = (i % nc) * C + tid;
-    return t < T ? betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H] : from_f<Tb>(0.f);
+    return t < T ? betag[at(p.sb, bh_ / H, t, bh_ % H)] : from_f<Tb>(0.f);
   };
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) mbar_init(mbar + 8 * i, 1);
@@ -270,7 +281,10 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   // ---- P0: this chunk's inputs (bounded waits) ----
   if (__syncthreads_or(!mbar_wait(mbar, it & 1) || !mbar_wait(mbar + 8, it & 1) ||
                        !mbar_wait(mbar + 16, it & 1))) {
-    if (tid == 0) atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+    if (tid == 0) {  // (bounded) the loads in flight land before the CTA exits
+      atomicExch(&g_bwd_status, KDA_ERR_TIMEOUT);
+      for (int s2 = 0; s2 < 3; ++s2) mbar_wait(mbar + 8 * s2, it & 1);
+    }
     break;
   }
   const int nvalid = min(C, T - t0);
@@ -306,6 +320,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       span = fmaxf(span, GS[gsw(i * 16, tid)] - GS[gsw(i * 16 + 8, tid)]);
       span = fmaxf(span, GS[gsw(i * 16 + 8, tid)] - GS[gsw(i * 16 + 15, tid)]);
     }
+    if (!(GS[gsw(8, tid)] - GS[gsw(56, tid)] <= kMidGapMax)) span = 2.f * kSpanMax;
     bigloc = !(span <= kSpanMax);
   }
   // a "big" chunk (decay too strong for the factored form) keeps gamma itself and takes exact
@@ -823,8 +838,11 @@ int launch(const Params &p, cudaStream_t st) {
   TmaMaps tm;  // 0 q, 1 k, 2 v, 3 dO, 4 g (loads); 5 dq, 6 dk, 7 dg (stores)
   const void *base[8] = {p.q, p.k, p.v, p.dO, p.gated ? p.f : (const void *)p.g, p.dq, p.dk,
                          p.gated ? p.df : (void *)p.dg};
+  const Str in_str[5] = {p.sq, p.sk, p.sv, p.sdo, p.sg};  // the loads read strided inputs
   for (int i = 0; i < 8; ++i)
-    if (int e = tma_map_bthd(&tm.m[i], base[i], p.B, p.T, p.H, D, (i == 4 || i == 7) && !p.gated)) return e;
+    if (int e = tma_map_bthd(&tm.m[i], base[i], p.B, p.T, p.H, D, (i == 4 || i == 7) && !p.gated,
+                             i < 5 ? &in_str[i] : nullptr))
+      return e;
   TmaMaps tms;
   tms.m[0] = tm.m[3];
   if (cudaFuncSetAttribute(kda_bwd_state_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM))

@@ -36,13 +36,23 @@ static __device__ int g_fwd_status;
 
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
+// the block-pair factors e^{r_i - r_j} of a chunk that is not "big" stay above fp32's smallest
+// normal (e^-87) only if gamma moves at most this much between the middle rows of the first and
+// the last block; beyond it the factor would flush to zero while the decay it stands for
+// (e^{gamma_t - gamma_s} for t, s close to the block boundary) is not negligible
+constexpr float kMidGapMax = 80.f;
 
-// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan (bf16 tiles, swizzled): Qd [t][d]
-// and -W [t][d] (together the 128-row A operand of the scan's first MMA), U [t][j], P [t][s]
-// (zero above the diagonal) and Kb^T [d][t] (together the A operand of its second MMA), and
-// e^{gamma_C} (fp32)
-constexpr int HO_QD = 0, HO_W = 8192, HO_U = 16384, HO_P = 24576, HO_KBT = 32768, HO_EG = 40960;
+// the chunk kernel's tiles of per-chunk values in shared memory (bf16, swizzled): Qd = q e^gamma
+// [t][d], -W [t][d], U [t][j], P [t][s] (zero above the diagonal), e^{gamma_C} (fp32)
+constexpr int HO_QD = 0, HO_W = 8192, HO_U = 16384, HO_P = 24576, HO_EG = 40960;
 constexpr int HO_SIZE = 40960 + 256;
+// per-chunk record handed from kda_fwd_chunks to kda_fwd_scan in the forward workspace (bf16
+// tiles, swizzled as in shared memory): Mneg = -Kb^T W [d][d'], Qt = Qd - P W [t][d], -W [t][d],
+// U [t][j], O_intra = P U [t][j], N = Kb^T U [d][j], e^{gamma_C} (fp32).  With a saved record
+// (training) Mneg, Qt and e^{gamma_C} go there instead and the scan reads them from it.
+constexpr int WS_MN = 0, WS_QT = 8192, WS_W = 16384, WS_U = 24576, WS_OI = 32768, WS_N = 40960,
+              WS_EG = 49152;
+constexpr int WS_SIZE = 49152 + 256;
 
 // ---------------------------------------------------------------------------------------
 // kda_fwd_chunks
@@ -178,7 +188,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
   // beta of the next chunk, kept raw until its use so that the load does not stall anyone
   auto load_beta = [&](int i) -> Tb {
     const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
-    return t < T ? betag[((int64_t)(bh_ / H) * T + t) * H + bh_ % H] : from_f<Tb>(0.f);
+    return t < T ? betag[at(p.sb, bh_ / H, t, bh_ % H)] : from_f<Tb>(0.f);
   };
   // P's blocks above the diagonal are zero (the scan multiplies the whole tile); nothing else
   // writes them, so they are cleared once
@@ -193,7 +203,10 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 
   for (int it = 0; idx < nchunks; idx += gridDim.x, ++it) {
   if (__syncthreads_or(!mbar_wait(mbar, it & 1))) {  // this chunk's q, k, v, g
-    if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+    if (tid == 0) {
+      atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+      mbar_wait(mbar, it & 1);  // (bounded) the loads in flight land before the CTA exits
+    }
     break;
   }
   const int nvalid = min(C, T - (idx % nc) * C);
@@ -231,6 +244,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       span = fmaxf(span, GS[gsw(i * 16, tid)] - GS[gsw(i * 16 + 8, tid)]);
       span = fmaxf(span, GS[gsw(i * 16 + 8, tid)] - GS[gsw(i * 16 + 15, tid)]);
     }
+    if (!(GS[gsw(8, tid)] - GS[gsw(56, tid)] <= kMidGapMax)) span = 2.f * kSpanMax;
     const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
     if (lane == 0) flag[warp] = any;
   }
@@ -479,92 +493,83 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
           *reinterpret_cast<uint32_t *>(Y + sw64(16 * i + g4 + 8 * hh, c0 + 8 * nt + 2 * c4)) =
               pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
     }
-    {  // Kb^T: warp (i, q) transposes the 16 x 16 block (rows 16 i, columns 16 q) of Kb
-      const int i = warp >> 2, q = warp & 3;
-      uint32_t r[4];
-      ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * i, 16 * q, lane), r);
-      stsm_x4(ho + HO_KBT + sw64(16 * q + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * i + (lane >> 4) * 8), r[0], r[1],
-              r[2], r[3]);
-    }
   }
 
-  fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
-  // ---- the record for kda_fwd_scan: one bulk copy, same swizzled layout as in smem ----
-  if (tid == 0) {
-    // the record stays in L2 for kda_fwd_scan; the saved record streams out
-    bulk_s2g_hint((uint8_t *)p.ws + (int64_t)idx * HO_SIZE, ho, HO_SIZE, l2_policy_keep());
-    if (p.saved) {  // P, M, Tinv for the backward
-      uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
-      const uint64_t pol = l2_policy_stream();
-      bulk_s2g_hint(sv + kSavedP, ho + HO_P, 8192, pol);
-      bulk_s2g_hint(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192, pol);
-    }
-    bulk_commit();
-  }
-  // ---- the state-independent part of the backward's record: Mneg = Kb^T (-W) (warps 0-7) and
-  //      Qt = Qd + P (-W) (warps 8-15), each warp 16 rows x 32 columns ----
-  if (p.saved) {
-    uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
+  // ---- (6) the state-independent products the scan and the backward need, each warp 16 rows x
+  //      64 columns of one of
+  //        [Mneg | N]       = Kb^T [-W | U]          (warps 0-7, rows d)
+  //        [Qt | O_intra]   = [Qd | 0] + P [-W | U]  (warps 8-15, rows t; P is lower triangular)
+  //      so that the scan advances S^T <- diag(e^{gamma_C}) S^T + Mneg S^T + N with one MMA per
+  //      chunk and forms O = Qt S^T + O_intra and Unew = U - W S^T beside it ----
+  {
     const int rb = (warp >> 1) & 3, jb = rb * 16, nh = warp & 1;
-    float X[4][4];
-    if (warp < 8) {  // Mneg rows d' in [jb, jb+16)
+    const uint32_t bsrc = ho + (nh ? HO_U : HO_W);
+    float X[8][4];
+    if (warp >= 8 && nh == 0) {  // Qt starts from Qd
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) X[nt][e] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t af[4];
-        ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * kk, jb, lane), af);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t bf[4];
-          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 32 * nh + 16 * np, lane), bf);
-          mma16816(X[2 * np], af, bf[0], bf[1]);
-          mma16816(X[2 * np + 1], af, bf[2], bf[3]);
-        }
-      }
-    } else {  // Qt rows t in [jb, jb+16)
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const float2 v = unpack_bf16(*reinterpret_cast<const uint32_t *>(
-              hom + HO_QD + sw64(jb + g4 + 8 * hh, 32 * nh + nt * 8 + 2 * c4)));
+              hom + HO_QD + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)));
           X[nt][2 * hh] = v.x;
           X[nt][2 * hh + 1] = v.y;
         }
+    } else {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        if (kk > rb) break;
-        uint32_t af[4];
-        ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);
+      for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int np = 0; np < 2; ++np) {
-          uint32_t bf[4];
-          ldsm_x4_t(bkn_frag_addr(ho + HO_W, 16 * kk, 32 * nh + 16 * np, lane), bf);
-          mma16816(X[2 * np], af, bf[0], bf[1]);
-          mma16816(X[2 * np + 1], af, bf[2], bf[3]);
-        }
+        for (int e = 0; e < 4; ++e) X[nt][e] = 0.f;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      if (warp >= 8 && kk > rb) break;
+      uint32_t af[4];
+      if (warp < 8)
+        ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * kk, jb, lane), af);  // Kb^T rows d, k = t
+      else
+        ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);            // P rows t, k = s
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_t(bkn_frag_addr(bsrc, 16 * kk, 16 * np, lane), bf);
+        mma16816(X[2 * np], af, bf[0], bf[1]);
+        mma16816(X[2 * np + 1], af, bf[2], bf[3]);
       }
     }
-    uint8_t *dst = sm + (warp < 8 ? OFF_XK : OFF_XV);  // staged in the free beta-Kd / beta-V tiles
+    // staged in tiles that are free by now: Mneg -> beta-Kd, Qt -> beta-V, N -> Kdec, O_intra -> Qdec
+    uint8_t *dst = sm + (warp < 8 ? (nh ? OFF_KD : OFF_XK) : (nh ? OFF_QD : OFF_XV));
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh)
-        *reinterpret_cast<uint32_t *>(dst + sw64(jb + g4 + 8 * hh, 32 * nh + nt * 8 + 2 * c4)) =
+        *reinterpret_cast<uint32_t *>(dst + sw64(jb + g4 + 8 * hh, nt * 8 + 2 * c4)) =
             pack_bf16(X[nt][2 * hh], X[nt][2 * hh + 1]);
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {  // Mneg, Qt (staged in the free beta-Kd / beta-V tiles) and e^{gamma_C}
-      const uint64_t pol = l2_policy_stream();
-      bulk_s2g_hint(sv + kSavedM, s_base + OFF_XK, 8192, pol);
-      bulk_s2g_hint(sv + kSavedQt, s_base + OFF_XV, 8192, pol);
-      bulk_s2g_hint(sv + kSavedEG, ho + HO_EG, 256, pol);
-      bulk_commit();
+  }
+  fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
+  __syncthreads();
+  // ---- the scan's record (ws) and, for training, the backward's record (saved): bulk copies
+  //      of the swizzled tiles as they lie in shared memory ----
+  if (tid == 0) {
+    uint8_t *wr = (uint8_t *)p.ws + (int64_t)idx * WS_SIZE;
+    const uint64_t keep = l2_policy_keep(), stream = l2_policy_stream();
+    bulk_s2g_hint(wr + WS_W, ho + HO_W, 2 * 8192, keep);          // -W | U
+    bulk_s2g_hint(wr + WS_OI, s_base + OFF_QD, 8192, keep);       // O_intra
+    bulk_s2g_hint(wr + WS_N, s_base + OFF_KD, 8192, keep);        // N
+    if (p.saved) {  // Mneg, Qt and e^{gamma_C} live in the saved record, where the scan reads them
+      uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
+      bulk_s2g_hint(sv + kSavedM, s_base + OFF_XK, 8192, keep);
+      bulk_s2g_hint(sv + kSavedQt, s_base + OFF_XV, 8192, keep);
+      bulk_s2g_hint(sv + kSavedEG, ho + HO_EG, 256, keep);
+      bulk_s2g_hint(sv + kSavedP, ho + HO_P, 8192, stream);
+      bulk_s2g_hint(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192, stream);  // M | Tinv
+    } else {
+      bulk_s2g_hint(wr + WS_MN, s_base + OFF_XK, 8192, keep);
+      bulk_s2g_hint(wr + WS_QT, s_base + OFF_XV, 8192, keep);
+      bulk_s2g_hint(wr + WS_EG, ho + HO_EG, 256, keep);
     }
+    bulk_commit();
   }
   }  // chunk loop
   if (tid == 0) bulk_wait_all();
@@ -573,28 +578,39 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 // ---------------------------------------------------------------------------------------
 // kda_fwd_scan
 // ---------------------------------------------------------------------------------------
-// One CTA of 5 warps per (b, h), on the tcgen05 tensor cores with one M = 128 accumulator in
-// TMEM (64 columns).  Per chunk, with Sᵀ [d][j] and Unew [t][j] as bf16 B operands in shared
-// memory and the record's stacked A operands [Qd; -W] and [P; Kb^T]:
-//   MMA A:  D = [Qd; -W] S^T            rows 0-63: Qd S^T,  rows 64-127: -W S^T
-//   warps 2-3 (rows 64-127): Unew = U - W S^T -> bf16 tile; then put e^{gamma_C} S^T (fp32
-//   state rows d, kept in registers) into rows 64-127 of D
-//   MMA B:  D += [P; Kb^T] Unew         rows 0-63: O = Qd S^T + P Unew,
-//                                       rows 64-127: S^T <- diag(e^{gamma_C}) S^T + Kb^T Unew
-//   warps 0-1 drain O (bf16, TMA store); warps 2-3 take the new state.
-// One thread of warp 4 issues the MMAs, the record loads (a three-slot ring of bulk copies, two
-// chunks ahead) and the stores; S^T | Unew of each chunk leave by one bulk store for the
-// backward.  Every CTA-wide barrier votes on failures, so a bounded wait that gives up takes
-// all warps out together.
-constexpr int NT2 = 160;
-constexpr int NREC = 3;                       // record ring
-constexpr int NSV = 3;                        // S^T | Unew tiles (B operands and saved-record staging)
-constexpr int REC_STRIDE = 41 * 1024;         // ring slot (HO_SIZE rounded up to 1024 bytes)
-constexpr int OFF2_O = 0;                     // O staging, 2 x 8 KB (TMA stores)
-constexpr int OFF2_SV = 2 * 8192;             // NSV x 16 KB
-constexpr int OFF2_REC = OFF2_SV + NSV * 16384;  // NREC x REC_STRIDE
-constexpr int OFF2_MBAR = OFF2_REC + NREC * REC_STRIDE;  // NREC record mbarriers, 2 MMA mbarriers, TMEM slot
-constexpr int SMEM2 = OFF2_MBAR + 64;
+// One CTA per (b, h) walks the chunks in order.  The state recurrence of a chunk is linear in
+// the state, with every other term precomputed by the chunk kernel:
+//     S^T <- diag(e^{gamma_C}) S^T + Mneg S^T + N          (Mneg = -Kb^T W, N = Kb^T U)
+// so only ONE tcgen05 MMA (Mneg S^T, K = 64) lies on the chain from one chunk's state to the
+// next; the fp32 state stays in registers (the diagonal decay is applied there exactly) and a
+// bf16 copy of S^T is the MMA's B operand.  The outputs come off the chain:
+//     O = Qt S^T + O_intra,   Unew = U - W S^T             (Qt = Qd - P W, O_intra = P U)
+// Per chunk two MMAs read S^T: MMA1 = [Mneg; -W] S^T into accumulator D1 (M = 128: rows 0-63
+// the state product, rows 64-127 -W S^T) and MMA2 = [Qt; .] S^T into D2 (rows 0-63; rows
+// 64-127 are not used).  Both accumulators are double-buffered in TMEM (256 columns).
+// Warp roles (TMEM lane quarter = warp % 4):
+//   warps 0-1  state rows d: D1 rows 0-63 + e^{gamma_C} S + N -> S, bf16 S^T tile for the next
+//              MMA, then one arrival on `sready`; one thread stores S^T (the chunk-entry state
+//              of the saved record);
+//   warps 2-3  Unew rows t (training only): D1 rows 64-127 + U, staged and bulk-stored;
+//   warps 4-5  O rows t: D2 rows 0-63 + O_intra, staged and TMA-stored;
+//   warp 6     one thread issues the MMAs and keeps a ring of the MMA operands (Mneg, -W, Qt,
+//              bulk copies) NREC chunks deep, with L2 prefetches further ahead.
+// Warps 0-5 read their row of N / U / O_intra (and e^{gamma_C}) straight from global memory into
+// registers one chunk ahead.  Every wait is bounded; a role that gives up raises `abort`, which
+// the others poll, and the teardown drains copies, MMAs and stores before TMEM is freed.
+constexpr int NT2 = 224;
+constexpr int NREC = 5;                        // ring of MMA operand slots
+constexpr int SLOT = 3 * 8192;                 // Mneg | -W | Qt
+constexpr int R_MN = 0, R_W = 8192, R_QT = 16384;
+constexpr int NST = 3;                         // bf16 S^T tiles (MMA B operand, saved-record staging)
+constexpr int PF = 3;                          // L2 prefetch distance beyond the ring (chunks)
+constexpr int OFF2_REC = 0;
+constexpr int OFF2_ST = OFF2_REC + NREC * SLOT;   // NST x 8 KB
+constexpr int OFF2_UN = OFF2_ST + NST * 8192;     // Unew staging, 2 x 8 KB
+constexpr int OFF2_O = OFF2_UN + 2 * 8192;        // O staging, 2 x 8 KB
+constexpr int OFF2_MBAR = OFF2_O + 2 * 8192;      // mrec[NREC] mA[2] mB[2] sready done[2], TMEM slot, abort
+constexpr int SMEM2 = OFF2_MBAR + 8 * (NREC + 7) + 16;
 constexpr uint32_t kIdescScan = idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
 
 // 64 fp32 values -> one 128-byte bf16 row of a swizzled tile
@@ -617,10 +633,30 @@ __device__ __forceinline__ void tmem_row64(uint32_t taddr, float *x) {
     x[32 + i] = __uint_as_float(w[i]);
   }
 }
+// row `row` of a swizzled bf16 tile in global memory (128 contiguous bytes): w[cb] = columns
+// 8 cb .. 8 cb + 7 (stored in 16-byte chunk cb ^ (row & 7))
+__device__ __forceinline__ void load_row_g(const uint8_t *tile, int row, uint4 (&w)[8]) {
+  const uint8_t *src = tile + row * 128;
+#pragma unroll
+  for (int cb = 0; cb < 8; ++cb) w[cb] = __ldg(reinterpret_cast<const uint4 *>(src + ((cb ^ (row & 7)) << 4)));
+}
+// x[j] += column j of a row loaded by load_row_g
+__device__ __forceinline__ void add_row(float *x, const uint4 (&w)[8]) {
+#pragma unroll
+  for (int cb = 0; cb < 8; ++cb) {
+    const uint32_t u[4] = {w[cb].x, w[cb].y, w[cb].z, w[cb].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16(u[e]);
+      x[8 * cb + 2 * e] += f.x;
+      x[8 * cb + 2 * e + 1] += f.y;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
@@ -628,26 +664,49 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
     return;
   }
-  const uint32_t mrec = s_base + OFF2_MBAR, mA = mrec + 8 * NREC, mB = mA + 8;
-  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * NREC + 16);
-  const bool leader = tid == 128, lower = warp >= 2 && warp < 4, upper = warp < 2;
-  const int m = 32 * warp + lane;  // TMEM lane / accumulator row of warps 0-3
-  const int r = m - 64;            // warps 2-3: row t of Unew, row d of S^T
+  const uint32_t mrec = s_base + OFF2_MBAR, mA = mrec + 8 * NREC, mB = mA + 16, sready = mB + 16,
+                 done = sready + 8;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * (NREC + 7));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF2_MBAR + 8 * (NREC + 7) + 4);
+  const bool leader = tid == 192;
+  // per-chunk sources: -W, U, O_intra, N in the workspace; Mneg, Qt, e^{gamma_C} in the saved
+  // record when there is one, else in the workspace
+  const uint8_t *wsb = (const uint8_t *)p.ws + (int64_t)bh * nc * WS_SIZE;
+  const uint8_t *svb = p.saved ? (const uint8_t *)p.saved + (int64_t)bh * nc * kSavedChunk : nullptr;
+  auto rec_ws = [&](int c) { return wsb + (int64_t)c * WS_SIZE; };
+  auto mq_src = [&](int c, int which) -> const uint8_t * {  // which: 0 Mneg, 1 Qt, 2 e^{gamma_C}
+    if (svb) return svb + (int64_t)c * kSavedChunk + (which == 0 ? kSavedM : which == 1 ? kSavedQt : kSavedEG);
+    return rec_ws(c) + (which == 0 ? WS_MN : which == 1 ? WS_QT : WS_EG);
+  };
 
   if (leader) {
-    for (int i = 0; i < NREC + 2; ++i) mbar_init(mrec + 8 * i, 1);
+    for (int i = 0; i < NREC; ++i) mbar_init(mrec + 8 * i, 1);
+    mbar_init(mA, 1);
+    mbar_init(mA + 8, 1);
+    mbar_init(mB, 1);
+    mbar_init(mB + 8, 1);
+    mbar_init(sready, 64);
+    mbar_init(done, 128);
+    mbar_init(done + 8, 128);
+    *abort_flag = 0;
     mbar_fence_init();
   }
-  float S[64];  // warps 2-3: S^T[r][j] = S[j][r]
-#pragma unroll
-  for (int j = 0; j < 64; ++j) S[j] = 0.f;
-  if (lower && p.state0) {
-#pragma unroll
-    for (int j = 0; j < 64; ++j) S[j] = p.state0[(int64_t)bh * D * D + j * D + r];
+  if (p.debug_wait_polls > 0) {  // test hook: a bounded wait on a barrier nothing completes,
+    __syncthreads();             // entered before any copy is issued or tensor memory is held
+    const bool ok = !leader || mbar_wait(mA, 0, p.debug_wait_polls);
+    if (__syncthreads_or(!ok)) {
+      if (leader) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+      return;
+    }
   }
-  if (lower) store_row_bf16(sm + OFF2_SV, r, S);
-  if (warp == 4) {
-    tmem_alloc(smem_u32(tslot), 64);
+  float S[64];  // warps 0-1: S^T[d][j] = S[j][d], d = tid
+  if (warp < 2) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) S[j] = p.state0 ? p.state0[(int64_t)bh * D * D + j * D + tid] : 0.f;
+    store_row_bf16(sm + OFF2_ST, tid, S);
+  }
+  if (warp == 6) {
+    tmem_alloc(smem_u32(tslot), 256);
     tmem_relinquish();
   }
   fence_proxy_async_smem();  // the S^T tile is read by the tensor cores
@@ -655,113 +714,181 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   __syncthreads();
   tc_fence_after();
   const uint32_t tD = *tslot;
-  const uint32_t tl = tD + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's lane quarter
-
-  auto issue = [&](int c) {  // leader: one bulk copy of the chunk's whole record
-    const uint8_t *rec = (const uint8_t *)p.ws + ((int64_t)bh * nc + c) * HO_SIZE;
-    const int s = c % NREC;
-    mbar_expect_tx(mrec + s * 8, HO_SIZE);
-    bulk_g2s(s_base + OFF2_REC + s * REC_STRIDE, rec, HO_SIZE, mrec + s * 8);
-  };
-  if (leader)
-    for (int c = 0; c < nc && c < NREC - 1; ++c) issue(c);
+  const uint32_t lq = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's TMEM lane quarter
   bool failed = false;
-  for (int c = 0; c < nc; ++c) {
-    const int buf = c & 1, slot = c % NREC;
-    const uint32_t rec = s_base + OFF2_REC + slot * REC_STRIDE;
-    const uint8_t *recm = sm + OFF2_REC + slot * REC_STRIDE;
-    const float *eG = reinterpret_cast<const float *>(recm + HO_EG);
-    const uint32_t sv = s_base + OFF2_SV + (c % NSV) * 16384;
-    uint8_t *svm = sm + OFF2_SV + (c % NSV) * 16384, *svnm = sm + OFF2_SV + ((c + 1) % NSV) * 16384;
-    // chunk c's record landed; the barrier also publishes S^T(c); the leader has seen the stores
-    // of chunk c-2 (same O staging, same S^T | Unew tiles as chunk c+1) read their sources
-    if (leader) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
-    if (__syncthreads_or(!mbar_wait(mrec + slot * 8, (c / NREC) & 1))) { failed = true; break; }
-    if (leader) {
-      if (c + NREC - 1 < nc) issue(c + NREC - 1);
+  if (p.saved && tid == 0) {  // the first chunk's entry state for the backward
+    bulk_s2g((uint8_t *)svb + kSavedS0, s_base + OFF2_ST, 8192);
+    bulk_commit();
+  }
+
+  if (leader) {
+    // ---- MMA issue and operand ring ----
+    int issued = 0, landed = 0;
+    auto issue = [&](int c) {
+      const int s = c % NREC;
+      const uint32_t dst = s_base + OFF2_REC + s * SLOT, mb = mrec + 8 * s;
+      mbar_expect_tx(mb, SLOT);
+      bulk_g2s(dst + R_MN, mq_src(c, 0), 8192, mb);
+      bulk_g2s(dst + R_W, rec_ws(c) + WS_W, 8192, mb);
+      bulk_g2s(dst + R_QT, mq_src(c, 1), 8192, mb);
+      issued = c + 1;
+    };
+    auto prefetch = [&](int c) {
+      if (c >= nc) return;
+      prefetch_l2(rec_ws(c) + WS_W, 4 * 8192);  // -W | U | O_intra | N
+      prefetch_l2(mq_src(c, 0), 8192);
+      prefetch_l2(mq_src(c, 1), 8192);
+    };
+    for (int c = 0; c < nc && c < NREC; ++c) issue(c);
+    for (int c = NREC; c < NREC + PF; ++c) prefetch(c);
+    for (int c = 0; c < nc; ++c) {
+      const int s = c % NREC, bb = c & 1;
+      bool ok = mbar_wait(mrec + 8 * s, (c / NREC) & 1);
+      if (ok) landed = c + 1;
+      if (ok && c >= 1) ok = mbar_wait(sready, (c - 1) & 1);              // S^T(c) written
+      if (ok && c >= 2) ok = mbar_wait(done + 8 * bb, ((c - 2) >> 1) & 1); // D1/D2[bb] drained
+      if (!ok || *abort_flag) {
+        failed = true;
+        *abort_flag = 1;
+        break;
+      }
       tc_fence_after();
+      const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + s * SLOT;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) tc_mma(tD, desc_k(rec + HO_QD, k), desc_mn(sv, k), kIdescScan, k > 0);
-      tc_commit(mA);
+      for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
+      tc_commit(mA + 8 * bb);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_QT, k), desc_mn(st, k), kIdescScan, k > 0);
+      tc_commit(mB + 8 * bb);
+      // refill the slot chunk c - 1 used: its MMAs are complete (state rows of c were written
+      // after them) and warps 2-5 have read D1/D2 of c - 1 (checked by the wait on done below)
+      if (c >= 1 && c - 1 + NREC < nc) {
+        if (!mbar_wait(done + 8 * ((c - 1) & 1), ((c - 1) >> 1) & 1)) {
+          failed = true;
+          *abort_flag = 1;
+          break;
+        }
+        issue(c - 1 + NREC);
+        prefetch(c - 1 + NREC + PF);
+      }
     }
-    bool ok = true;
-    if (lower) {  // Unew = U - W S^T; then rows 64-127 of D <- e^{gamma_C} S^T
-      ok = mbar_wait(mA, c & 1);
+    if (failed) {  // (bounded) every copy in flight lands, every MMA issued completes
+      for (int c = landed; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_wait(mA + 8 * i, 0);
+        mbar_wait(mA + 8 * i, 1);
+        mbar_wait(mB + 8 * i, 0);
+        mbar_wait(mB + 8 * i, 1);
+      }
+    }
+  } else if (warp < 2) {
+    // ---- state rows: S <- D1 + e^{gamma_C} S + N ----
+    const int d = tid;
+    uint4 nw[8];
+    float eg = 0.f;
+    if (nc > 0) {
+      load_row_g(rec_ws(0) + WS_N, d, nw);
+      eg = __ldg(reinterpret_cast<const float *>(mq_src(0, 2)) + d);
+    }
+    for (int c = 0; c < nc; ++c) {
+      const int bb = c & 1;
+      // one decision for both warps (they meet at named barriers below)
+      if (!bar_and(1, 64, mbar_wait(mA + 8 * bb, (c >> 1) & 1) && !*abort_flag)) {
+        failed = true;
+        *abort_flag = 1;
+        break;
+      }
       tc_fence_after();
       float x[64];
-      tmem_row64(tl, x);
+      tmem_row64(tD + 64 * bb + lq, x);
+      const uint4 ncur[8] = {nw[0], nw[1], nw[2], nw[3], nw[4], nw[5], nw[6], nw[7]};
+      const float e = eg;
+      if (c + 1 < nc) {  // next chunk's N row and decay, one chunk ahead
+        load_row_g(rec_ws(c + 1) + WS_N, d, nw);
+        eg = __ldg(reinterpret_cast<const float *>(mq_src(c + 1, 2)) + d);
+      }
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const uint4 u = *reinterpret_cast<const uint4 *>(recm + HO_U + sw64(r, ch * 8));
-        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+      for (int j = 0; j < 64; ++j) x[j] = fmaf(e, S[j], x[j]);
+      add_row(x, ncur);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16(uw[e]);
-          x[8 * ch + 2 * e] += f.x;
-          x[8 * ch + 2 * e + 1] += f.y;
+      for (int j = 0; j < 64; ++j) S[j] = x[j];
+      if (c + 1 < nc) {
+        // the tile of S^T(c + 1) last held S^T(c + 1 - NST), whose saved-record store (thread 0
+        // has issued NST - 1 stores since) must have read it
+        if (tid == 0) bulk_wait_read<NST - 1>();
+        bar_sync(1, 64);
+        store_row_bf16(sm + OFF2_ST + ((c + 1) % NST) * 8192, d, S);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(sready);
+        if (p.saved) {
+          bar_sync(1, 64);
+          if (tid == 0) {
+            bulk_s2g((uint8_t *)svb + (int64_t)(c + 1) * kSavedChunk + kSavedS0,
+                     s_base + OFF2_ST + ((c + 1) % NST) * 8192, 8192);
+            bulk_commit();
+          }
         }
       }
-      store_row_bf16(svm + 8192, r, x);
-      const float e = eG[r];
-      uint32_t v[32], w[32];
+    }
+    if (!failed) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        v[j] = __float_as_uint(e * S[j]);
-        w[j] = __float_as_uint(e * S[32 + j]);
+      for (int j = 0; j < 64; ++j) p.stateT[(int64_t)bh * D * D + j * D + d] = S[j];
+    }
+  } else if (warp < 6) {
+    // ---- warps 2-3: Unew rows (training); warps 4-5: O rows ----
+    const bool un = warp < 4;
+    const int t = tid - (un ? 64 : 128), bar = un ? 2 : 3;
+    const uint32_t macc = un ? mA : mB;
+    const uint32_t tcol = un ? 0 : 128;
+    const int src_off = un ? WS_U : WS_OI;
+    uint4 rw[8];
+    const bool active = !un || p.saved;
+    if (active && nc > 0) load_row_g(rec_ws(0) + src_off, t, rw);
+    for (int c = 0; c < nc; ++c) {
+      const int bb = c & 1;
+      if (!bar_and(bar, 64, mbar_wait(macc + 8 * bb, (c >> 1) & 1) && !*abort_flag)) {
+        failed = true;
+        *abort_flag = 1;
+        break;
       }
-      tmem_st32(tl, v);
-      tmem_st32(tl + 32, w);
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-    }
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    if (leader) {
       tc_fence_after();
-#pragma unroll
-      for (int k = 0; k < 4; ++k) tc_mma(tD, desc_k(rec + HO_P, k), desc_mn(sv + 8192, k), kIdescScan, 1);
-      tc_commit(mB);
-    }
-    if (warp < 4) {
-      ok = mbar_wait(mB, c & 1);
-      tc_fence_after();
-      float x[64];
-      tmem_row64(tl, x);
-      if (upper) {
-        store_row_bf16(sm + OFF2_O + buf * 8192, m, x);  // O row t
+      if (active) {
+        float x[64];
+        tmem_row64(tD + tcol + 64 * bb + lq, x);
+        const uint4 cur[8] = {rw[0], rw[1], rw[2], rw[3], rw[4], rw[5], rw[6], rw[7]};
+        if (c + 1 < nc) load_row_g(rec_ws(c + 1) + src_off, t, rw);
+        add_row(x, cur);
+        uint8_t *stage = sm + (un ? OFF2_UN : OFF2_O) + bb * 8192;
+        // the staging tile of chunk c - 2 has been read by its store
+        if (t == 0) bulk_wait_read<1>();
+        bar_sync(bar, 64);
+        store_row_bf16(stage, t, x);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(done + 8 * bb);
+        bar_sync(bar, 64);
+        if (t == 0) {
+          const uint32_t src = s_base + (un ? OFF2_UN : OFF2_O) + bb * 8192;
+          if (un)
+            bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedUnT, src, 8192);
+          else
+            tma_store_rows(&tm.m[0], src, h, c * C, b);  // rows past T are dropped
+          bulk_commit();
+        }
       } else {
-#pragma unroll
-        for (int j = 0; j < 64; ++j) S[j] = x[j];
-        store_row_bf16(svnm, r, S);  // S^T(c+1) row d
+        tc_fence_before();
+        mbar_arrive(done + 8 * bb);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-    }
-    if (__syncthreads_or(!ok)) { failed = true; break; }
-    if (leader) {  // O by TMA (rows past T dropped); S^T | Unew of chunk c for the backward
-      tma_store_rows(&tm.m[0], s_base + OFF2_O + buf * 8192, h, c * C, b);
-      if (p.saved) bulk_s2g((uint8_t *)p.saved + ((int64_t)bh * nc + c) * kSavedChunk + kSavedS0, sv, 16384);
-      bulk_commit();
     }
   }
-  if (failed && leader) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
-  if (!failed && lower) {
-#pragma unroll
-    for (int j = 0; j < 64; ++j) p.stateT[(int64_t)bh * D * D + j * D + r] = S[j];
-  }
-  if (leader) {
-    bulk_wait_all();
-    if (failed) {  // no MMA may still write TMEM when it is freed
-      mbar_wait(mA, 0);
-      mbar_wait(mA, 1);
-      mbar_wait(mB, 0);
-      mbar_wait(mB, 1);
-    }
-  }
+  if (failed && (leader || tid == 0 || tid == 64 || tid == 128)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+  if (tid == 0 || tid == 64 || tid == 128) bulk_wait_all();  // the stores this thread issued
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) tmem_dealloc(tD, 64);
+  if (warp == 6) tmem_dealloc(tD, 256);
 }
 
 template <typename Tb>
@@ -776,8 +903,9 @@ int launch(const Params &p, cudaStream_t st) {
   const int nchunks = p.B * p.H * p.nc;
   TmaMaps tm;
   const void *srcs[4] = {p.q, p.k, p.v, p.gated ? p.f : (const void *)p.g};
+  const Str in_str[4] = {p.sq, p.sk, p.sv, p.sg};
   for (int i = 0; i < 4; ++i)
-    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3 && !p.gated)) return e;
+    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3 && !p.gated, &in_str[i])) return e;
   k1<<<nchunks < nsm ? nchunks : nsm, NT1, smem1, st>>>(p, tm);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
@@ -802,7 +930,7 @@ int tc_fwd_device_status(bool reset) {
 }
 
 size_t tc_fwd_workspace_bytes(const KdaDesc *d) {
-  return (size_t)(d->B * d->H * ((d->T + d->chunk - 1) / d->chunk)) * tcfwd::HO_SIZE;
+  return (size_t)(d->B * d->H * ((d->T + d->chunk - 1) / d->chunk)) * tcfwd::WS_SIZE;
 }
 
 int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st) {

@@ -33,6 +33,11 @@ static __device__ int g_fwd128_status;
 
 constexpr int C = 64, D = 128;
 constexpr float kSpanMax = 60.f;
+// the block-pair factors e^{r_i - r_j} of a chunk that is not "big" stay above fp32's smallest
+// normal (e^-87) only if gamma moves at most this much between the middle rows of the first and
+// the last block; beyond it the factor would flush to zero while the decay it stands for
+// (e^{gamma_t - gamma_s} for t, s close to the block boundary) is not negligible
+constexpr float kMidGapMax = 80.f;
 
 // byte offset of (row, col) in a 64 x 128 bf16 tile kept as two 64-column swizzled halves
 __device__ __forceinline__ uint32_t sw128(int row, int col) { return ((col >> 6) << 13) + sw64(row, col & 63); }
@@ -157,10 +162,13 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd128_chunks_kernel(Params p, con
   }
   if (tid < C) {
     const Tb *betag = (const Tb *)p.beta;
-    bet[tid] = t0 + tid < T ? to_f(betag[((int64_t)b * T + t0 + tid) * H + h]) : 0.f;
+    bet[tid] = t0 + tid < T ? to_f(betag[at(p.sb, b, t0 + tid, h)]) : 0.f;
   }
   if (__syncthreads_or(!mbar_wait(mbar, 0))) {
-    if (tid == 0) atomicExch(&g_fwd128_status, KDA_ERR_TIMEOUT);
+    if (tid == 0) {
+      atomicExch(&g_fwd128_status, KDA_ERR_TIMEOUT);
+      mbar_wait(mbar, 0);  // (bounded) the loads in flight land before the CTA exits
+    }
     return;
   }
 
@@ -192,6 +200,7 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd128_chunks_kernel(Params p, con
       span = fmaxf(span, GS[gsw128(i * 16, tid)] - GS[gsw128(i * 16 + 8, tid)]);
       span = fmaxf(span, GS[gsw128(i * 16 + 8, tid)] - GS[gsw128(i * 16 + 15, tid)]);
     }
+    if (!(GS[gsw128(8, tid)] - GS[gsw128(56, tid)] <= kMidGapMax)) span = 2.f * kSpanMax;
     const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
     if (lane == 0) flag[warp] = any;
   }
@@ -516,6 +525,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd128_scan_kernel(Params p, const
     bulk_g2s(dst + S_P, rec + R_P, REC - R_P, mb);
   };
   if (leader) issue(0);
+  int issued = 1, landed = 0;  // leader: record copies issued / seen complete
   bool failed = false;
   for (int c = 0; c < nc; ++c) {
     const int s = c & 1, buf = c & 1;
@@ -526,8 +536,12 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd128_scan_kernel(Params p, const
     // the O store of chunk c - 2 (same staging buffer) has read its source
     if (leader) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
     if (__syncthreads_or(!mbar_wait(mrec + 8 * s, (c >> 1) & 1))) { failed = true; break; }
+    landed = c + 1;
     if (leader) {
-      if (c + 1 < nc) issue(c + 1);
+      if (c + 1 < nc) {
+        issue(c + 1);
+        issued = c + 2;
+      }
       tc_fence_after();
 #pragma unroll
       for (int k = 0; k < 8; ++k)
@@ -607,7 +621,8 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd128_scan_kernel(Params p, const
   }
   if (leader) {
     bulk_wait_all();
-    if (failed) {  // no MMA may still write TMEM when it is freed (bounded waits)
+    if (failed) {  // no copy may still land and no MMA may still write TMEM (bounded waits)
+      for (int c = landed; c < issued; ++c) mbar_wait(mrec + 8 * (c & 1), (c >> 1) & 1);
       mbar_wait(mA, 0);
       mbar_wait(mA, 1);
       mbar_wait(mB, 0);
@@ -627,8 +642,9 @@ int launch(const Params &p, cudaStream_t st) {
   const int nchunks = p.B * p.H * p.nc;
   TmaMaps tm;
   const void *srcs[4] = {p.q, p.k, p.v, p.g};
+  const Str in_str[4] = {p.sq, p.sk, p.sv, p.sg};
   for (int i = 0; i < 4; ++i)
-    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3)) return e;
+    if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3, &in_str[i])) return e;
   k1<<<nchunks, NT1, SMEM1, st>>>(p, tm);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd128_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))

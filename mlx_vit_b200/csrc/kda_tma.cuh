@@ -11,6 +11,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "kda_common.cuh"
+
 namespace kda {
 
 struct alignas(64) TmaMaps {
@@ -18,8 +20,11 @@ struct alignas(64) TmaMaps {
 };
 
 // Encodes the map of a [B, T, H, D] tensor (bf16 or fp32) with a box of 64 rows of one head
-// and 128 bytes of columns (64 for bf16, 32 for fp32; x selects the first column).  Returns 0 on success, a KDA_ERR_* code otherwise.
-int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32);
+// and 128 bytes of columns (64 for bf16, 32 for fp32; x selects the first column).  `st` gives
+// the element strides of b, t, h (nullptr: dense).  Returns 0 on success, a KDA_ERR_* code
+// otherwise.
+int tma_map_bthd(CUtensorMap *map, const void *base, int64_t B, int64_t T, int64_t H, int64_t D, bool fp32,
+                 const Str *st = nullptr);
 
 // x: first column of the box (a multiple of 64 for bf16, of 32 for fp32)
 __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap *map, int h, int t0, int b,

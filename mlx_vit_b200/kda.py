@@ -63,11 +63,43 @@ def _ptr(x):
     return ctypes.c_void_p(x.data_ptr()) if x is not None else ctypes.c_void_p(0)
 
 
-def _desc(q, beta, chunk_size, flags):
+def _strides(x):
+    """KdaStrides of an input view (b, t, h element strides; zeros for a dense tensor)."""
+    if x is None or x.is_contiguous():
+        return _lib.KdaStrides(0, 0, 0)
+    st = x.stride()
+    return _lib.KdaStrides(st[0], st[1], st[2])
+
+
+def _desc(q, beta, chunk_size, flags, k=None, v=None, g=None, do=None):
+    """The call's descriptor; the strides of any strided input view go along with it."""
     B, T, H, D = q.shape
     if q.dtype not in _DT or beta.dtype not in _DT:
         raise ValueError(f"unsupported dtypes q={q.dtype} beta={beta.dtype}")
-    return _lib.KdaDesc(B, T, H, D, D, int(chunk_size), _DT[q.dtype], _DT[beta.dtype], flags, 0)
+    return _lib.KdaDesc(B, T, H, D, D, int(chunk_size), _DT[q.dtype], _DT[beta.dtype], flags, 0,
+                        _strides(q), _strides(k), _strides(v), _strides(g), _strides(beta),
+                        _strides(do))
+
+
+def _in_place_ok(x):
+    """Whether the kernels can read a (B, T, H[, D]) input view where it lies: the last axis
+    unit-stride (for 4-D views), non-negative strides that span whole 16-byte units and a
+    16-byte aligned base (what the tensor-core kernels' TMA loads need).  Anything else is
+    copied into a dense tensor first."""
+    if x.is_contiguous():
+        return True
+    st, es = x.stride(), x.element_size()
+    if x.dim() == 4 and st[3] != 1:
+        return False
+    if any(s < 0 for s in st):
+        return False
+    if x.dim() == 3:  # beta: read element by element
+        return True
+    return all((s * es) % 16 == 0 for s in st[:3]) and x.data_ptr() % 16 == 0
+
+
+def _dense_unless_readable(x):
+    return x if _in_place_ok(x) else x.contiguous()
 
 
 def _check_shapes(q, k, v, g, beta, state):
@@ -88,6 +120,22 @@ def _check_shapes(q, k, v, g, beta, state):
         raise ValueError(f"all operands must be on one device, got {devs}")
 
 
+def _canonical(q, k, v, g, beta, state):
+    """Checks shapes, dtypes and devices, and returns the operands as the kernels read them:
+    q, k, v, beta in their own dtype and g float32, as the caller's views where the kernels can
+    read those in place (strides passed in the descriptor), else dense copies; the state dense
+    float32."""
+    q, k, v, g, beta, state = (_as_torch(x, n) for x, n in
+                               ((q, "q"), (k, "k"), (v, "v"), (g, "g"), (beta, "beta"),
+                                (state, "state")))
+    _check_shapes(q, k, v, g, beta, state)
+    q, k, v, beta = (_dense_unless_readable(x) for x in (q, k, v, beta))
+    g = _dense_unless_readable(g) if g.dtype == torch.float32 else g.to(torch.float32).contiguous()
+    if state is not None:
+        state = state.to(torch.float32).contiguous()
+    return q, k, v, g, beta, state
+
+
 def _workspace(desc, backward, device):
     n = _lib.lib().kda_workspace_bytes(ctypes.byref(desc), backward)
     if n == 0:
@@ -103,9 +151,10 @@ def kda_forward(q, k, v, g, beta, state=None, chunk_size=64, save_states=False, 
     """One ``kda_fwd`` call.  Returns (o, S_T, saved | None); ``saved`` is the opaque
     per-chunk record (uint8 device tensor) that ``kda_backward`` consumes."""
     L = _lib.lib()
+    q, k, v, g, beta, state = _canonical(q, k, v, g, beta, state)
     B, T, H, D = q.shape
-    desc = _desc(q, beta, chunk_size, flags)
-    o = torch.empty_like(q)
+    desc = _desc(q, beta, chunk_size, flags, k, v, g)
+    o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
     cs = None
     if save_states:
@@ -127,11 +176,24 @@ def kda_backward(q, k, v, g, beta, state, saved, do, dstate=None, chunk_size=64,
                  flags=0, want_dstate0=True):
     """One ``kda_bwd`` call.  Returns (dq, dk, dv, dg, dbeta, dstate0 | None)."""
     L = _lib.lib()
+    q, k, v, g, beta, state = _canonical(q, k, v, g, beta, state)
+    saved = _as_torch(saved, "saved")
+    if saved is None or saved.dtype != torch.uint8 or not saved.is_contiguous():
+        raise ValueError("saved must be the uint8 record kda_forward(save_states=True) returned")
+    do = _as_torch(do, "do")
+    if tuple(do.shape) != tuple(q.shape):
+        raise ValueError(f"do shape {tuple(do.shape)} != q shape {tuple(q.shape)}")
+    do = _dense_unless_readable(do.to(q.dtype))
+    if dstate is not None:
+        dstate = _as_torch(dstate, "dstate")
+        if tuple(dstate.shape) != (q.shape[0], q.shape[2], q.shape[3], q.shape[3]):
+            raise ValueError(f"dstate shape {tuple(dstate.shape)} != state shape")
+        dstate = dstate.to(torch.float32).contiguous()
     B, T, H, D = q.shape
-    desc = _desc(q, beta, chunk_size, flags)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    desc = _desc(q, beta, chunk_size, flags, k, v, g, do)
+    dq, dk, dv = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(3))
     dg = torch.empty((B, T, H, D), dtype=torch.float32, device=q.device)
-    db = torch.empty_like(beta)
+    db = torch.empty(beta.shape, dtype=beta.dtype, device=q.device)
     ds0 = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device) if want_dstate0 else None
     ws, nws = _workspace(desc, 1, q.device)
     with torch.cuda.device(q.device):
@@ -151,9 +213,10 @@ def kda_recurrent(q, k, v, g, beta, state=None):
     """One ``kda_fwd_recurrent`` call: the step form token by token (exact fp32 arithmetic, one
     launch), for decoding and short segments.  Returns (o, S_T); no gradients."""
     L = _lib.lib()
+    q, k, v, g, beta, state = _canonical(q, k, v, g, beta, state)
     B, T, H, D = q.shape
-    desc = _desc(q, beta, 64, 0)
-    o = torch.empty_like(q)
+    desc = _desc(q, beta, 64, 0, k, v, g)
+    o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream().cuda_stream
@@ -180,7 +243,7 @@ class CudaKdaFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do, dS_T):
         q, k, v, g, beta, state, cs = ctx.saved_tensors
-        do = torch.zeros_like(q) if do is None else do.to(q.dtype).contiguous()
+        do = torch.zeros(q.shape, dtype=q.dtype, device=q.device) if do is None else do.to(q.dtype)
         dS_T = None if dS_T is None else dS_T.float().contiguous()
         dq, dk, dv, dg, db, ds0 = kda_backward(q, k, v, g, beta, state, cs, do, dS_T,
                                                ctx.chunk_size, ctx.flags,
@@ -195,21 +258,13 @@ def cuda_kda(q, k, v, g, beta, state: Optional[torch.Tensor] = None, chunk_size:
     ``force_generic`` selects the fp32 SIMT kernels even where a tensor-core kernel exists.
     fp32 inputs always run on the fp32 kernels.
     """
-    q, k, v, g, beta, state = (_as_torch(x, n) for x, n in
-                               ((q, "q"), (k, "k"), (v, "v"), (g, "g"), (beta, "beta"),
-                                (state, "state")))
-    _check_shapes(q, k, v, g, beta, state)
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    g = g.to(torch.float32).contiguous()
-    beta = beta.contiguous()
-    if state is not None:
-        state = state.to(torch.float32).contiguous()
+    q, k, v, g, beta, state = _canonical(q, k, v, g, beta, state)
     flags = _lib.KDA_FLAG_FORCE_GENERIC if force_generic else 0
     need_grad = torch.is_grad_enabled() and any(
         x is not None and x.requires_grad for x in (q, k, v, g, beta, state))
     if need_grad:
         # fail before the forward runs if no backward kernel covers the shape (e.g. D = 128)
-        st = _lib.lib().kda_check_desc(ctypes.byref(_desc(q, beta, chunk_size, flags)), 1)
+        st = _lib.lib().kda_check_desc(ctypes.byref(_desc(q, beta, chunk_size, flags, k, v, g)), 1)
         if st:
             raise ValueError(f"cuda_kda: gradients need a backward for this shape, which is not "
                              f"available ({_lib.lib().kda_strerror(st).decode()})")
@@ -226,19 +281,45 @@ def _gate_struct(f, A_log, dt_bias, b, allow_neg_eigval):
                         int(bool(allow_neg_eigval)), 0)
 
 
+def _canonical_gated(q, k, v, f, A_log, dt_bias, b, state):
+    """The gated entry points' operand checks; returns dense operands (A_log, dt_bias and the
+    state as float32)."""
+    q, k, v, f, A_log, dt_bias, b, state = (
+        _as_torch(x, n) for x, n in ((q, "q"), (k, "k"), (v, "v"), (f, "f"), (A_log, "A_log"),
+                                     (dt_bias, "dt_bias"), (b, "b"), (state, "state")))
+    if q.dim() != 4:
+        raise ValueError(f"q must be (B, L, H, D), got {tuple(q.shape)}")
+    B, T, H, D = q.shape
+    _check_shapes(q, k, v, f, b, state)
+    if q.dtype != torch.bfloat16 or f.dtype != torch.bfloat16:
+        raise ValueError("the fused-gate path needs bf16 q, k, v and f")
+    if tuple(A_log.shape) != (H,) or tuple(dt_bias.shape) not in ((H * D,), (H, D)):
+        raise ValueError(f"A_log must be ({H},) and dt_bias ({H * D},)")
+    q, k, v, f, b = (_dense_unless_readable(x) for x in (q, k, v, f, b))
+    A_log = A_log.to(torch.float32).contiguous()
+    dt_bias = dt_bias.to(torch.float32).reshape(H * D).contiguous()
+    if state is not None:
+        state = state.to(torch.float32).contiguous()
+    return q, k, v, f, A_log, dt_bias, b, state
+
+
 def kda_forward_gated(q, k, v, f, A_log, dt_bias, b, state=None, chunk_size=64,
                       allow_neg_eigval=False, save_states=False):
     """One ``kda_fwd_gated`` call: the decay gate g = -exp(A_log) softplus(f + dt_bias) and
     the write gate beta = s sigmoid(b) are computed inside the chunk kernel
     (nope_gdn_mlx.py:802-816).  Returns (o, S_T, saved | None)."""
     L = _lib.lib()
-    desc = _desc(q, b, chunk_size, 0)
-    o = torch.empty_like(q)
+    q, k, v, f, A_log, dt_bias, b, state = _canonical_gated(q, k, v, f, A_log, dt_bias, b, state)
+    desc = _desc(q, b, chunk_size, 0, k, v, f)  # f takes g's place in the descriptor
+    o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     B, T, H, D = q.shape
     S_T = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
     cs = None
     if save_states:
-        cs = torch.empty(L.kda_saved_bytes(ctypes.byref(desc)), dtype=torch.uint8, device=q.device)
+        n = L.kda_saved_bytes(ctypes.byref(desc))
+        if n == 0:
+            _lib.check(L.kda_check_desc(ctypes.byref(desc), 0) or -1, "kda_saved_bytes")
+        cs = torch.empty(n, dtype=torch.uint8, device=q.device)
     ws, nws = _workspace(desc, 0, q.device)
     gate = _gate_struct(f, A_log, dt_bias, b, allow_neg_eigval)
     with torch.cuda.device(q.device):
@@ -255,11 +336,20 @@ def kda_backward_gated(q, k, v, f, A_log, dt_bias, b, state, saved, do, dstate=N
     """One ``kda_bwd_gated`` call.  Returns (dq, dk, dv, df, db, dA_log, ddt_bias,
     dstate0 | None): the VJP of the recurrence chained through both gates."""
     L = _lib.lib()
-    desc = _desc(q, b, chunk_size, 0)
+    q, k, v, f, A_log, dt_bias, b, state = _canonical_gated(q, k, v, f, A_log, dt_bias, b, state)
+    saved = _as_torch(saved, "saved")
+    if saved is None or saved.dtype != torch.uint8 or not saved.is_contiguous():
+        raise ValueError("saved must be the uint8 record kda_forward_gated(save_states=True) returned")
+    do = _as_torch(do, "do")
+    if tuple(do.shape) != tuple(q.shape):
+        raise ValueError(f"do shape {tuple(do.shape)} != q shape {tuple(q.shape)}")
+    do = _dense_unless_readable(do.to(q.dtype))
+    if dstate is not None:
+        dstate = _as_torch(dstate, "dstate").to(torch.float32).contiguous()
+    desc = _desc(q, b, chunk_size, 0, k, v, f, do)
     B, T, H, D = q.shape
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    df = torch.empty_like(f)
-    db = torch.empty_like(b)
+    dq, dk, dv, df = (torch.empty(q.shape, dtype=q.dtype, device=q.device) for _ in range(4))
+    db = torch.empty(b.shape, dtype=b.dtype, device=q.device)
     dA = torch.empty((H,), dtype=torch.float32, device=q.device)
     ddtb = torch.empty((H * D,), dtype=torch.float32, device=q.device)
     ds0 = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device) if want_dstate0 else None
@@ -291,7 +381,7 @@ class CudaKdaGatedFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do, dS_T):
         q, k, v, f, A_log, dt_bias, b, state, cs = ctx.saved_tensors
-        do = torch.zeros_like(q) if do is None else do.to(q.dtype).contiguous()
+        do = torch.zeros(q.shape, dtype=q.dtype, device=q.device) if do is None else do.to(q.dtype)
         dS_T = None if dS_T is None else dS_T.float().contiguous()
         dq, dk, dv, df, db, dA, ddtb, ds0 = kda_backward_gated(
             q, k, v, f, A_log, dt_bias, b, state, cs, do, dS_T, ctx.chunk_size, ctx.allow_neg,
@@ -310,22 +400,7 @@ def cuda_kda_gated(q, k, v, f, A_log, dt_bias, b, state: Optional[torch.Tensor] 
     g = -exp(A_log) softplus(f + dt_bias) and beta = (2 if allow_neg_eigval else 1) sigmoid(b)
     (nope_gdn_mlx.py:802-816), without materialising g or beta.  bf16 q/k/v/f only.
     """
-    q, k, v, f, A_log, dt_bias, b, state = (
-        _as_torch(x, n) for x, n in ((q, "q"), (k, "k"), (v, "v"), (f, "f"), (A_log, "A_log"),
-                                     (dt_bias, "dt_bias"), (b, "b"), (state, "state")))
-    if q.dim() != 4:
-        raise ValueError(f"q must be (B, L, H, D), got {tuple(q.shape)}")
-    B, T, H, D = q.shape
-    _check_shapes(q, k, v, f, b, state)
-    if q.dtype != torch.bfloat16 or f.dtype != torch.bfloat16:
-        raise ValueError("cuda_kda_gated needs bf16 q, k, v and f")
-    if tuple(A_log.shape) != (H,) or tuple(dt_bias.shape) not in ((H * D,), (H, D)):
-        raise ValueError(f"A_log must be ({H},) and dt_bias ({H * D},)")
-    q, k, v, f, b = (x.contiguous() for x in (q, k, v, f, b))
-    A_log = A_log.to(torch.float32).contiguous()
-    dt_bias = dt_bias.to(torch.float32).reshape(H * D).contiguous()
-    if state is not None:
-        state = state.to(torch.float32).contiguous()
+    q, k, v, f, A_log, dt_bias, b, state = _canonical_gated(q, k, v, f, A_log, dt_bias, b, state)
     need_grad = torch.is_grad_enabled() and any(
         x is not None and x.requires_grad for x in (q, k, v, f, A_log, dt_bias, b, state))
     if need_grad:

@@ -97,11 +97,12 @@ class GatedDeltaLayer(nn.Module):
             k = cv(self.k_conv1d, self.k_proj(x), True, 1.0).view(B, L, H, D)
             v = cv(self.v_conv1d, self.v_proj(x), False, 1.0).view(B, L, H, D)
         else:
+            # the L2 norm spans the whole H*D row, before the head reshape (nope_gdn_mlx.py:797-799)
             v = F.silu(self.v_conv1d(self.v_proj(x))).view(B, L, H, D)
-            qr = self.q_conv1d(self.q_proj(x)).view(B, L, H, D)
-            kr = self.k_conv1d(self.k_proj(x)).view(B, L, H, D)
-            q = (F.normalize(F.silu(qr).float(), dim=-1) * self.scale).to(bf)
-            k = F.normalize(F.silu(kr).float(), dim=-1).to(bf)
+            qr = self.q_conv1d(self.q_proj(x))
+            kr = self.k_conv1d(self.k_proj(x))
+            q = (F.normalize(F.silu(qr).float(), dim=-1) * self.scale).to(bf).view(B, L, H, D)
+            k = F.normalize(F.silu(kr).float(), dim=-1).to(bf).view(B, L, H, D)
         f = self.f_proj_2(self.f_proj_1(x)).view(B, L, H, D).to(bf)
         b = self.b_proj(x).to(bf)
         o, new_state = cuda_kda_gated(q, k, v.to(bf).contiguous(), f.contiguous(), self.A_log,

@@ -1,8 +1,11 @@
-"""Fused row operations of the GDN layer around the recurrence (bf16, D = 64 or 128), with
-autograd: ``l2norm_silu`` is the q / k prologue y = l2norm(silu(x)) * scale
-(nope_gdn_mlx.py:797-799, l2_normalize :76-79) and ``gated_rmsnorm`` the output's
-y = rmsnorm(o) * w * sigmoid(gate) (RMSNormGated, :340-371).  One CUDA pass each way
-(``kda_l2norm_silu_*`` / ``kda_gated_rmsnorm_*`` in include/kda_b200.h); no CPU path."""
+"""Fused row operations of the GDN layer around the recurrence (bf16), with autograd:
+``l2norm_silu`` is the q / k prologue y = l2norm(silu(x)) * scale over the last dimension, which
+in the layer is a token's whole H*D channel row (nope_gdn_mlx.py:797-799, l2_normalize :76-79,
+normalised before the head reshape at :818-821); ``conv_silu`` fuses the short causal
+convolution in front of it; ``gated_rmsnorm`` is the output's y = rmsnorm(o) * w * sigmoid(gate)
+over each head's D = 64 or 128 channels (RMSNormGated(D), :340-371).  One CUDA pass each way
+(``kda_l2norm_silu_*``, ``kda_conv_silu_*``, ``kda_gated_rmsnorm_*`` in include/kda_b200.h); no
+CPU path."""
 from __future__ import annotations
 
 import ctypes
@@ -30,11 +33,21 @@ def _check_rows(*xs):
     return xs[0].numel() // D, D
 
 
+def _check_wide(*xs):
+    for x in xs:
+        if not x.is_cuda or x.dtype != torch.bfloat16:
+            raise ValueError("fused row ops take bf16 CUDA tensors")
+    n = xs[0].shape[-1]
+    if n % 8 or n > 8192:
+        raise ValueError(f"l2norm_silu needs a row length that is a multiple of 8 and at most 8192, got {n}")
+    return xs[0].numel() // n, n
+
+
 class L2NormSiLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, scale):
         x = x.contiguous()
-        rows, D = _check_rows(x)
+        rows, D = _check_wide(x)
         y = torch.empty_like(x)
         with torch.cuda.device(x.device):
             _lib.check(_lib.lib().kda_l2norm_silu_fwd(rows, D, _ptr(x), _ptr(y), float(scale), _stream(x)),
@@ -47,7 +60,7 @@ class L2NormSiLU(torch.autograd.Function):
     def backward(ctx, dy):
         (x,) = ctx.saved_tensors
         dy = dy.to(torch.bfloat16).contiguous()
-        rows, D = _check_rows(x, dy)
+        rows, D = _check_wide(x, dy)
         dx = torch.empty_like(x)
         with torch.cuda.device(x.device):
             _lib.check(_lib.lib().kda_l2norm_silu_bwd(rows, D, _ptr(x), _ptr(dy), _ptr(dx), float(ctx.scale),
@@ -87,8 +100,9 @@ class ConvSiLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, H, D, norm, scale):
         x = x.contiguous()
-        if not x.is_cuda or x.dtype != torch.bfloat16 or D not in (64, 128) or x.shape[-1] != H * D:
-            raise ValueError("conv_silu takes a bf16 CUDA tensor [B, T, H*D] with D = 64 or 128")
+        if not x.is_cuda or x.dtype != torch.bfloat16 or x.shape[-1] != H * D or (H * D) % 8 or H * D > 8192:
+            raise ValueError("conv_silu takes a bf16 CUDA tensor [B, T, H*D] with H*D a multiple of 8, "
+                             "at most 8192")
         B, T = x.shape[0], x.shape[1]
         w32 = w.reshape(H * D, 4).to(torch.float32).contiguous()
         b32 = b.to(torch.float32).contiguous()
@@ -120,12 +134,14 @@ class ConvSiLU(torch.autograd.Function):
 def conv_silu(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, heads: int, head_dim: int,
               norm: bool = False, scale: float = 1.0) -> torch.Tensor:
     """silu(causal depthwise conv4(x)) over time for x [B, T, H*D] (bf16); with ``norm`` also the
-    per-head L2 norm and ``scale``.  ``weight`` is the conv's [C, 1, 4] (or [C, 4]) tensor."""
+    L2 norm over each token's whole H*D row and ``scale`` (nope_gdn_mlx.py:793-799).  ``weight``
+    is the conv's [C, 1, 4] (or [C, 4]) tensor."""
     return ConvSiLU.apply(x, weight, bias, heads, head_dim, norm, scale)
 
 
 def l2norm_silu(x: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
-    """y = silu(x) / max(||silu(x)||, 1e-12) * scale over the last dim (bf16 in and out)."""
+    """y = silu(x) / max(||silu(x)||, 1e-12) * scale over the last dim (bf16 in and out; the layer
+    passes rows of H*D channels, as the reference normalises before its head reshape)."""
     return L2NormSiLU.apply(x, scale)
 
 

@@ -57,6 +57,15 @@ def test_check_desc_status(kw, status):
     assert L.kda_check_desc(ctypes.byref(desc(**kw)), 0) == status
 
 
+def test_negative_stride_rejected():
+    L = _lib.lib()
+    d = desc()
+    d.q = _lib.KdaStrides(256 * 4 * 64, -4 * 64, 64)
+    assert L.kda_check_desc(ctypes.byref(d), 0) == -1
+    d.q = _lib.KdaStrides(256 * 4 * 64 * 3, 4 * 64 * 3, 64)  # a slice of a fused projection
+    assert L.kda_check_desc(ctypes.byref(d), 0) == 0
+
+
 def test_backward_head_dim_limit():
     L = _lib.lib()
     d = desc(Dk=128, Dv=128, flags=_lib.KDA_FLAG_FORCE_GENERIC)

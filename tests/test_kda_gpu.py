@@ -173,3 +173,38 @@ def test_fresh_host_thread(cuda):
     ref = O.fwd_bwd(rounded_inputs(inp, torch.bfloat16), dtype=np.float64)
     for k in OUT_KEYS:
         assert rel_err(out["r"][k], ref[k]) <= TOL_BF16, k
+
+
+def _gap_decay(B, T, H, D):
+    """g that moves gamma 50 within each half block around the block-2 / block-3 boundary (rows
+    41-46 and 49-56 of every chunk) and not at all between rows 47 and 48: every half-block span
+    stays under the factored form's per-block limit, yet gamma drops 100 between the middle rows
+    of blocks 2 and 3.  A block-pair factor e^{r_3 - r_2} = e^-100 is below fp32's normal range
+    while the decay it stands for between rows 47 and 48 is 1."""
+    g = np.zeros((B, T, H, D), np.float32)
+    r = np.arange(T) % 64
+    g[:, (r >= 41) & (r <= 46)] = -50.0 / 6
+    g[:, (r >= 49) & (r <= 56)] = -50.0 / 8
+    return g
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_block_gap_beyond_fp32_range(cuda, D):
+    inp = make_inputs(1, 200, 2, D, seed=5, state_std=0.1)
+    inp["g"] = _gap_decay(1, 200, 2, D) + inp["g"] * 0.01
+    r = rounded_inputs(inp, torch.bfloat16)
+    if D == 64:
+        ref = O.fwd_bwd(r, dtype=np.float64)
+        got = run_fwd_bwd(to_dev(inp, cuda, torch.bfloat16), 64)
+        keys = OUT_KEYS
+    else:  # the D = 128 tensor-core path is forward-only
+        o_ref, S_ref = O.compiled_forward(r["q"], r["k"], r["v"], r["g"], r["beta"], r["state"],
+                                          dtype=np.float64)
+        ref = dict(o=o_ref, S_T=S_ref)
+        t = to_dev(inp, cuda, torch.bfloat16)
+        with torch.no_grad():
+            o, S = cuda_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], t["state"])
+        got = dict(o=o.float().cpu().numpy(), S_T=S.cpu().numpy())
+        keys = ("o", "S_T")
+    for k in keys:
+        assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))

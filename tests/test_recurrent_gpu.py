@@ -69,3 +69,38 @@ def test_recurrent_rejects_unsupported_dim(cuda):
     t = dev_inputs(inp, cuda, torch.float32)
     with pytest.raises(Exception):
         kda_recurrent(t["q"], t["k"], t["v"], t["g"], t["beta"])
+
+
+def test_low_level_wrappers_take_strided_and_bf16_operands(cuda):
+    """The public low-level calls (kda_recurrent, kda_forward, kda_backward) accept what
+    cuda_kda accepts: a strided time slice of a B = 2 batch and a bf16 g / state are made dense
+    float32 before the kernel reads them, and give the dense float32 answer."""
+    import torch
+    from mlx_vit_b200 import kda_recurrent, kda_forward, kda_backward
+    from mlx_vit_b200.synthetic import make_inputs
+    inp = make_inputs(2, 40, 2, 64, seed=12, state_std=0.1)
+    t = {k: torch.from_numpy(v).to(cuda) for k, v in inp.items()}
+    sl = slice(5, 9)
+    view = {k: (t[k][:, sl] if t[k].dim() >= 3 and k not in ("state", "dst") else t[k]) for k in t}
+    assert not view["q"].is_contiguous()
+    dense = {k: x.contiguous() for k, x in view.items()}
+    o1, S1 = kda_recurrent(view["q"], view["k"], view["v"], view["g"].to(torch.bfloat16),
+                           view["beta"], view["state"].to(torch.bfloat16))
+    o2, S2 = kda_recurrent(dense["q"], dense["k"], dense["v"],
+                           dense["g"].to(torch.bfloat16).float(), dense["beta"],
+                           dense["state"].to(torch.bfloat16).float())
+    assert torch.equal(o1, o2) and torch.equal(S1, S2)
+    bf = torch.bfloat16
+    qv, kv, vv = (x.to(bf)[:, :, :] for x in (t["q"], t["k"], t["v"]))
+    args = (qv[:, 1:], kv[:, 1:], vv[:, 1:], t["g"][:, 1:].to(bf), t["beta"][:, 1:].to(bf), t["state"])
+    o, S, cs = kda_forward(*args, 64, save_states=True)
+    ref_o, ref_S, ref_cs = kda_forward(*(x.contiguous() if x is not None else None for x in args[:3]),
+                                       args[3].float().contiguous(), args[4].contiguous(), args[5], 64,
+                                       save_states=True)
+    assert torch.equal(o, ref_o) and torch.equal(S, ref_S)
+    do = t["do"][:, 1:].to(bf)
+    g1 = kda_backward(*args, cs, do, None, 64)
+    g2 = kda_backward(*(x.contiguous() for x in args[:3]), args[3].float().contiguous(),
+                      args[4].contiguous(), args[5], ref_cs, do.contiguous(), None, 64)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
