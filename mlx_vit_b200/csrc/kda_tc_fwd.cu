@@ -585,39 +585,44 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 // next; the fp32 state stays in registers (the diagonal decay is applied there exactly) and a
 // bf16 copy of S^T is the MMA's B operand.  The outputs come off the chain:
 //     O = Qt S^T + O_intra,   Unew = U - W S^T             (Qt = Qd - P W, O_intra = P U)
-// Per chunk two MMAs read S^T: MMA1 = [Mneg; -W] S^T into accumulator D1 (M = 128: rows 0-63
-// the state product, rows 64-127 -W S^T) and MMA2 = [Qt; .] S^T into D2 (rows 0-63; rows
-// 64-127 are not used).  Both accumulators are double-buffered in TMEM (256 columns).
-// Warp roles (TMEM lane quarter = warp % 4):
-//   warps 0-1  state rows d: D1 rows 0-63 + e^{gamma_C} S + N -> S, bf16 S^T tile for the next
-//              MMA, then one arrival on `sready`; one thread stores S^T (the chunk-entry state
-//              of the saved record);
-//   warps 2-3  Unew rows t (training only): D1 rows 64-127 + U, staged and bulk-stored;
-//   warps 4-5  O rows t: D2 rows 0-63 + O_intra, staged and TMA-stored;
-//   warp 6     one thread issues the MMAs and keeps a ring of the MMA operands (Mneg, -W, Qt,
-//              bulk copies) NREC chunks deep, with L2 prefetches further ahead.
-// Warps 0-5 read their row of N / U / O_intra (and e^{gamma_C}) straight from global memory into
-// registers one chunk ahead.  Every wait is bounded; a role that gives up raises `abort`, which
-// the others poll, and the teardown drains copies, MMAs and stores before TMEM is freed.
-constexpr int NT2 = 224;
-constexpr int NREC = 5;                        // ring of MMA operand slots
-constexpr int SLOT = 3 * 8192;                 // Mneg | -W | Qt
-constexpr int R_MN = 0, R_W = 8192, R_QT = 16384;
+// Per chunk two MMAs read S^T: MMA1 = [Mneg; -W] S^T into accumulator D1 (rows 0-63 the state
+// product, rows 64-127 -W S^T) and MMA2 = [-W; Qt] S^T into D2 (rows 64-127 Qt S^T; rows 0-63
+// repeat -W S^T and are not read).  Both accumulators are double-buffered in TMEM (256 columns).
+// Warp roles (a warp reaches TMEM lanes 32 (warp % 4) ..):
+//   warps 0, 1, 4, 5  state rows d (lanes 0-63 of D1), warps 0-1 columns 0-31, warps 4-5
+//              columns 32-63: S <- D1 + e^{gamma_C} S + N, bf16 S^T tile for the next MMA;
+//              thread 0 then issues the next chunk's two MMAs itself (no hand-off on the chain)
+//              and stores S^T (the saved chunk-entry state);
+//   warps 2-3  Unew rows t (training only): D1 rows 64-127 + U;
+//   warps 6-7  O rows t: D2 rows 64-127 + O_intra;
+//              each of these two roles keeps a ring of NIO tiles: one thread bulk-loads the
+//              chunk's U / O_intra tile NIO - 1 chunks ahead, every thread adds its TMEM row in
+//              place, and the tile then leaves by a bulk / TMA store;
+//   warp 8     one thread keeps a ring of the chunk operands (Mneg, -W, Qt, N, e^{gamma_C}: bulk
+//              copies) NREC chunks deep, refilling a slot once the MMAs that read it are done.
+// Every wait is bounded; a role that gives up raises `abort`, which the others poll, and the
+// teardown drains copies, MMAs and stores before TMEM is freed.
+constexpr int NT2 = 288;
+constexpr int NREC = 4;                        // ring of chunk operand slots
+constexpr int R_MN = 0, R_W = 8192, R_QT = 16384, R_N = 24576, R_EG = 32768;
+constexpr int SLOT_BYTES = 32768 + 256;        // what one slot's copies bring
+constexpr int SLOT = 33 * 1024;                // slot stride (1024-byte aligned)
 constexpr int NST = 3;                         // bf16 S^T tiles (MMA B operand, saved-record staging)
-constexpr int PF = 3;                          // L2 prefetch distance beyond the ring (chunks)
+constexpr int NIO = 4;                         // U -> Unew and O_intra -> O tiles per role
 constexpr int OFF2_REC = 0;
 constexpr int OFF2_ST = OFF2_REC + NREC * SLOT;   // NST x 8 KB
-constexpr int OFF2_UN = OFF2_ST + NST * 8192;     // Unew staging, 2 x 8 KB
-constexpr int OFF2_O = OFF2_UN + 2 * 8192;        // O staging, 2 x 8 KB
-constexpr int OFF2_MBAR = OFF2_O + 2 * 8192;      // mrec[NREC] mA[2] mB[2] sready done[2], TMEM slot, abort
-constexpr int SMEM2 = OFF2_MBAR + 8 * (NREC + 7) + 16;
+constexpr int OFF2_UN = OFF2_ST + NST * 8192;     // NIO x 8 KB
+constexpr int OFF2_O = OFF2_UN + NIO * 8192;      // NIO x 8 KB
+constexpr int OFF2_MBAR = OFF2_O + NIO * 8192;    // mrec[NREC] sfree[NREC] mA[2] mB[2] done[2] io[2][NIO], TMEM slot, abort
+constexpr int NMBAR2 = 2 * NREC + 6 + 2 * NIO;
+constexpr int SMEM2 = OFF2_MBAR + 8 * NMBAR2 + 16;
 constexpr uint32_t kIdescScan = idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
 
-// 64 fp32 values -> one 128-byte bf16 row of a swizzled tile
-__device__ __forceinline__ void store_row_bf16(uint8_t *tile, int row, const float *x) {
+// 32 fp32 values -> columns c0 .. c0 + 31 of a row of a swizzled bf16 tile
+__device__ __forceinline__ void store_half_row_bf16(uint8_t *tile, int row, int c0, const float *x) {
 #pragma unroll
-  for (int ch = 0; ch < 8; ++ch)
-    *reinterpret_cast<uint4 *>(tile + sw64(row, ch * 8)) =
+  for (int ch = 0; ch < 4; ++ch)
+    *reinterpret_cast<uint4 *>(tile + sw64(row, c0 + ch * 8)) =
         make_uint4(pack_bf16(x[8 * ch], x[8 * ch + 1]), pack_bf16(x[8 * ch + 2], x[8 * ch + 3]),
                    pack_bf16(x[8 * ch + 4], x[8 * ch + 5]), pack_bf16(x[8 * ch + 6], x[8 * ch + 7]));
 }
@@ -633,30 +638,10 @@ __device__ __forceinline__ void tmem_row64(uint32_t taddr, float *x) {
     x[32 + i] = __uint_as_float(w[i]);
   }
 }
-// row `row` of a swizzled bf16 tile in global memory (128 contiguous bytes): w[cb] = columns
-// 8 cb .. 8 cb + 7 (stored in 16-byte chunk cb ^ (row & 7))
-__device__ __forceinline__ void load_row_g(const uint8_t *tile, int row, uint4 (&w)[8]) {
-  const uint8_t *src = tile + row * 128;
-#pragma unroll
-  for (int cb = 0; cb < 8; ++cb) w[cb] = __ldg(reinterpret_cast<const uint4 *>(src + ((cb ^ (row & 7)) << 4)));
-}
-// x[j] += column j of a row loaded by load_row_g
-__device__ __forceinline__ void add_row(float *x, const uint4 (&w)[8]) {
-#pragma unroll
-  for (int cb = 0; cb < 8; ++cb) {
-    const uint32_t u[4] = {w[cb].x, w[cb].y, w[cb].z, w[cb].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16(u[e]);
-      x[8 * cb + 2 * e] += f.x;
-      x[8 * cb + 2 * e + 1] += f.y;
-    }
-  }
-}
 
 __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   const int nc = p.nc;
   const uint32_t s_base = smem_u32(sm);
@@ -664,11 +649,14 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
     return;
   }
-  const uint32_t mrec = s_base + OFF2_MBAR, mA = mrec + 8 * NREC, mB = mA + 16, sready = mB + 16,
-                 done = sready + 8;
-  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * (NREC + 7));
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF2_MBAR + 8 * (NREC + 7) + 4);
-  const bool leader = tid == 192;
+  const uint32_t mrec = s_base + OFF2_MBAR, sfree = mrec + 8 * NREC, mA = sfree + 8 * NREC, mB = mA + 16,
+                 done = mB + 16, mio = done + 16;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * NMBAR2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF2_MBAR + 8 * NMBAR2 + 4);
+  const bool leader = tid == 256;
+  const bool state_warp = warp == 0 || warp == 1 || warp == 4 || warp == 5;
+  const int d = 32 * (warp & 1) + lane;   // state warps: row d of S^T
+  const int half = warp >= 4 ? 32 : 0;    // state warps: first column of their half
   // per-chunk sources: -W, U, O_intra, N in the workspace; Mneg, Qt, e^{gamma_C} in the saved
   // record when there is one, else in the workspace
   const uint8_t *wsb = (const uint8_t *)p.ws + (int64_t)bh * nc * WS_SIZE;
@@ -680,14 +668,17 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   };
 
   if (leader) {
-    for (int i = 0; i < NREC; ++i) mbar_init(mrec + 8 * i, 1);
+    for (int i = 0; i < NREC; ++i) {
+      mbar_init(mrec + 8 * i, 1);
+      mbar_init(sfree + 8 * i, 1);
+    }
     mbar_init(mA, 1);
     mbar_init(mA + 8, 1);
     mbar_init(mB, 1);
     mbar_init(mB + 8, 1);
-    mbar_init(sready, 64);
     mbar_init(done, 128);
     mbar_init(done + 8, 128);
+    for (int i = 0; i < 2 * NIO; ++i) mbar_init(mio + 8 * i, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -699,13 +690,13 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       return;
     }
   }
-  float S[64];  // warps 0-1: S^T[d][j] = S[j][d], d = tid
-  if (warp < 2) {
+  float S[32];  // state warps: S^T[d][half + j] = S[half + j][d]
+  if (state_warp) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j) S[j] = p.state0 ? p.state0[(int64_t)bh * D * D + j * D + tid] : 0.f;
-    store_row_bf16(sm + OFF2_ST, tid, S);
+    for (int j = 0; j < 32; ++j) S[j] = p.state0 ? p.state0[(int64_t)bh * D * D + (half + j) * D + d] : 0.f;
+    store_half_row_bf16(sm + OFF2_ST, d, half, S);
   }
-  if (warp == 6) {
+  if (warp == 8) {
     tmem_alloc(smem_u32(tslot), 256);
     tmem_relinquish();
   }
@@ -720,162 +711,173 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     bulk_s2g((uint8_t *)svb + kSavedS0, s_base + OFF2_ST, 8192);
     bulk_commit();
   }
+  // MMA1 / MMA2 of chunk c (one thread): D1[c & 1] = [Mneg; -W] S^T(c), D2[c & 1] = [-W; Qt] S^T(c)
+  auto issue_mmas = [&](int c) {
+    const int bb = c & 1;
+    const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
+    tc_fence_after();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
+    tc_commit(mA + 8 * bb);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
+    tc_commit(mB + 8 * bb);
+  };
 
   if (leader) {
-    // ---- MMA issue and operand ring ----
-    int issued = 0, landed = 0;
+    // ---- operand ring: a slot is refilled once the MMAs of its chunk and the state warps'
+    //      reads of it are done (thread 0 commits the next chunk's MMAs to sfree[slot]) ----
+    int issued = 0;
     auto issue = [&](int c) {
       const int s = c % NREC;
       const uint32_t dst = s_base + OFF2_REC + s * SLOT, mb = mrec + 8 * s;
-      mbar_expect_tx(mb, SLOT);
+      mbar_expect_tx(mb, SLOT_BYTES);
       bulk_g2s(dst + R_MN, mq_src(c, 0), 8192, mb);
       bulk_g2s(dst + R_W, rec_ws(c) + WS_W, 8192, mb);
       bulk_g2s(dst + R_QT, mq_src(c, 1), 8192, mb);
+      bulk_g2s(dst + R_N, rec_ws(c) + WS_N, 8192, mb);
+      bulk_g2s(dst + R_EG, mq_src(c, 2), 256, mb);
       issued = c + 1;
     };
-    auto prefetch = [&](int c) {
-      if (c >= nc) return;
-      prefetch_l2(rec_ws(c) + WS_W, 4 * 8192);  // -W | U | O_intra | N
-      prefetch_l2(mq_src(c, 0), 8192);
-      prefetch_l2(mq_src(c, 1), 8192);
-    };
     for (int c = 0; c < nc && c < NREC; ++c) issue(c);
-    for (int c = NREC; c < NREC + PF; ++c) prefetch(c);
+    for (int c = 0; c + NREC < nc; ++c) {
+      if (!mbar_wait(sfree + 8 * (c % NREC), (c / NREC) & 1) || *abort_flag) {
+        failed = true;
+        *abort_flag = 1;
+        break;
+      }
+      issue(c + NREC);
+    }
+    if (*abort_flag)  // (bounded) the last copy issued into each slot lands before the CTA exits
+      for (int c = issued > NREC ? issued - NREC : 0; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
+  } else if (state_warp) {
+    // ---- state rows: S <- D1 + e^{gamma_C} S + N, 32 columns per thread ----
+    if (tid == 0) {  // chunk 0's MMAs
+      if (!mbar_wait(mrec, 0)) *abort_flag = 1;
+      else issue_mmas(0);
+    }
     for (int c = 0; c < nc; ++c) {
-      const int s = c % NREC, bb = c & 1;
-      bool ok = mbar_wait(mrec + 8 * s, (c / NREC) & 1);
-      if (ok) landed = c + 1;
-      if (ok && c >= 1) ok = mbar_wait(sready, (c - 1) & 1);              // S^T(c) written
-      if (ok && c >= 2) ok = mbar_wait(done + 8 * bb, ((c - 2) >> 1) & 1); // D1/D2[bb] drained
-      if (!ok || *abort_flag) {
+      const int bb = c & 1, s = c % NREC;
+      const uint8_t *recm = sm + OFF2_REC + s * SLOT;
+      // one decision for the four warps (they meet at named barriers below)
+      if (!bar_and(1, 128, mbar_wait(mrec + 8 * s, (c / NREC) & 1) && mbar_wait(mA + 8 * bb, (c >> 1) & 1) &&
+                              !*abort_flag)) {
         failed = true;
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + s * SLOT;
+      uint32_t v[32];
+      tmem_ld32(tD + 64 * bb + lq + half, v);
+      const float e = reinterpret_cast<const float *>(recm + R_EG)[d];
+      uint4 nw[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
-      tc_commit(mA + 8 * bb);
+      for (int ch = 0; ch < 4; ++ch) nw[ch] = *reinterpret_cast<const uint4 *>(recm + R_N + sw64(d, half + 8 * ch));
+      tmem_wait_ld();
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_QT, k), desc_mn(st, k), kIdescScan, k > 0);
-      tc_commit(mB + 8 * bb);
-      // refill the slot chunk c - 1 used: its MMAs are complete (state rows of c were written
-      // after them) and warps 2-5 have read D1/D2 of c - 1 (checked by the wait on done below)
-      if (c >= 1 && c - 1 + NREC < nc) {
-        if (!mbar_wait(done + 8 * ((c - 1) & 1), ((c - 1) >> 1) & 1)) {
-          failed = true;
-          *abort_flag = 1;
-          break;
+      for (int ch = 0; ch < 4; ++ch) {
+        const uint32_t u[4] = {nw[ch].x, nw[ch].y, nw[ch].z, nw[ch].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16(u[q]);
+          const int j = 8 * ch + 2 * q;
+          S[j] = fmaf(e, S[j], __uint_as_float(v[j]) + f.x);
+          S[j + 1] = fmaf(e, S[j + 1], __uint_as_float(v[j + 1]) + f.y);
         }
-        issue(c - 1 + NREC);
-        prefetch(c - 1 + NREC + PF);
       }
-    }
-    if (failed) {  // (bounded) every copy in flight lands, every MMA issued completes
-      for (int c = landed; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
-      for (int i = 0; i < 2; ++i) {
-        mbar_wait(mA + 8 * i, 0);
-        mbar_wait(mA + 8 * i, 1);
-        mbar_wait(mB + 8 * i, 0);
-        mbar_wait(mB + 8 * i, 1);
-      }
-    }
-  } else if (warp < 2) {
-    // ---- state rows: S <- D1 + e^{gamma_C} S + N ----
-    const int d = tid;
-    uint4 nw[8];
-    float eg = 0.f;
-    if (nc > 0) {
-      load_row_g(rec_ws(0) + WS_N, d, nw);
-      eg = __ldg(reinterpret_cast<const float *>(mq_src(0, 2)) + d);
-    }
-    for (int c = 0; c < nc; ++c) {
-      const int bb = c & 1;
-      // one decision for both warps (they meet at named barriers below)
-      if (!bar_and(1, 64, mbar_wait(mA + 8 * bb, (c >> 1) & 1) && !*abort_flag)) {
-        failed = true;
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      float x[64];
-      tmem_row64(tD + 64 * bb + lq, x);
-      const uint4 ncur[8] = {nw[0], nw[1], nw[2], nw[3], nw[4], nw[5], nw[6], nw[7]};
-      const float e = eg;
-      if (c + 1 < nc) {  // next chunk's N row and decay, one chunk ahead
-        load_row_g(rec_ws(c + 1) + WS_N, d, nw);
-        eg = __ldg(reinterpret_cast<const float *>(mq_src(c + 1, 2)) + d);
-      }
-#pragma unroll
-      for (int j = 0; j < 64; ++j) x[j] = fmaf(e, S[j], x[j]);
-      add_row(x, ncur);
-#pragma unroll
-      for (int j = 0; j < 64; ++j) S[j] = x[j];
       if (c + 1 < nc) {
         // the tile of S^T(c + 1) last held S^T(c + 1 - NST), whose saved-record store (thread 0
         // has issued NST - 1 stores since) must have read it
         if (tid == 0) bulk_wait_read<NST - 1>();
-        bar_sync(1, 64);
-        store_row_bf16(sm + OFF2_ST + ((c + 1) % NST) * 8192, d, S);
+        bar_sync(1, 128);
+        store_half_row_bf16(sm + OFF2_ST + ((c + 1) % NST) * 8192, d, half, S);
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(sready);
-        if (p.saved) {
-          bar_sync(1, 64);
-          if (tid == 0) {
-            bulk_s2g((uint8_t *)svb + (int64_t)(c + 1) * kSavedChunk + kSavedS0,
-                     s_base + OFF2_ST + ((c + 1) % NST) * 8192, 8192);
-            bulk_commit();
+        bar_sync(1, 128);
+        if (tid == 0) {
+          // chunk c + 1's operands have landed and D1 / D2[(c + 1) & 1] (chunk c - 1) are drained
+          bool ok = mbar_wait(mrec + 8 * ((c + 1) % NREC), ((c + 1) / NREC) & 1);
+          if (ok && c >= 1) ok = mbar_wait(done + 8 * ((c + 1) & 1), ((c - 1) >> 1) & 1);
+          if (ok) {
+            issue_mmas(c + 1);
+            tc_commit(sfree + 8 * s);  // slot s (chunk c) is free once these MMAs complete
+            if (p.saved) {
+              bulk_s2g((uint8_t *)svb + (int64_t)(c + 1) * kSavedChunk + kSavedS0,
+                       s_base + OFF2_ST + ((c + 1) % NST) * 8192, 8192);
+              bulk_commit();
+            }
+          } else {
+            *abort_flag = 1;
           }
         }
       }
     }
     if (!failed) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) p.stateT[(int64_t)bh * D * D + j * D + d] = S[j];
+      for (int j = 0; j < 32; ++j) p.stateT[(int64_t)bh * D * D + (half + j) * D + d] = S[j];
     }
-  } else if (warp < 6) {
-    // ---- warps 2-3: Unew rows (training); warps 4-5: O rows ----
+  } else if (warp < 8) {
+    // ---- warps 2-3: Unew rows (training); warps 6-7: O rows ----
     const bool un = warp < 4;
-    const int t = tid - (un ? 64 : 128), bar = un ? 2 : 3;
-    const uint32_t macc = un ? mA : mB;
-    const uint32_t tcol = un ? 0 : 128;
+    const int t = 32 * (warp & 1) + lane, bar = un ? 2 : 3;
+    const bool lead = t == 0;
+    const uint32_t macc = un ? mA : mB, tcol = un ? 0 : 128, mb0 = mio + (un ? 0 : 8 * NIO);
     const int src_off = un ? WS_U : WS_OI;
-    uint4 rw[8];
+    const int ring = un ? OFF2_UN : OFF2_O;
     const bool active = !un || p.saved;
-    if (active && nc > 0) load_row_g(rec_ws(0) + src_off, t, rw);
+    int io_issued = 0;
+    auto load_tile = [&](int c) {
+      const int s = c % NIO;
+      io_issued = c + 1;
+      mbar_expect_tx(mb0 + 8 * s, 8192);
+      bulk_g2s(s_base + ring + s * 8192, rec_ws(c) + src_off, 8192, mb0 + 8 * s);
+    };
+    if (active && lead)
+      for (int c = 0; c < nc && c < NIO - 1; ++c) load_tile(c);
     for (int c = 0; c < nc; ++c) {
-      const int bb = c & 1;
-      if (!bar_and(bar, 64, mbar_wait(macc + 8 * bb, (c >> 1) & 1) && !*abort_flag)) {
+      const int bb = c & 1, s = c % NIO;
+      const bool ok = mbar_wait(macc + 8 * bb, (c >> 1) & 1) && (!active || mbar_wait(mb0 + 8 * s, (c / NIO) & 1));
+      if (!bar_and(bar, 64, ok && !*abort_flag)) {
         failed = true;
         *abort_flag = 1;
+        if (lead)  // (bounded) the last tile load issued into each slot lands before the CTA exits
+          for (int c2 = io_issued > NIO ? io_issued - NIO : 0; c2 < io_issued; ++c2)
+            mbar_wait(mb0 + 8 * (c2 % NIO), (c2 / NIO) & 1);
         break;
       }
       tc_fence_after();
       if (active) {
         float x[64];
         tmem_row64(tD + tcol + 64 * bb + lq, x);
-        const uint4 cur[8] = {rw[0], rw[1], rw[2], rw[3], rw[4], rw[5], rw[6], rw[7]};
-        if (c + 1 < nc) load_row_g(rec_ws(c + 1) + src_off, t, rw);
-        add_row(x, cur);
-        uint8_t *stage = sm + (un ? OFF2_UN : OFF2_O) + bb * 8192;
-        // the staging tile of chunk c - 2 has been read by its store
-        if (t == 0) bulk_wait_read<1>();
-        bar_sync(bar, 64);
-        store_row_bf16(stage, t, x);
+        uint8_t *tile = sm + ring + s * 8192;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {  // + this thread's row of U / O_intra, written back in place
+          const uint4 u = *reinterpret_cast<const uint4 *>(tile + sw64(t, 8 * ch));
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16(w[e]);
+            o[e] = pack_bf16(x[8 * ch + 2 * e] + f.x, x[8 * ch + 2 * e + 1] + f.y);
+          }
+          *reinterpret_cast<uint4 *>(tile + sw64(t, 8 * ch)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(done + 8 * bb);
         bar_sync(bar, 64);
-        if (t == 0) {
-          const uint32_t src = s_base + (un ? OFF2_UN : OFF2_O) + bb * 8192;
+        if (lead) {
+          const uint32_t src = s_base + ring + s * 8192;
           if (un)
             bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedUnT, src, 8192);
           else
             tma_store_rows(&tm.m[0], src, h, c * C, b);  // rows past T are dropped
           bulk_commit();
+          // refill the tile of chunk c - 1 with chunk c - 1 + NIO once its store has read it
+          if (c + NIO - 1 < nc) {
+            bulk_wait_read<1>();
+            load_tile(c + NIO - 1);
+          }
         }
       } else {
         tc_fence_before();
@@ -883,12 +885,21 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       }
     }
   }
-  if (failed && (leader || tid == 0 || tid == 64 || tid == 128)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
-  if (tid == 0 || tid == 64 || tid == 128) bulk_wait_all();  // the stores this thread issued
+  const bool storer = tid == 0 || tid == 64 || tid == 192;  // threads that issue bulk stores
+  if (failed && (leader || storer)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+  if (storer) bulk_wait_all();  // the stores this thread issued have completed
+  if (tid == 0 && *abort_flag) {  // (bounded) no MMA may still write TMEM when it is freed
+    for (int i = 0; i < 2; ++i) {
+      mbar_wait(mA + 8 * i, 0);
+      mbar_wait(mA + 8 * i, 1);
+      mbar_wait(mB + 8 * i, 0);
+      mbar_wait(mB + 8 * i, 1);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 6) tmem_dealloc(tD, 256);
+  if (warp == 8) tmem_dealloc(tD, 256);
 }
 
 template <typename Tb>
