@@ -131,6 +131,19 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, int li
   return false;
 }
 
+// The same bound for a wait on the latency-critical path: polls with the non-blocking test_wait, so
+// the thread sees the phase complete without a suspended try_wait's wake-up delay.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t mbar, uint32_t parity, int limit = kMbarSpinLimit) {
+  for (int i = 0; i < limit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(mbar), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  return mbar_wait(mbar, parity, limit);
+}
+
 // shared -> global bulk copies (bulk-group completion)
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");

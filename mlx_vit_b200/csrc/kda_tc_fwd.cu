@@ -591,15 +591,15 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
 // Warp roles (a warp reaches TMEM lanes 32 (warp % 4) ..):
 //   warps 0, 1, 4, 5  state rows d (lanes 0-63 of D1), warps 0-1 columns 0-31, warps 4-5
 //              columns 32-63: S <- D1 + e^{gamma_C} S + N, bf16 S^T tile for the next MMA;
-//              thread 0 then issues the next chunk's two MMAs itself (no hand-off on the chain)
-//              and stores S^T (the saved chunk-entry state);
+//              thread 0 then issues the next chunk's MMA1 itself (no hand-off on the chain);
 //   warps 2-3  Unew rows t (training only): D1 rows 64-127 + U;
 //   warps 6-7  O rows t: D2 rows 64-127 + O_intra;
 //              each of these two roles keeps a ring of NIO tiles: one thread bulk-loads the
 //              chunk's U / O_intra tile NIO - 1 chunks ahead, every thread adds its TMEM row in
 //              place, and the tile then leaves by a bulk / TMA store;
-//   warp 8     one thread keeps a ring of the chunk operands (Mneg, -W, Qt, N, e^{gamma_C}: bulk
-//              copies) NREC chunks deep, refilling a slot once the MMAs that read it are done.
+//   warp 8     one thread issues MMA2, stores S^T (the saved chunk-entry state) and keeps a ring of
+//              the chunk operands (Mneg, -W, Qt, N, e^{gamma_C}: bulk copies) NREC chunks deep,
+//              refilling a slot once the MMAs that read it are done.
 // Every wait is bounded; a role that gives up raises `abort`, which the others poll, and the
 // teardown drains copies, MMAs and stores before TMEM is freed.
 constexpr int NT2 = 288;
@@ -607,14 +607,14 @@ constexpr int NREC = 4;                        // ring of chunk operand slots
 constexpr int R_MN = 0, R_W = 8192, R_QT = 16384, R_N = 24576, R_EG = 32768;
 constexpr int SLOT_BYTES = 32768 + 256;        // what one slot's copies bring
 constexpr int SLOT = 33 * 1024;                // slot stride (1024-byte aligned)
-constexpr int NST = 3;                         // bf16 S^T tiles (MMA B operand, saved-record staging)
-constexpr int NIO = 4;                         // U -> Unew and O_intra -> O tiles per role
+constexpr int NST = 4;                         // bf16 S^T tiles (MMA B operand, saved-record staging)
+constexpr int NIO = 3;                         // U -> Unew and O_intra -> O tiles per role
 constexpr int OFF2_REC = 0;
 constexpr int OFF2_ST = OFF2_REC + NREC * SLOT;   // NST x 8 KB
 constexpr int OFF2_UN = OFF2_ST + NST * 8192;     // NIO x 8 KB
 constexpr int OFF2_O = OFF2_UN + NIO * 8192;      // NIO x 8 KB
-constexpr int OFF2_MBAR = OFF2_O + NIO * 8192;    // mrec[NREC] sfree[NREC] mA[2] mB[2] done[2] io[2][NIO], TMEM slot, abort
-constexpr int NMBAR2 = 2 * NREC + 6 + 2 * NIO;
+constexpr int OFF2_MBAR = OFF2_O + NIO * 8192;    // mrec[NREC] sfree[NREC] mA[2] mB[2] done[2] io[2][NIO] go2[2], TMEM slot, abort
+constexpr int NMBAR2 = 2 * NREC + 8 + 2 * NIO;
 constexpr int SMEM2 = OFF2_MBAR + 8 * NMBAR2 + 16;
 constexpr uint32_t kIdescScan = idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
 
@@ -650,7 +650,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     return;
   }
   const uint32_t mrec = s_base + OFF2_MBAR, sfree = mrec + 8 * NREC, mA = sfree + 8 * NREC, mB = mA + 16,
-                 done = mB + 16, mio = done + 16;
+                 done = mB + 16, mio = done + 16, go2 = mio + 16 * NIO;
   uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * NMBAR2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF2_MBAR + 8 * NMBAR2 + 4);
   const bool leader = tid == 256;
@@ -679,6 +679,8 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     mbar_init(done, 128);
     mbar_init(done + 8, 128);
     for (int i = 0; i < 2 * NIO; ++i) mbar_init(mio + 8 * i, 1);
+    mbar_init(go2, 1);
+    mbar_init(go2 + 8, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -707,26 +709,21 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   const uint32_t tD = *tslot;
   const uint32_t lq = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's TMEM lane quarter
   bool failed = false;
-  if (p.saved && tid == 0) {  // the first chunk's entry state for the backward
-    bulk_s2g((uint8_t *)svb + kSavedS0, s_base + OFF2_ST, 8192);
-    bulk_commit();
-  }
-  // MMA1 / MMA2 of chunk c (one thread): D1[c & 1] = [Mneg; -W] S^T(c), D2[c & 1] = [-W; Qt] S^T(c)
-  auto issue_mmas = [&](int c) {
+  // MMA1 of chunk c (thread 0, on the chain): D1[c & 1] = [Mneg; -W] S^T(c); then thread 0 hands
+  // chunk c to the leader (go2), which issues MMA2: D2[c & 1] = [-W; Qt] S^T(c)
+  auto issue_mma1 = [&](int c) {
     const int bb = c & 1;
     const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
     tc_fence_after();
 #pragma unroll
     for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
     tc_commit(mA + 8 * bb);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
-    tc_commit(mB + 8 * bb);
+    mbar_arrive(go2 + 8 * bb);
   };
-
   if (leader) {
-    // ---- operand ring: a slot is refilled once the MMAs of its chunk and the state warps'
-    //      reads of it are done (thread 0 commits the next chunk's MMAs to sfree[slot]) ----
+    // ---- MMA2 of every chunk, and the operand ring: a slot is refilled once both MMAs of its
+    //      chunk are complete and the state warps have read it (thread 0 commits the next
+    //      chunk's MMA1 to sfree[slot]) ----
     int issued = 0;
     auto issue = [&](int c) {
       const int s = c % NREC;
@@ -740,13 +737,31 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       issued = c + 1;
     };
     for (int c = 0; c < nc && c < NREC; ++c) issue(c);
-    for (int c = 0; c + NREC < nc; ++c) {
-      if (!mbar_wait(sfree + 8 * (c % NREC), (c / NREC) & 1) || *abort_flag) {
+    for (int c = 0; c < nc; ++c) {
+      const int bb = c & 1;
+      // thread 0 has written S^T(c) and issued MMA1(c) (after chunk c's operands landed)
+      bool ok = mbar_wait(go2 + 8 * bb, (c >> 1) & 1) && mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
+      if (ok && !*abort_flag) {
+        const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
+        tc_commit(mB + 8 * bb);
+        if (p.saved) {  // S^T(c), the chunk-entry state of the saved record
+          bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedS0, st, 8192);
+          bulk_commit();
+          bulk_wait_read<1>();  // S^T(c - 1)'s store has read its tile (see the state warps)
+        }
+      }
+      if (ok && c >= 1 && c - 1 + NREC < nc)  // chunk c - 1's slot: MMA2(c - 1) done, state reads done
+        ok = mbar_wait(mB + 8 * ((c - 1) & 1), ((c - 1) >> 1) & 1) &&
+             mbar_wait(sfree + 8 * ((c - 1) % NREC), ((c - 1) / NREC) & 1);
+      if (!ok || *abort_flag) {
         failed = true;
         *abort_flag = 1;
         break;
       }
-      issue(c + NREC);
+      if (c >= 1 && c - 1 + NREC < nc) issue(c - 1 + NREC);
     }
     if (*abort_flag)  // (bounded) the last copy issued into each slot lands before the CTA exits
       for (int c = issued > NREC ? issued - NREC : 0; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
@@ -754,13 +769,13 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     // ---- state rows: S <- D1 + e^{gamma_C} S + N, 32 columns per thread ----
     if (tid == 0) {  // chunk 0's MMAs
       if (!mbar_wait(mrec, 0)) *abort_flag = 1;
-      else issue_mmas(0);
+      else issue_mma1(0);
     }
     for (int c = 0; c < nc; ++c) {
       const int bb = c & 1, s = c % NREC;
       const uint8_t *recm = sm + OFF2_REC + s * SLOT;
       // one decision for the four warps (they meet at named barriers below)
-      if (!bar_and(1, 128, mbar_wait(mrec + 8 * s, (c / NREC) & 1) && mbar_wait(mA + 8 * bb, (c >> 1) & 1) &&
+      if (!bar_and(1, 128, mbar_wait(mrec + 8 * s, (c / NREC) & 1) && mbar_wait_spin(mA + 8 * bb, (c >> 1) & 1) &&
                               !*abort_flag)) {
         failed = true;
         *abort_flag = 1;
@@ -786,26 +801,22 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
         }
       }
       if (c + 1 < nc) {
-        // the tile of S^T(c + 1) last held S^T(c + 1 - NST), whose saved-record store (thread 0
-        // has issued NST - 1 stores since) must have read it
-        if (tid == 0) bulk_wait_read<NST - 1>();
+        // D1 / D2[(c + 1) & 1] (chunk c - 1) are drained.  This also frees the tile of S^T(c + 1),
+        // which last held S^T(c + 1 - NST): the leader saw that state's saved-record store read
+        // its tile before it issued MMA2(c - 1), and done(c - 1) follows MMA2(c - 1)
+        bool drained = true;
+        if (tid == 0 && c >= 1) drained = mbar_wait(done + 8 * ((c + 1) & 1), ((c - 1) >> 1) & 1);
         bar_sync(1, 128);
         store_half_row_bf16(sm + OFF2_ST + ((c + 1) % NST) * 8192, d, half, S);
         fence_proxy_async_smem();
         tc_fence_before();
         bar_sync(1, 128);
         if (tid == 0) {
-          // chunk c + 1's operands have landed and D1 / D2[(c + 1) & 1] (chunk c - 1) are drained
-          bool ok = mbar_wait(mrec + 8 * ((c + 1) % NREC), ((c + 1) / NREC) & 1);
-          if (ok && c >= 1) ok = mbar_wait(done + 8 * ((c + 1) & 1), ((c - 1) >> 1) & 1);
+          // chunk c + 1's operands have landed
+          const bool ok = drained && mbar_wait(mrec + 8 * ((c + 1) % NREC), ((c + 1) / NREC) & 1);
           if (ok) {
-            issue_mmas(c + 1);
-            tc_commit(sfree + 8 * s);  // slot s (chunk c) is free once these MMAs complete
-            if (p.saved) {
-              bulk_s2g((uint8_t *)svb + (int64_t)(c + 1) * kSavedChunk + kSavedS0,
-                       s_base + OFF2_ST + ((c + 1) % NST) * 8192, 8192);
-              bulk_commit();
-            }
+            issue_mma1(c + 1);
+            tc_commit(sfree + 8 * s);  // slot s (chunk c) is free once MMA1(c + 1) completes
           } else {
             *abort_flag = 1;
           }
@@ -885,7 +896,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       }
     }
   }
-  const bool storer = tid == 0 || tid == 64 || tid == 192;  // threads that issue bulk stores
+  const bool storer = leader || tid == 64 || tid == 192;  // threads that issue bulk stores
   if (failed && (leader || storer)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
   if (storer) bulk_wait_all();  // the stores this thread issued have completed
   if (tid == 0 && *abort_flag) {  // (bounded) no MMA may still write TMEM when it is freed
@@ -929,6 +940,7 @@ int launch(const Params &p, cudaStream_t st) {
 }
 
 }  // namespace tcfwd
+
 
 int tc_fwd_device_status(bool reset) {
   int v = 0;
