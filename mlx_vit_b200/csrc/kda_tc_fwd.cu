@@ -1,14 +1,13 @@
 // Tensor-core KDA forward for D = 64, chunk = 64, bf16 q/k/v, in two kernels.
 //
-//  kda_fwd_chunks  one persistent CTA per SM walking all (b, h, chunk), which are independent:
-//                  every state-independent quantity of the chunk, written as a per-chunk record
-//                  (-W, U, Qd, Kb, P as bf16 tiles, e^{gamma_C}) to the forward workspace,
-//                  and, for training, the state-independent part of the backward's record
-//                  (P, M, Tinv = (I+A)^{-1}, Mneg = -Kb^T W, Qt = Qd - P W).
-//  kda_fwd_scan    one CTA of 5 warps per (b, h): streams the chunk records (bulk copies, two
-//                  chunks ahead) and advances the state with two tcgen05 MMAs per chunk into one
-//                  M = 128 TMEM accumulator (the fp32 state itself stays in registers):
-//                    Unew = U - W S^T;  O = Qd S^T + P Unew;  S^T <- diag(e^{gamma_C}) S^T + Kb^T Unew
+//  kda_fwd_chunks  one CTA per (b, h, chunk), two CTAs per SM; chunks are independent: every
+//                  state-independent quantity of the chunk, written as a per-chunk record to the
+//                  forward workspace (-W, U, O_intra = P U, N = Kb^T U) and, for training, the
+//                  backward's record (P, M, Tinv = (I+A)^{-1}, Mneg = -Kb^T W, Qt = Qd - P W,
+//                  e^{gamma_C}; without one, Mneg, Qt and e^{gamma_C} go to the workspace).
+//  kda_fwd_scan    one CTA per (b, h): the state recurrence S^T <- diag(e^{gamma_C}) S^T +
+//                  Mneg S^T + N, one tcgen05 MMA per chunk on the chain, with O = Qt S^T +
+//                  O_intra and Unew = U - W S^T formed beside it (see the kernel's comment).
 //
 // Chunk quantities (gamma = cumsum(g) inside the chunk, rows t, 16-row blocks b(t), r_i = gamma
 // at the middle row of block i):
@@ -44,8 +43,7 @@ constexpr float kMidGapMax = 80.f;
 
 // the chunk kernel's tiles of per-chunk values in shared memory (bf16, swizzled): Qd = q e^gamma
 // [t][d], -W [t][d], U [t][j], P [t][s] (zero above the diagonal), e^{gamma_C} (fp32)
-constexpr int HO_QD = 0, HO_W = 8192, HO_U = 16384, HO_P = 24576, HO_EG = 40960;
-constexpr int HO_SIZE = 40960 + 256;
+constexpr int HO_QD = 0, HO_W = 8192, HO_U = 16384, HO_P = 24576, HO_EG = 32768;
 // per-chunk record handed from kda_fwd_chunks to kda_fwd_scan in the forward workspace (bf16
 // tiles, swizzled as in shared memory): Mneg = -Kb^T W [d][d'], Qt = Qd - P W [t][d], -W [t][d],
 // U [t][j], O_intra = P U [t][j], N = Kb^T U [d][j], e^{gamma_C} (fp32).  With a saved record
@@ -57,48 +55,39 @@ constexpr int WS_SIZE = 49152 + 256;
 // ---------------------------------------------------------------------------------------
 // kda_fwd_chunks
 // ---------------------------------------------------------------------------------------
-constexpr int NT1 = 512;  // 16 warps: every phase splits into more independent pieces
-constexpr int OFF_QS = 0;                                // raw q/k/v tiles (TMA, 128-byte swizzle,
-constexpr int OFF_KS = OFF_QS + 8192;                    //   1024-byte aligned)
-constexpr int OFF_VS = OFF_KS + 8192;
-constexpr int OFF_GS = OFF_VS + 8192;                    // g (TMA) -> gamma (fp32, gsw layout) 16 KB
-constexpr int OFF_OUT = OFF_GS + 16384;                  // the record, swizzled tiles
-constexpr int OFF_KD = OFF_OUT + HO_SIZE;                // Kdec
-constexpr int OFF_QD = OFF_KD + 8192;                    // Qdec
-constexpr int OFF_KI = OFF_QD + 8192;                    // Kinc, 10 tiles of 16x64
-constexpr int OFF_AB = OFF_KI + 10 * 2048;               // A off-diagonal blocks (bf16)
-constexpr int OFF_AD = OFF_AB + 8192;                    // A diagonal blocks fp32 4x16x16
-constexpr int OFF_TI = OFF_AD + 4096;                    // T_ii bf16 4x16x16
-constexpr int OFF_XK = OFF_TI + 2048;                    // beta Kd
-constexpr int OFF_XV = OFF_XK + 8192;                    // beta V
-constexpr int OFF_MK = OFF_XV + 8192;                    // M = Kdec Kinc^T strict lower (bf16)
-constexpr int OFF_TF = OFF_MK + 8192;                    // Tinv = (I + A)^{-1} (bf16), after OFF_MK
-constexpr int OFF_KBS = OFF_TF + 8192;                   // Kb [t][d] (bf16)
-constexpr int OFF_RS = OFF_KBS + 8192;                   // per-warp 16x16 staging
-constexpr int OFF_VEC = OFF_RS + 16 * 256;
-// vectors (floats): bet[64] refs[4][64] part[8][64] erb[4][64] egr[4][64] gij[16][64] flag[4]
-constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 832, V_EGR = 1088, V_G = 1344,
-              V_FLAG = 2368;
-constexpr int OFF_MBAR1 = OFF_VEC + (2368 + 4) * 4;      // mbarrier of the TMA loads
+// One CTA of 8 warps per chunk, with about 107 KB of shared memory so that two CTAs share an SM:
+// each chunk's phases meet at CTA barriers, and the other CTA's work fills those gaps.  Tiles are
+// reused as their contents die (the phase that frees each is noted).
+constexpr int NT1 = 256;
+constexpr int R_QS = 0;                // q (TMA) -> Qdec (operand build, in place) -> N staging (6)
+constexpr int R_KS = 8192;             // k (TMA) -> Kdec (in place) -> Tinv (4)
+constexpr int R_VS = 16384;            // v (TMA) -> beta V (in place) -> Qt staging (6)
+constexpr int R_GS = 24576;            // g (TMA, fp32) or f -> gamma -> beta Kd | Kb (operand build)
+constexpr int R_XK = R_GS, R_KB = R_GS + 8192;   //   beta Kd -> Mneg staging (6);  Kb [t][d]
+constexpr int OFF_OUT = 40960;         // Qd, -W, U, P tiles and e^{gamma_C} (HO_*); Kinc's four
+                                       //   diagonal 16 x 64 tiles sit in -W | U until (2) is done
+constexpr int R_KI = OFF_OUT + HO_W;
+constexpr int R_MK = OFF_OUT + 33 * 1024;   // M = Kdec Kinc^T strict lower (bf16), saved
+constexpr int R_AB = R_MK + 8192;      // A off-diagonal blocks (bf16) -> O_intra staging (6)
+constexpr int R_AD = R_AB + 8192;      // A diagonal blocks fp32 4 x 16 x 16
+constexpr int R_TI = R_AD + 4096;      // T_ii bf16 4 x 16 x 16
+constexpr int R_RS = R_TI + 2048;      // per-warp 16 x 16 staging of the block solve
+constexpr int OFF_VEC = R_RS + 8 * 256;
+// vectors (floats): bet[64] refs[4][64] part[4][64] erb[4][64] egr[4][64] gij[16][64] gend[4][64]
+// gC[64] flag[4]
+constexpr int V_BET = 0, V_REFS = 64, V_PART = 320, V_ERB = 576, V_EGR = 832, V_G = 1088, V_GEND = 2112,
+              V_GC = 2368, V_FLAG = 2432;
+constexpr int OFF_MBAR1 = OFF_VEC + (2432 + 4) * 4;  // mbarrier of the TMA loads
 constexpr int SMEM1 = OFF_MBAR1 + 8;
-// fused gates only: the raw f tile (TMA, bf16), then the staged gate parameters
-constexpr int OFF_FS1 = (SMEM1 + 1023) & ~1023;
-constexpr int SMEM1_GP = OFF_FS1 + 8192;
 
-__device__ __forceinline__ int ki_index(int i, int j) { return i * (i + 1) / 2 + j; }
-
-// Block forward substitution Y = (I+A)^{-1} X for the 8 columns n0..n0+7, by one warp:
-//   Y_i = T_ii (X_i - sum_{j<i} A_ij Y_j),  i = ib..3  (rows of blocks below ib are zero).
-// Y is a swizzled tile at byte offset y_off from OFF_OUT, stored as so * Y; the stored values
-// of earlier blocks are read back with the sign sg = -so.  X is a swizzled tile at x_off, or the
-// identity when x_off < 0 (Y is then Tinv).
-__device__ __forceinline__ void solve_columns(uint8_t *sm, uint32_t s_base, int y_off, int x_off, int n0,
-                                              int ib, float sg, float so, int warp, int lane) {
+// Block forward substitution Tinv = (I+A)^{-1} for the 8 columns n0..n0+7, by one warp:
+//   Y_i = T_ii (E_i - sum_{j<i} A_ij Y_j),  i = ib..3  (rows of blocks below ib are zero).
+__device__ __forceinline__ void solve_columns(uint8_t *sm, uint32_t s_base, int n0, int ib, int warp, int lane) {
   const int g4 = lane >> 2, c4 = lane & 3, l15 = lane & 15;
-  const uint32_t Yb = s_base + OFF_OUT + y_off;
-  uint8_t *Ym = sm + OFF_OUT + y_off;
-  const uint32_t Rs = s_base + OFF_RS + warp * 256;
-  uint8_t *Rm = sm + OFF_RS + warp * 256;
+  const uint32_t Yb = s_base + R_KS;
+  uint8_t *Ym = sm + R_KS;
+  const uint32_t Rs = s_base + R_RS + warp * 256;
+  uint8_t *Rm = sm + R_RS + warp * 256;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     if (i < ib) continue;
@@ -107,136 +96,114 @@ __device__ __forceinline__ void solve_columns(uint8_t *sm, uint32_t s_base, int 
     for (int j = 0; j < i; ++j) {
       if (j < ib) continue;
       uint32_t af[4], bf[2];
-      ldsm_x4(a_frag_addr(s_base + OFF_AB, 16 * i, 16 * j, lane), af);
+      ldsm_x4(a_frag_addr(s_base + R_AB, 16 * i, 16 * j, lane), af);
       ldsm_x2_t(Yb + sw64(16 * j + (l15 & 7) + ((l15 >> 3) << 3), n0), bf);
       mma16816(acc, af, bf[0], bf[1]);
     }
-    // R = X_i + sg * acc -> bf16 staging [t][col] 16x8
+    // R = E_i - acc -> bf16 staging [t][col] 16x8
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int tl = g4 + 8 * hh, col = n0 + 2 * c4;
-      float2 x;
-      if (x_off >= 0) {
-        x = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + x_off + sw64(16 * i + tl, col)));
-      } else {
-        x.x = 16 * i + tl == col ? 1.f : 0.f;
-        x.y = 16 * i + tl == col + 1 ? 1.f : 0.f;
-      }
-      *reinterpret_cast<uint32_t *>(Rm + tl * 16 + c4 * 4) =
-          pack_bf16(x.x + sg * acc[2 * hh], x.y + sg * acc[2 * hh + 1]);
+      const float x0 = 16 * i + tl == col ? 1.f : 0.f, x1 = 16 * i + tl == col + 1 ? 1.f : 0.f;
+      *reinterpret_cast<uint32_t *>(Rm + tl * 16 + c4 * 4) = pack_bf16(x0 - acc[2 * hh], x1 - acc[2 * hh + 1]);
     }
     __syncwarp();
     uint32_t af[4], bf[2];
-    ldsm_x4(s_base + OFF_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
+    ldsm_x4(s_base + R_TI + i * 512 + (lane & 15) * 32 + (lane >> 4) * 16, af);
     ldsm_x2_t(Rs + ((l15 & 7) + ((l15 >> 3) << 3)) * 16, bf);
     float y[4] = {};
     mma16816(y, af, bf[0], bf[1]);
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int t = 16 * i + g4 + 8 * hh, col = n0 + 2 * c4;
-      *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(so * y[2 * hh], so * y[2 * hh + 1]);
+      *reinterpret_cast<uint32_t *>(Ym + sw64(t, col)) = pack_bf16(y[2 * hh], y[2 * hh + 1]);
     }
     __syncwarp();
   }
 }
 
 template <typename Tb>
-__global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
+__global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g4 = lane >> 2, c4 = lane & 3;
-  const int nc = p.nc, T = p.T, H = p.H, nchunks = p.B * p.H * nc;
+  const int nc = p.nc, T = p.T, H = p.H;
+  const int idx = blockIdx.x, bh = idx / nc, c = idx % nc, b = bh / H, h = bh % H, t0 = c * C;
   const uint32_t s_base = smem_u32(sm);
   if (s_base & 1023) {  // TMA tiles with the 128-byte swizzle need a 1024-byte aligned base
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
     return;
   }
-  float *GS = reinterpret_cast<float *>(sm + OFF_GS);
-  float *AD = reinterpret_cast<float *>(sm + OFF_AD);
+  float *GS = reinterpret_cast<float *>(sm + R_GS);
+  float *AD = reinterpret_cast<float *>(sm + R_AD);
   float *vec = reinterpret_cast<float *>(sm + OFF_VEC);
   float *bet = vec + V_BET, *refs = vec + V_REFS, *part = vec + V_PART;
-  float *erb = vec + V_ERB, *egr = vec + V_EGR, *gij = vec + V_G;
+  float *erb = vec + V_ERB, *egr = vec + V_EGR, *gij = vec + V_G, *gend = vec + V_GEND, *gCv = vec + V_GC;
   int *flag = reinterpret_cast<int *>(vec + V_FLAG);
   uint8_t *hom = sm + OFF_OUT;
   const uint32_t ho = s_base + OFF_OUT;
   float *eG = reinterpret_cast<float *>(hom + HO_EG);
-  const Tb *betag = (const Tb *)p.beta;
+  const int nvalid = min(C, T - t0);
 
-  // the CTA is persistent: it walks chunks idx = blockIdx.x, + gridDim.x, ...; the TMA loads of
-  // the next chunk are issued as soon as this chunk's raw tiles are consumed
   const uint32_t mbar = s_base + OFF_MBAR1;
   if (tid == 0) {
     mbar_init(mbar, 1);
     mbar_fence_init();
+    mbar_expect_tx(mbar, 3 * 8192 + (p.gated ? 8192 : 16384));
+    tma_load_rows(s_base + R_QS, &tm.m[0], h, t0, b, mbar);
+    tma_load_rows(s_base + R_KS, &tm.m[1], h, t0, b, mbar);
+    tma_load_rows(s_base + R_VS, &tm.m[2], h, t0, b, mbar);
+    if (p.gated)  // the gate pre-activation f (bf16) into the first half of GS, converted in place
+      tma_load_rows(s_base + R_GS, &tm.m[3], h, t0, b, mbar);
+    else
+      tma_load_rows_f32(s_base + R_GS, &tm.m[3], h, t0, b, mbar);
   }
-  const float *gA_log;
-  const float *gdtb = stage_gate_params(reinterpret_cast<float *>(sm + SMEM1_GP), p, tid, NT1, &gA_log);
-  __syncthreads();
-  auto issue_loads = [&](int i) {  // q, k, v tiles (swizzled) and g (fp32) of chunk i
-    if (tid == 0) {
-      const int bh_ = i / nc, t0_ = (i % nc) * C, b_ = bh_ / H, h_ = bh_ % H;
-      mbar_expect_tx(mbar, 3 * 8192 + (p.gated ? 8192 : 16384));
-      tma_load_rows(s_base + OFF_QS, &tm.m[0], h_, t0_, b_, mbar);
-      tma_load_rows(s_base + OFF_KS, &tm.m[1], h_, t0_, b_, mbar);
-      tma_load_rows(s_base + OFF_VS, &tm.m[2], h_, t0_, b_, mbar);
-      if (p.gated)  // the gate pre-activation f (bf16), converted into GS
-        tma_load_rows(s_base + OFF_FS1, &tm.m[3], h_, t0_, b_, mbar);
-      else
-        tma_load_rows_f32(s_base + OFF_GS, &tm.m[3], h_, t0_, b_, mbar);
-    }
-  };
-  // beta of the next chunk, kept raw until its use so that the load does not stall anyone
-  auto load_beta = [&](int i) -> Tb {
-    const int bh_ = i / nc, c_ = i % nc, t = c_ * C + tid;
-    return t < T ? betag[at(p.sb, bh_ / H, t, bh_ % H)] : from_f<Tb>(0.f);
-  };
-  // P's blocks above the diagonal are zero (the scan multiplies the whole tile); nothing else
-  // writes them, so they are cleared once
+  Tb beta_raw = from_f<Tb>(0.f);
+  if (tid < C && tid < nvalid) beta_raw = ((const Tb *)p.beta)[at(p.sb, b, t0 + tid, h)];
+  // P's blocks above the diagonal are zero (the scan's products read whole tiles)
   for (int u = tid; u < 192; u += NT1) {
-    const int blk = u >> 5, r = (u >> 1) & 15, half = u & 1;
+    const int blk = u >> 5, r = (u >> 1) & 15, hf = u & 1;
     const int i = blk < 3 ? 0 : blk < 5 ? 1 : 2, j = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-    *reinterpret_cast<uint4 *>(hom + HO_P + sw64(16 * i + r, 16 * j + 8 * half)) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4 *>(hom + HO_P + sw64(16 * i + r, 16 * j + 8 * hf)) = make_uint4(0u, 0u, 0u, 0u);
   }
-  int idx = blockIdx.x;
-  if (idx < nchunks) issue_loads(idx);
-  Tb beta_next = (idx < nchunks && tid < C) ? load_beta(idx) : from_f<Tb>(0.f);
-
-  for (int it = 0; idx < nchunks; idx += gridDim.x, ++it) {
-  if (__syncthreads_or(!mbar_wait(mbar, it & 1))) {  // this chunk's q, k, v, g
+  __syncthreads();  // the mbarrier is initialised before anyone waits on it
+  if (__syncthreads_or(!mbar_wait(mbar, 0))) {
     if (tid == 0) {
       atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
-      mbar_wait(mbar, it & 1);  // (bounded) the loads in flight land before the CTA exits
+      mbar_wait(mbar, 0);  // (bounded) the loads in flight land before the CTA exits
     }
-    break;
+    return;
   }
-  const int nvalid = min(C, T - (idx % nc) * C);
   if (tid < C)
-    bet[tid] = !p.gated ? to_f(beta_next) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_next)) : 0.f;
-  if (p.gated) gate_to_g(sm + OFF_FS1, GS, gA_log, gdtb, idx / nc % H, nvalid, tid, false);
+    bet[tid] = !p.gated ? to_f(beta_raw) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_raw)) : 0.f;
+  if (p.gated) {  // rows 0-31, then 32-63 (each call reads its rows of f before writing them)
+    gate_to_g(sm + R_GS, GS, p.A_log, p.dt_bias, h, nvalid, tid, true);
+    gate_to_g(sm + R_GS, GS, p.A_log, p.dt_bias, h, nvalid, tid + NT1, true);
+  }
   __syncthreads();
 
-  // ---- (1a) gamma = cumsum(g): 8 segments of 8 rows per channel ----
+  // ---- (1a) gamma = cumsum(g): 4 segments of 16 rows per channel ----
   {
     const int d = tid & 63, seg = tid >> 6;
     float acc = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc += GS[gsw(seg * 8 + r, d)];
+    for (int r = 0; r < 16; ++r) acc += GS[gsw(seg * 16 + r, d)];
     part[seg * 64 + d] = acc;
     __syncthreads();
     float off = 0.f;
     for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      off += GS[gsw(seg * 8 + r, d)];
-      GS[gsw(seg * 8 + r, d)] = off;
+    for (int r = 0; r < 16; ++r) {
+      off += GS[gsw(seg * 16 + r, d)];
+      GS[gsw(seg * 16 + r, d)] = off;
     }
     __syncthreads();
   }
   // guard: factored decay stays within e^{kSpanMax} unless gamma moves more than that across
-  // half a 16-row block.  Such a "big" chunk factors e^{gamma_t - gamma_s} (t in block i > j,
-  // the block of s) as A_t G_ij B_s with A_t = e^{gamma_t - gamma(start of i)},
-  // G_ij = e^{gamma(start of i) - gamma(end of j)}, B_s = e^{gamma(end of j) - gamma_s}, every
-  // factor <= 1, and computes its diagonal blocks exactly.
+  // half a 16-row block (or the block-pair factors would leave fp32's range, kMidGapMax).  Such a
+  // "big" chunk factors e^{gamma_t - gamma_s} (t in block i > j, the block of s) as A_t G_ij B_s
+  // with A_t = e^{gamma_t - gamma(start of i)}, G_ij = e^{gamma(start of i) - gamma(end of j)},
+  // B_s = e^{gamma(end of j) - gamma_s}, every factor <= 1, and computes its diagonal blocks exactly.
   if (tid < 64) {
     float span = 0.f;
 #pragma unroll
@@ -248,12 +215,11 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     const int any = __any_sync(0xffffffffu, !(span <= kSpanMax));
     if (lane == 0) flag[warp] = any;
   }
-  // the previous chunk's bulk stores have read the record and staging tiles written from here on
-  if (tid == 0) bulk_wait_read_all();
   __syncthreads();
   const bool big = flag[0] | flag[1];
-  {  // per-block vectors, thread (slot, d): slot i < 4 -> block i's entries, slot 4 -> e^{gamma_C}
-    const int d = tid & 63, slot = tid >> 6, ro = big ? 0 : 8;
+  // per-block vectors, item (slot, d): slot i < 4 -> block i's entries, slot 4 -> gamma_C
+  for (int u = tid; u < 320; u += NT1) {
+    const int d = u & 63, slot = u >> 6, ro = big ? 0 : 8;
     const float gC = GS[gsw(63, d)];
     if (slot < 4) {
       const int i = slot;
@@ -261,79 +227,21 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       refs[i * 64 + d] = ri;
       erb[i * 64 + d] = __expf(ri);
       egr[i * 64 + d] = __expf(gC - ri);
+      gend[i * 64 + d] = GS[gsw(i * 16 + 15, d)];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         gij[(i * 4 + j) * 64 + d] = j < i ? __expf(ri - GS[gsw(j * 16 + (big ? 15 : ro), d)]) : (j == i ? 1.f : 0.f);
-    } else if (slot == 4) {
+    } else {
       eG[d] = __expf(gC);
+      gCv[d] = gC;
     }
   }
   __syncthreads();
 
-  // ---- (1b) operand build: 512 units of (row t, 8 consecutive channels) ----
-  for (int u = tid; u < 512; u += NT1) {
-    const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
-    const uint32_t off = sw64(t, d0);
-    const uint4 kq = *reinterpret_cast<const uint4 *>(sm + OFF_KS + off);
-    const uint4 qq = *reinterpret_cast<const uint4 *>(sm + OFF_QS + off);
-    const uint4 vq = *reinterpret_cast<const uint4 *>(sm + OFF_VS + off);
-    const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w},
-                   vw[4] = {vq.x, vq.y, vq.z, vq.w};
-    const float bt = bet[t];
-    const float4 ga4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0));
-    const float4 gb4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0 + 4));
-    const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
-    uint32_t okd[4], oqd[4], oxk[4], oxv[4], oqe[4], okb[4], oki[1][4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
-      const int d = d0 + 2 * e;
-      float F[2], iF[2], eg[2], eb[2];
-      const float2 rf2 = *reinterpret_cast<const float2 *>(refs + blk * 64 + d);
-      const float2 er2 = *reinterpret_cast<const float2 *>(erb + blk * 64 + d);
-      const float2 eq2 = *reinterpret_cast<const float2 *>(egr + blk * 64 + d);
-      const float rf[2] = {rf2.x, rf2.y}, er[2] = {er2.x, er2.y}, eq[2] = {eq2.x, eq2.y};
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        const float gm = gam[2 * e + x];
-        F[x] = __expf(gm - rf[x]);
-        if (!big) {
-          iF[x] = __fdividef(1.f, F[x]);
-          eg[x] = F[x] * er[x];
-          eb[x] = iF[x] * eq[x];
-        } else {
-          iF[x] = 0.f;
-          eg[x] = __expf(gm);
-          eb[x] = __expf(GS[gsw(63, d + x)] - gm);
-        }
-      }
-      okd[e] = pack_bf16(kf.x * F[0], kf.y * F[1]);
-      oqd[e] = pack_bf16(qf.x * F[0], qf.y * F[1]);
-      oxk[e] = pack_bf16(bt * kf.x * eg[0], bt * kf.y * eg[1]);
-      oqe[e] = pack_bf16(qf.x * eg[0], qf.y * eg[1]);
-      oxv[e] = pack_bf16(bt * vf.x, bt * vf.y);
-      okb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
-      if (!big) {  // Kinc of the diagonal block only: k / F (the GEMMs rescale it per block pair)
-        oki[0][e] = pack_bf16(kf.x * iF[0], kf.y * iF[1]);
-      } else {  // k B_s
-        const float ge0 = GS[gsw(16 * blk + 15, d)], ge1 = GS[gsw(16 * blk + 15, d + 1)];
-        oki[0][e] = pack_bf16(kf.x * __expf(ge0 - gam[2 * e]), kf.y * __expf(ge1 - gam[2 * e + 1]));
-      }
-    }
-    *reinterpret_cast<uint4 *>(sm + OFF_KD + off) = make_uint4(okd[0], okd[1], okd[2], okd[3]);
-    *reinterpret_cast<uint4 *>(sm + OFF_QD + off) = make_uint4(oqd[0], oqd[1], oqd[2], oqd[3]);
-    *reinterpret_cast<uint4 *>(sm + OFF_XK + off) = make_uint4(oxk[0], oxk[1], oxk[2], oxk[3]);
-    *reinterpret_cast<uint4 *>(sm + OFF_XV + off) = make_uint4(oxv[0], oxv[1], oxv[2], oxv[3]);
-    *reinterpret_cast<uint4 *>(hom + HO_QD + off) = make_uint4(oqe[0], oqe[1], oqe[2], oqe[3]);
-    *reinterpret_cast<uint4 *>(sm + OFF_KBS + off) = make_uint4(okb[0], okb[1], okb[2], okb[3]);
-    *reinterpret_cast<uint4 *>(sm + OFF_KI + ki_index(blk, blk) * 2048 + sw64(t & 15, d0)) =
-        make_uint4(oki[0][0], oki[0][1], oki[0][2], oki[0][3]);
-  }
-  __syncthreads();
-
-  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors): the 136
-  // pairs s <= t of each block, each summed over d by four adjacent lanes (16 channels each);
-  // the pair's lane for channels 0-15 also zeroes the mirror entry above the diagonal
+  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors, from the raw
+  // q / k tiles, so before the operand build reuses them): the 136 pairs s <= t of each block,
+  // each summed over d by four adjacent lanes (16 channels each); the pair's lane for channels
+  // 0-15 also zeroes the mirror entry above the diagonal
   if (big) {
     for (int item = tid; item < 4 * 136 * 4; item += NT1) {
       const int qd = item & 3, pr = item >> 2, i = pr / 136, pi = pr - i * 136;
@@ -344,9 +252,9 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       float mk = 0.f, mq = 0.f;
 #pragma unroll 4
       for (int d = 16 * qd; d < 16 * qd + 16; d += 2) {
-        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(t, d)));
-        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_QS + sw64(t, d)));
-        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + OFF_KS + sw64(s, d)));
+        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(t, d)));
+        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_QS + sw64(t, d)));
+        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(s, d)));
         const float2 gt = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
         const float2 gs = *reinterpret_cast<const float2 *>(GS + gsw(s, d));
         const float e0 = __expf(gt.x - gs.x), e1 = __expf(gt.y - gs.y);
@@ -359,38 +267,108 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
       mq += __shfl_xor_sync(0xffffffffu, mq, 2);
       if (qd == 0) {
         AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
-        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
+        *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
         *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(mq);
       } else if (qd == 1 && sl < tl) {  // the mirror (sl, tl) above the diagonal
         AD[i * 256 + sl * 16 + tl] = 0.f;
-        *reinterpret_cast<__nv_bfloat16 *>(sm + OFF_MK + sw64(s, t)) = __float2bfloat16_rn(0.f);
+        *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(s, t)) = __float2bfloat16_rn(0.f);
         *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(s, t)) = __float2bfloat16_rn(0.f);
       }
     }
     __syncthreads();
   }
 
-  __syncthreads();  // the raw tiles are consumed: prefetch the next chunk behind the GEMMs
-  if (idx + (int)gridDim.x < nchunks) {
-    issue_loads(idx + gridDim.x);
-    if (tid < C) beta_next = load_beta(idx + gridDim.x);
+  // ---- (1b) operand build: 512 units of (row t, 8 consecutive channels), two per thread; all
+  //      reads first, then (after a barrier) the writes, several of which go over the inputs ----
+  {
+    uint4 okd[2], oqd[2], oxk[2], oqe[2], oxv[2], okb[2], oki[2];
+#pragma unroll
+    for (int w2 = 0; w2 < 2; ++w2) {
+      const int u = tid + NT1 * w2;
+      const int t = u >> 3, ch = u & 7, d0 = ch * 8, blk = t >> 4;
+      const uint32_t off = sw64(t, d0);
+      const uint4 kq = *reinterpret_cast<const uint4 *>(sm + R_KS + off);
+      const uint4 qq = *reinterpret_cast<const uint4 *>(sm + R_QS + off);
+      const uint4 vq = *reinterpret_cast<const uint4 *>(sm + R_VS + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w},
+                     vw[4] = {vq.x, vq.y, vq.z, vq.w};
+      const float bt = bet[t];
+      const float4 ga4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0));
+      const float4 gb4 = *reinterpret_cast<const float4 *>(GS + gsw(t, d0 + 4));
+      const float gam[8] = {ga4.x, ga4.y, ga4.z, ga4.w, gb4.x, gb4.y, gb4.z, gb4.w};
+      uint32_t a_kd[4], a_qd[4], a_xk[4], a_xv[4], a_qe[4], a_kb[4], a_ki[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]), vf = unpack_bf16(vw[e]);
+        const int d = d0 + 2 * e;
+        const float2 rf2 = *reinterpret_cast<const float2 *>(refs + blk * 64 + d);
+        const float2 er2 = *reinterpret_cast<const float2 *>(erb + blk * 64 + d);
+        const float2 eq2 = *reinterpret_cast<const float2 *>(egr + blk * 64 + d);
+        const float rf[2] = {rf2.x, rf2.y}, er[2] = {er2.x, er2.y}, eq[2] = {eq2.x, eq2.y};
+        float F[2], iF[2], eg[2], eb[2];
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float gm = gam[2 * e + x];
+          F[x] = __expf(gm - rf[x]);
+          if (!big) {
+            iF[x] = __fdividef(1.f, F[x]);
+            eg[x] = F[x] * er[x];
+            eb[x] = iF[x] * eq[x];
+          } else {
+            iF[x] = __expf(gend[blk * 64 + d + x] - gm);  // B_s = e^{gamma(end of block) - gamma_s}
+            eg[x] = __expf(gm);
+            eb[x] = __expf(gCv[d + x] - gm);
+          }
+        }
+        a_kd[e] = pack_bf16(kf.x * F[0], kf.y * F[1]);
+        a_qd[e] = pack_bf16(qf.x * F[0], qf.y * F[1]);
+        a_xk[e] = pack_bf16(bt * kf.x * eg[0], bt * kf.y * eg[1]);
+        a_qe[e] = pack_bf16(qf.x * eg[0], qf.y * eg[1]);
+        a_xv[e] = pack_bf16(bt * vf.x, bt * vf.y);
+        a_kb[e] = pack_bf16(kf.x * eb[0], kf.y * eb[1]);
+        // Kinc of the diagonal block only: k / F (the GEMMs rescale it per block pair), or k B_s
+        a_ki[e] = pack_bf16(kf.x * iF[0], kf.y * iF[1]);
+      }
+      okd[w2] = make_uint4(a_kd[0], a_kd[1], a_kd[2], a_kd[3]);
+      oqd[w2] = make_uint4(a_qd[0], a_qd[1], a_qd[2], a_qd[3]);
+      oxk[w2] = make_uint4(a_xk[0], a_xk[1], a_xk[2], a_xk[3]);
+      oqe[w2] = make_uint4(a_qe[0], a_qe[1], a_qe[2], a_qe[3]);
+      oxv[w2] = make_uint4(a_xv[0], a_xv[1], a_xv[2], a_xv[3]);
+      okb[w2] = make_uint4(a_kb[0], a_kb[1], a_kb[2], a_kb[3]);
+      oki[w2] = make_uint4(a_ki[0], a_ki[1], a_ki[2], a_ki[3]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int w2 = 0; w2 < 2; ++w2) {
+      const int u = tid + NT1 * w2;
+      const int t = u >> 3, d0 = (u & 7) * 8, blk = t >> 4;
+      const uint32_t off = sw64(t, d0);
+      *reinterpret_cast<uint4 *>(sm + R_KS + off) = okd[w2];
+      *reinterpret_cast<uint4 *>(sm + R_QS + off) = oqd[w2];
+      *reinterpret_cast<uint4 *>(sm + R_XK + off) = oxk[w2];
+      *reinterpret_cast<uint4 *>(sm + R_VS + off) = oxv[w2];
+      *reinterpret_cast<uint4 *>(hom + HO_QD + off) = oqe[w2];
+      *reinterpret_cast<uint4 *>(sm + R_KB + off) = okb[w2];
+      *reinterpret_cast<uint4 *>(sm + R_KI + blk * 2048 + sw64(t & 15, d0)) = oki[w2];
+    }
   }
+  __syncthreads();
 
   // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T per (block row i, block column j <= i), and
-  //      (3) T_ii = (I + A_ii)^{-1}.  Warps 0-3 take the diagonal M block i = warp and invert
-  //      it right away (one column per lane, fp32 substitution); warps 4-15 take the 10 P
-  //      blocks and the 6 off-diagonal M blocks. ----
+  //      (3) T_ii = (I + A_ii)^{-1}.  Warps 0-3 take the diagonal M block i = warp and invert it
+  //      right away (one column per lane, fp32 substitution), then one of the 16 other blocks
+  //      each; warps 4-7 take three each ----
   auto mp_block = [&](int mat, int i, int j) {
     float acc[2][4] = {};
     // only the diagonal Kinc tiles exist (k / F, or k B for a big chunk); the block pair's
     // factor (e^{r_i - r_j}, or G_ij) scales the A operand along d
     const bool scale = j < i;
-    const uint32_t kib = s_base + OFF_KI + ki_index(scale ? j : i, j) * 2048;
+    const uint32_t kib = s_base + R_KI + j * 2048;
     const float *G = gij + (i * 4 + j) * 64;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t af[4], bf[4];
-      ldsm_x4(a_frag_addr(s_base + (mat ? OFF_QD : OFF_KD), 16 * i, 16 * kk, lane), af);
+      ldsm_x4(a_frag_addr(s_base + (mat ? R_QS : R_KS), 16 * i, 16 * kk, lane), af);
       if (scale) {
 #pragma unroll
         for (int x = 0; x < 4; ++x) {
@@ -413,13 +391,13 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
         if (mat == 0) {
           v0 = s < t ? v0 : 0.f;
           v1 = s + 1 < t ? v1 : 0.f;
-          *reinterpret_cast<uint32_t *>(sm + OFF_MK + sw64(t, s)) = pack_bf16(v0, v1);
+          *reinterpret_cast<uint32_t *>(sm + R_MK + sw64(t, s)) = pack_bf16(v0, v1);
           v0 *= bet[t];
           v1 *= bet[t];
           if (j == i) {
             *reinterpret_cast<float2 *>(AD + i * 256 + tl * 16 + sl) = make_float2(v0, v1);
           } else {
-            *reinterpret_cast<uint32_t *>(sm + OFF_AB + sw64(t, s)) = pack_bf16(v0, v1);
+            *reinterpret_cast<uint32_t *>(sm + R_AB + sw64(t, s)) = pack_bf16(v0, v1);
           }
         } else {
           v0 = s <= t ? v0 : 0.f;
@@ -427,6 +405,14 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
           *reinterpret_cast<uint32_t *>(hom + HO_P + sw64(t, s)) = pack_bf16(v0, v1);
         }
       }
+  };
+  // task q < 10: P block number q of the 10 pairs (i, j <= i); else off-diagonal M block q - 10
+  auto mp_task = [&](int q) {
+    const int pr = q < 10 ? q : (q == 10 ? 1 : q == 11 ? 3 : q == 12 ? 4 : q - 7);
+    const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
+    const int j = pr - i * (i + 1) / 2;
+    if (big && j == i && q < 10) return;  // diagonal block already computed exactly
+    mp_block(q < 10 ? 1 : 0, i, j);
   };
   if (warp < 4) {
     const int i = warp;
@@ -443,43 +429,34 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
         for (int s2 = 0; s2 < t; ++s2) v = fmaf(-A[t * 16 + s2], x[s2], v);
         x[t] = v;
       }
-      __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + OFF_TI + i * 512);
+      __nv_bfloat16 *Ti = reinterpret_cast<__nv_bfloat16 *>(sm + R_TI + i * 512);
 #pragma unroll
       for (int t = 0; t < 16; ++t) Ti[t * 16 + u] = __float2bfloat16_rn(x[t]);
     }
+    mp_task(12 + warp);
   } else {
-    for (int q = warp - 4; q < 16; q += 12) {
-      // q < 10: P block number q of the 10 pairs (i, j <= i); else off-diagonal M block q - 10
-      const int pr = q < 10 ? q : (q == 10 ? 1 : q == 11 ? 3 : q == 12 ? 4 : q - 7);
-      const int i = pr < 1 ? 0 : pr < 3 ? 1 : pr < 6 ? 2 : 3;
-      const int j = pr - i * (i + 1) / 2;
-      const int mat = q < 10 ? 1 : 0;
-      if (big && j == i) continue;  // diagonal block already computed exactly
-      mp_block(mat, i, j);
-    }
+    for (int q = warp - 4; q < 12; q += 4) mp_task(q);
   }
   __syncthreads();
 
-  // ---- (4) Tinv = (I+A)^{-1}: block forward substitution on the identity, 8 columns per warp
-  //      (warps 0-7; the rows above a column's diagonal block are zero and skipped) ----
-  if (warp < 8) solve_columns(sm, s_base, OFF_TF - OFF_OUT, -1, warp * 8, warp >> 1, -1.f, 1.f, warp, lane);
+  // ---- (4) Tinv = (I+A)^{-1} (into the Kdec tile): block forward substitution on the identity,
+  //      8 columns per warp (the rows above a column's diagonal block are zero and skipped) ----
+  solve_columns(sm, s_base, warp * 8, warp >> 1, warp, lane);
   __syncthreads();
   // ---- (5) W = Tinv beta Kd (stored negated) and U = Tinv beta V as one block-triangular GEMM;
-  //      warp w takes 16 of the 128 columns of [W | U] for the row blocks {0, 3} or {1, 2}, so
-  //      every warp does 5 of the 10 nonzero blocks of a column ----
+  //      warp w takes 16 of the 128 columns of [W | U] for all four row blocks ----
   {
-    const int cg = warp & 7, c0 = 16 * (cg & 3);
-    const bool isW = cg < 4;
-    const uint32_t xb = s_base + (isW ? OFF_XK : OFF_XV);
+    const int c0 = 16 * (warp & 3);
+    const bool isW = warp < 4;
+    const uint32_t xb = s_base + (isW ? R_XK : R_VS);
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int i = half == 0 ? (warp >> 3) : 3 - (warp >> 3);
+    for (int i = 0; i < 4; ++i) {
       float acc[2][4] = {};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         if (k > i) break;
         uint32_t af[4], bf[4];
-        ldsm_x4(a_frag_addr(s_base + OFF_TF, 16 * i, 16 * k, lane), af);
+        ldsm_x4(a_frag_addr(s_base + R_KS, 16 * i, 16 * k, lane), af);
         ldsm_x4_t(bkn_frag_addr(xb, 16 * k, c0, lane), bf);
         mma16816(acc[0], af, bf[0], bf[1]);
         mma16816(acc[1], af, bf[2], bf[3]);
@@ -494,19 +471,20 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
               pack_bf16(so * acc[nt][2 * hh], so * acc[nt][2 * hh + 1]);
     }
   }
-
   __syncthreads();
-  // ---- (6) the state-independent products the scan and the backward need, each warp 16 rows x
-  //      64 columns of one of
-  //        [Mneg | N]       = Kb^T [-W | U]          (warps 0-7, rows d)
-  //        [Qt | O_intra]   = [Qd | 0] + P [-W | U]  (warps 8-15, rows t; P is lower triangular)
+  // ---- (6) the state-independent products the scan and the backward need, 16 tasks of 16 rows
+  //      x 64 columns, two per warp:
+  //        [Mneg | N]       = Kb^T [-W | U]          (tasks 0-7, rows d)
+  //        [Qt | O_intra]   = [Qd | 0] + P [-W | U]  (tasks 8-15, rows t; P is lower triangular)
   //      so that the scan advances S^T <- diag(e^{gamma_C}) S^T + Mneg S^T + N with one MMA per
   //      chunk and forms O = Qt S^T + O_intra and Unew = U - W S^T beside it ----
-  {
-    const int rb = (warp >> 1) & 3, jb = rb * 16, nh = warp & 1;
+#pragma unroll 1
+  for (int r = 0; r < 2; ++r) {
+    const int q = warp + 8 * r;
+    const int rb = (q >> 1) & 3, jb = rb * 16, nh = q & 1;
     const uint32_t bsrc = ho + (nh ? HO_U : HO_W);
     float X[8][4];
-    if (warp >= 8 && nh == 0) {  // Qt starts from Qd
+    if (q >= 8 && nh == 0) {  // Qt starts from Qd
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -524,12 +502,12 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     }
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      if (warp >= 8 && kk > rb) break;
+      if (q >= 8 && kk > rb) break;
       uint32_t af[4];
-      if (warp < 8)
-        ldsm_x4_t(ct_frag_addr(s_base + OFF_KBS, 16 * kk, jb, lane), af);  // Kb^T rows d, k = t
+      if (q < 8)
+        ldsm_x4_t(ct_frag_addr(s_base + R_KB, 16 * kk, jb, lane), af);  // Kb^T rows d, k = t
       else
-        ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);            // P rows t, k = s
+        ldsm_x4(a_frag_addr(ho + HO_P, jb, 16 * kk, lane), af);          // P rows t, k = s
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t bf[4];
@@ -538,8 +516,8 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
         mma16816(X[2 * np + 1], af, bf[2], bf[3]);
       }
     }
-    // staged in tiles that are free by now: Mneg -> beta-Kd, Qt -> beta-V, N -> Kdec, O_intra -> Qdec
-    uint8_t *dst = sm + (warp < 8 ? (nh ? OFF_KD : OFF_XK) : (nh ? OFF_QD : OFF_XV));
+    // staged in tiles that are free by now: Mneg -> beta-Kd, N -> Qdec, Qt -> beta-V, O_intra -> A
+    uint8_t *dst = sm + (q < 8 ? (nh ? R_QS : R_XK) : (nh ? R_AB : R_VS));
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -555,24 +533,24 @@ __global__ void __launch_bounds__(NT1, 1) kda_fwd_chunks_kernel(Params p, const 
     uint8_t *wr = (uint8_t *)p.ws + (int64_t)idx * WS_SIZE;
     const uint64_t keep = l2_policy_keep(), stream = l2_policy_stream();
     bulk_s2g_hint(wr + WS_W, ho + HO_W, 2 * 8192, keep);          // -W | U
-    bulk_s2g_hint(wr + WS_OI, s_base + OFF_QD, 8192, keep);       // O_intra
-    bulk_s2g_hint(wr + WS_N, s_base + OFF_KD, 8192, keep);        // N
+    bulk_s2g_hint(wr + WS_OI, s_base + R_AB, 8192, keep);         // O_intra
+    bulk_s2g_hint(wr + WS_N, s_base + R_QS, 8192, keep);          // N
     if (p.saved) {  // Mneg, Qt and e^{gamma_C} live in the saved record, where the scan reads them
       uint8_t *sv = (uint8_t *)p.saved + (int64_t)idx * kSavedChunk;
-      bulk_s2g_hint(sv + kSavedM, s_base + OFF_XK, 8192, keep);
-      bulk_s2g_hint(sv + kSavedQt, s_base + OFF_XV, 8192, keep);
+      bulk_s2g_hint(sv + kSavedM, s_base + R_XK, 8192, keep);
+      bulk_s2g_hint(sv + kSavedQt, s_base + R_VS, 8192, keep);
       bulk_s2g_hint(sv + kSavedEG, ho + HO_EG, 256, keep);
       bulk_s2g_hint(sv + kSavedP, ho + HO_P, 8192, stream);
-      bulk_s2g_hint(sv + kSavedMkk, s_base + OFF_MK, 2 * 8192, stream);  // M | Tinv
+      bulk_s2g_hint(sv + kSavedMkk, s_base + R_MK, 8192, stream);   // M
+      bulk_s2g_hint(sv + kSavedTinv, s_base + R_KS, 8192, stream);  // Tinv
     } else {
-      bulk_s2g_hint(wr + WS_MN, s_base + OFF_XK, 8192, keep);
-      bulk_s2g_hint(wr + WS_QT, s_base + OFF_XV, 8192, keep);
+      bulk_s2g_hint(wr + WS_MN, s_base + R_XK, 8192, keep);
+      bulk_s2g_hint(wr + WS_QT, s_base + R_VS, 8192, keep);
       bulk_s2g_hint(wr + WS_EG, ho + HO_EG, 256, keep);
     }
     bulk_commit();
+    bulk_wait_read_all();  // shared memory stays valid until the stores have read it
   }
-  }  // chunk loop
-  if (tid == 0) bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -916,11 +894,8 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
 template <typename Tb>
 int launch(const Params &p, cudaStream_t st) {
   auto k1 = kda_fwd_chunks_kernel<Tb>;
-  const int smem1 = p.gated ? SMEM1_GP + gate_smem_bytes(p.gated, p.H) : SMEM1;
-  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1)) return KDA_ERR_CUDA;
-  int dev = 0, nsm = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+  if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1) ||
+      cudaFuncSetAttribute(k1, cudaFuncAttributePreferredSharedMemoryCarveout, 100))
     return KDA_ERR_CUDA;
   const int nchunks = p.B * p.H * p.nc;
   TmaMaps tm;
@@ -928,7 +903,7 @@ int launch(const Params &p, cudaStream_t st) {
   const Str in_str[4] = {p.sq, p.sk, p.sv, p.sg};
   for (int i = 0; i < 4; ++i)
     if (int e = tma_map_bthd(&tm.m[i], srcs[i], p.B, p.T, p.H, D, i == 3 && !p.gated, &in_str[i])) return e;
-  k1<<<nchunks < nsm ? nchunks : nsm, NT1, smem1, st>>>(p, tm);
+  k1<<<nchunks, NT1, SMEM1, st>>>(p, tm);
   count_launch();
   if (cudaFuncSetAttribute(kda_fwd_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2))
     return KDA_ERR_CUDA;
