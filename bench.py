@@ -616,7 +616,8 @@ def kernel_only(args):
                 _, st, _ = kda_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], st, CHUNK)
         torch.cuda.synchronize()
         return 0
-    inp = make_inputs_torch(B, T, H, D, seed=1234, device=dev, dtype=torch.bfloat16, state_std=0.1)
+    Bk = 2 if args.small else B  # --small: a case for multi-pass ncu captures (~100 MB resident)
+    inp = make_inputs_torch(Bk, T, H, D, seed=1234, device=dev, dtype=torch.bfloat16, state_std=0.1)
     q, k, v, g, beta, S0, do, dst = (inp[n] for n in ("q", "k", "v", "g", "beta", "state", "do", "dst"))
     _, _, cs = kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=True)
     for _ in range(args.warmup + args.steps):
@@ -717,6 +718,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-cfg3", action="store_true", help="leave out the nested config-3 leg")
+    ap.add_argument("--small", action="store_true", help="with --kernel-only: B = 2 instead of 8")
     ap.add_argument("--workload", choices=("cfg2", "cfg3"), default="cfg2",
                     help="cfg2: the KDA op (the headline line); cfg3: full-model DP training step")
     ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both", "stream"), default=None,
