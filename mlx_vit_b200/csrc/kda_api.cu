@@ -11,6 +11,7 @@ int generic_fwd(const Params &p, int dq, int db, cudaStream_t st);
 int generic_bwd(const Params &p, int dq, int db, cudaStream_t st);
 int generic_fwd_split(int D, int C);
 size_t generic_bwd_smem(int D, int C);
+int generic_chunk(int D, int C);
 bool tc_supported(const KdaDesc *d, int backward);
 size_t tc_workspace_bytes(const KdaDesc *d, int backward);
 size_t tc_saved_bytes(const KdaDesc *d);
@@ -78,7 +79,7 @@ const char *kda_strerror(int s) {
   switch (s) {
     case KDA_OK: return "ok";
     case KDA_ERR_INVALID_ARG: return "invalid argument (null pointer, non-positive size or bad descriptor)";
-    case KDA_ERR_UNSUPPORTED: return "unsupported shape: needs Dk == Dv, chunk <= 64, D <= 128 (forward) / D <= 64 (backward)";
+    case KDA_ERR_UNSUPPORTED: return "unsupported shape: needs Dk == Dv, chunk <= 64, D <= 128";
     case KDA_ERR_DTYPE: return "unsupported dtype code";
     case KDA_ERR_MISALIGNED: return "pointer not 16-byte aligned";
     case KDA_ERR_WORKSPACE: return "workspace missing or too small (see kda_workspace_bytes)";
@@ -93,8 +94,7 @@ int kda_check_desc(const KdaDesc *d, int backward) {
   int s = check_desc_shape(d);
   if (s) return s;
   if (use_tc(d, backward) || use_tc128(d, backward)) return KDA_OK;
-  if (!backward) return kda::generic_fwd_split((int)d->Dk, (int)d->chunk) ? KDA_OK : KDA_ERR_UNSUPPORTED;
-  return kda::generic_bwd_smem((int)d->Dk, (int)d->chunk) <= 227 * 1024 ? KDA_OK : KDA_ERR_UNSUPPORTED;
+  return kda::generic_chunk((int)d->Dk, (int)d->chunk) ? KDA_OK : KDA_ERR_UNSUPPORTED;
 }
 
 size_t kda_workspace_bytes(const KdaDesc *d, int backward) {
@@ -108,7 +108,8 @@ size_t kda_workspace_bytes(const KdaDesc *d, int backward) {
 size_t kda_saved_bytes(const KdaDesc *d) {
   if (kda_check_desc(d, 0)) return 0;
   if (use_tc(d, 1)) return kda::tc_saved_bytes(d);
-  const int64_t nc = (d->T + d->chunk - 1) / d->chunk;
+  const int64_t gc = kda::generic_chunk((int)d->Dk, (int)d->chunk);
+  const int64_t nc = (d->T + gc - 1) / gc;
   return (size_t)(d->B * d->H * nc * d->Dk * d->Dv) * sizeof(float);
 }
 
@@ -161,6 +162,8 @@ int kda_fwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
     return KDA_ERR_MISALIGNED;
   if (tc) return kda::tc_fwd(p, d->dtype_beta, st);
   if (tc128) return kda::tc128_fwd(p, d->dtype_beta, st);
+  p.C = kda::generic_chunk(p.D, p.C);  // the fp32 kernels' chunk (see generic_chunk)
+  p.nc = (p.T + p.C - 1) / p.C;
   return kda::generic_fwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 
@@ -190,6 +193,8 @@ int kda_bwd(const KdaDesc *d, const void *q, const void *k, const void *v, const
       return KDA_ERR_MISALIGNED;
     return kda::tc_bwd(p, d->dtype_beta, st);
   }
+  p.C = kda::generic_chunk(p.D, p.C);
+  p.nc = (p.T + p.C - 1) / p.C;
   return kda::generic_bwd(p, d->dtype_qkv, d->dtype_beta, st);
 }
 

@@ -358,6 +358,17 @@ size_t generic_bwd_smem(int D, int C) {
 }
 static constexpr size_t kMaxSmem = 227 * 1024;
 
+// The chunk the fp32 kernels run at: the caller's chunk C, or the largest smaller one whose
+// backward working set fits shared memory, halving C (D = 96 runs at 32, D = 128 at 16).  The chunkwise
+// algebra gives the recurrence's values at any chunk size, so this changes only rounding; the
+// forward and the backward of one descriptor use the same chunk, so the saved per-chunk states
+// line up.  0 if none fits.
+int generic_fwd_split(int D, int C);
+int generic_chunk(int D, int C) {
+  for (int c = C; c >= 1; c /= 2)
+    if (generic_bwd_smem(D, c) <= kMaxSmem && generic_fwd_split(D, c)) return c;
+  return 0;
+}
 int generic_fwd_split(int D, int C) {
   for (int dvs = D; dvs >= 1; --dvs) {
     if (D % dvs) continue;

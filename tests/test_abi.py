@@ -66,10 +66,16 @@ def test_negative_stride_rejected():
     assert L.kda_check_desc(ctypes.byref(d), 0) == 0
 
 
-def test_backward_head_dim_limit():
+def test_backward_head_dims_up_to_128():
+    """Gradients exist for every head dim the forward takes (the fp32 kernels run D = 96 and
+    D = 128 at a smaller internal chunk); beyond D = 128 both directions are refused."""
     L = _lib.lib()
-    d = desc(Dk=128, Dv=128, flags=_lib.KDA_FLAG_FORCE_GENERIC)
-    assert L.kda_check_desc(ctypes.byref(d), 0) == 0
+    for D in (96, 128):
+        d = desc(Dk=D, Dv=D, flags=_lib.KDA_FLAG_FORCE_GENERIC)
+        assert L.kda_check_desc(ctypes.byref(d), 0) == 0
+        assert L.kda_check_desc(ctypes.byref(d), 1) == 0
+        assert L.kda_saved_bytes(ctypes.byref(d)) > 0
+    d = desc(Dk=256, Dv=256)
     assert L.kda_check_desc(ctypes.byref(d), 1) == -2
 
 

@@ -208,3 +208,17 @@ def test_block_gap_beyond_fp32_range(cuda, D):
         keys = ("o", "S_T")
     for k in keys:
         assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))
+
+
+@pytest.mark.parametrize("D", [96, 128])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_wide_heads_fwd_bwd(cuda, D, dtype):
+    """Training at head dims 96 (the SSv2 trainer's) and 128 (config 4's): forward + VJP against
+    the oracle, ragged T, nonzero initial state (the fp32 kernels at a smaller internal chunk)."""
+    inp = make_inputs(2, 100, 2, D, seed=D, state_std=0.1)
+    ref_in = inp if dtype == torch.float32 else rounded_inputs(inp, dtype)
+    ref = O.fwd_bwd(ref_in, dtype=np.float64)
+    got = run_fwd_bwd(to_dev(inp, cuda, dtype), 64)
+    tol = TOL_FP32 if dtype == torch.float32 else TOL_BF16
+    for k in OUT_KEYS:
+        assert rel_err(got[k], ref[k]) <= tol, (k, rel_err(got[k], ref[k]))
