@@ -616,10 +616,47 @@ def kernel_only(args):
                 _, st, _ = kda_forward(x["q"], x["k"], x["v"], x["g"], x["beta"], st, CHUNK)
         torch.cuda.synchronize()
         return 0
+    if args.kernel_only == "recurrent":  # token-by-token decode: cfg4's heads, 64 tokens per call
+        x = make_inputs_torch(1, 64, 16, 128, seed=77, device=dev, dtype=torch.bfloat16)
+        from mlx_vit_b200 import kda_recurrent
+        st = x["state"]
+        for _ in range(args.warmup + args.steps):
+            _, st = kda_recurrent(x["q"], x["k"], x["v"], x["g"], x["beta"], st)
+        torch.cuda.synchronize()
+        return 0
+    if args.kernel_only == "rowops":  # the layer's fused row ops at cfg2/cfg3 size (B8 T1568 H12 D64)
+        from mlx_vit_b200.rowops import conv_silu, gated_rmsnorm
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        xr = torch.randn(B, T, H * D, generator=gen, device=dev).to(torch.bfloat16).requires_grad_(True)
+        w = torch.randn(H * D, 1, 4, generator=gen, device=dev).requires_grad_(True)
+        bias = torch.zeros(H * D, device=dev, requires_grad=True)
+        o = torch.randn(B, T, H, D, generator=gen, device=dev).to(torch.bfloat16).requires_grad_(True)
+        gt = torch.randn_like(o).requires_grad_(True)
+        rw = torch.ones(D, device=dev, requires_grad=True)
+        for _ in range(args.warmup + args.steps):
+            y = conv_silu(xr, w, bias, H, D, True, D ** -0.5)
+            z = gated_rmsnorm(o, gt, rw)
+            torch.autograd.backward([y, z], [torch.ones_like(y), torch.ones_like(z)])
+        torch.cuda.synchronize()
+        return 0
     Bk = 2 if args.small else B  # --small: a case for multi-pass ncu captures (~100 MB resident)
     inp = make_inputs_torch(Bk, T, H, D, seed=1234, device=dev, dtype=torch.bfloat16, state_std=0.1)
     q, k, v, g, beta, S0, do, dst = (inp[n] for n in ("q", "k", "v", "g", "beta", "state", "do", "dst"))
     _, _, cs = kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=True)
+    if args.kernel_only == "gated":  # the fused-gate calls, reference gate init (A in [1, 16])
+        from mlx_vit_b200.kda import kda_forward_gated, kda_backward_gated
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(99)
+        f = torch.randn(Bk, T, H, D, generator=gen, device=dev).to(torch.bfloat16)
+        bl = torch.randn(Bk, T, H, generator=gen, device=dev).to(torch.bfloat16)
+        A_log = torch.log(torch.rand(H, generator=gen, device=dev) * 15 + 1)
+        dtb = torch.zeros(H * D, device=dev)
+        for _ in range(args.warmup + args.steps):
+            _, _, sg = kda_forward_gated(q, k, v, f, A_log, dtb, bl, S0, CHUNK, save_states=True)
+            kda_backward_gated(q, k, v, f, A_log, dtb, bl, S0, sg, do, dst, CHUNK)
+        torch.cuda.synchronize()
+        return 0
     for _ in range(args.warmup + args.steps):
         if args.kernel_only in ("fwd", "both"):
             kda_forward(q, k, v, g, beta, S0, CHUNK, save_states=args.kernel_only == "both")
@@ -721,7 +758,8 @@ def main():
     ap.add_argument("--small", action="store_true", help="with --kernel-only: B = 2 instead of 8")
     ap.add_argument("--workload", choices=("cfg2", "cfg3"), default="cfg2",
                     help="cfg2: the KDA op (the headline line); cfg3: full-model DP training step")
-    ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both", "stream"), default=None,
+    ap.add_argument("--kernel-only", choices=("fwd", "bwd", "both", "stream", "gated", "recurrent", "rowops"),
+                    default=None,
                     help="profiling driver: run only the kda_fwd/kda_bwd launches (steps+warmup "
                          "times), no timing, no e2e, no JSON line")
     args = ap.parse_args()

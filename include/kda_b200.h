@@ -172,7 +172,7 @@ KDA_API int kda_gated_rmsnorm_fwd(int64_t rows, int D, const void *o, const void
                                   void *y, float eps, void *stream);
 /* The layer's short causal depthwise convolution (kernel 4) with SiLU, and for q / k the L2 norm
  * over each token's whole H*D channel row and the scale (norm != 0), in one pass: x, y [B, T, H*D]
- * bf16 (H*D a multiple of 8, at most 8192), w [H*D][4] and bias [H*D] float32.  The VJP writes dx
+ * bf16 (H*D a multiple of 8, at most 2048), w [H*D][4] and bias [H*D] float32.  The VJP writes dx
  * (bf16) and dw, db (float32, overwritten) and needs a float32 [B, T, H*D] scratch.
  * Replaces: ShortCausalConv1d (nope_gdn_mlx.py:400-431) applied at :793-795 and followed by the
  * SiLU / L2 norm of :797-799. */

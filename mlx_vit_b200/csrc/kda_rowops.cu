@@ -249,125 +249,193 @@ __global__ void __launch_bounds__(32 * kWarps) gated_rmsnorm_bwd_kernel(int64_t 
 // Short causal depthwise convolution (kernel 4, the reference's ShortCausalConv1d,
 // nope_gdn_mlx.py:400-431: z[t, c] = b[c] + sum_j w[c, j] x[t - 3 + j, c], zeros before t = 0)
 // followed by SiLU, and for q / k by the L2 norm over the whole C = H D channel row (the
-// reference normalises before its head reshape, :797-799 then :818-821) and the scale: one CTA
-// per (b, t) row, the four input rows it reads come through L1.  x, y: [B, T, C] bf16;
-// w [C][4], b [C] fp32.
-template <int KC>
-__device__ __forceinline__ void conv_row(int64_t r, int t, int C, const __nv_bfloat16 *x, const float *w,
-                                         const float *bias, float (&z)[KC][8]) {
-  const int nch = C >> 3;
+// reference normalises before its head reshape, :797-799 then :818-821) and the scale.  x, y:
+// [B, T, C] bf16 (C at most kConvMaxC); w [C][4], b [C] fp32.  A CTA walks kConvRows consecutive
+// rows of one sequence with one thread per 4 channels (blockDim = C / 4 rounded up to a warp):
+// the thread keeps its weights and the last three input rows in registers (a sliding window, so
+// every input row is read once) and the rows go kConvG at a time through one block reduction of
+// their norms.
+constexpr int kConvRows = 16, kConvG = 4, kConvV = 4;  // rows per CTA, per reduction; channels per thread
+constexpr int kConvMaxC = 2048;                         // 512 threads of 4 channels
+
+__device__ __forceinline__ void load4(const __nv_bfloat16 *p, float (&x)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2 *>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+  x[0] = a.x; x[1] = a.y; x[2] = b.x; x[3] = b.y;
+}
+__device__ __forceinline__ void store4(__nv_bfloat16 *p, const float (&x)[4]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+  *reinterpret_cast<uint2 *>(p) = make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&b));
+}
+
+// sums of G per-row partials over the CTA (nw warps, at most 16); red holds two slots per warp
+template <int G>
+__device__ __forceinline__ void block_sums(const float (&v)[G], float (&out)[G], float (*red)[16][G], int parity,
+                                           int nw) {
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
 #pragma unroll
-  for (int k = 0; k < KC; ++k) {
-    const int c = threadIdx.x + kRowThreads * k;
-    if (c >= nch) continue;
-    const int c0 = 8 * c;
-    const float4 b0 = *reinterpret_cast<const float4 *>(bias + c0);
-    const float4 b1 = *reinterpret_cast<const float4 *>(bias + c0 + 4);
-    z[k][0] = b0.x; z[k][1] = b0.y; z[k][2] = b0.z; z[k][3] = b0.w;
-    z[k][4] = b1.x; z[k][5] = b1.y; z[k][6] = b1.z; z[k][7] = b1.w;
-    float wt[8][4];
+  for (int g = 0; g < G; ++g) {
+    const float x = warp_sum(v[g]);
+    if (lane == 0) red[parity][wp][g] = x;
+  }
+  __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 q = *reinterpret_cast<const float4 *>(w + (c0 + i) * 4);
-      wt[i][0] = q.x; wt[i][1] = q.y; wt[i][2] = q.z; wt[i][3] = q.w;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (t - 3 + j < 0) continue;
-      float xv[8];
-      load8(x + (r - 3 + j) * C + c0, xv);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) z[k][i] = fmaf(wt[i][j], xv[i], z[k][i]);
-    }
+  for (int g = 0; g < G; ++g) {
+    float s = 0.f;
+    for (int i = 0; i < nw; ++i) s += red[parity][i][g];
+    out[g] = s;
   }
 }
 
-template <int KC, bool NORM>
-__global__ void __launch_bounds__(kRowThreads) conv_silu_fwd_kernel(int64_t rows, int T, int C, const __nv_bfloat16 *x,
-                                                                    const float *w, const float *bias,
-                                                                    __nv_bfloat16 *y, float scale) {
-  __shared__ float2 red[2][kRowThreads / 32];
-  const int nch = C >> 3;
-  int parity = 0;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
-    const int t = (int)(r % T);
-    float z[KC][8];
-    conv_row<KC>(r, t, C, x, w, bias, z);
-    float ss = 0.f;
+struct ConvThread {  // one thread's channels: weights, bias and the input window
+  float w[kConvV][4], bias[kConvV], win[3][kConvV];
+  __device__ __forceinline__ void init(int b, int t0, int T, int C, int c0, const __nv_bfloat16 *x,
+                                       const float *wg, const float *bg) {
 #pragma unroll
-    for (int k = 0; k < KC; ++k)
-      if (threadIdx.x + kRowThreads * k < nch)
+    for (int i = 0; i < kConvV; ++i) {
+      const float4 q = *reinterpret_cast<const float4 *>(wg + (c0 + i) * 4);
+      w[i][0] = q.x; w[i][1] = q.y; w[i][2] = q.z; w[i][3] = q.w;
+      bias[i] = bg[c0 + i];
+    }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          z[k][i] *= sigm(z[k][i]);
-          ss += z[k][i] * z[k][i];
-        }
-    float inv = 1.f;
-    if (NORM) inv = scale / fmaxf(sqrtf(block_sum2(make_float2(ss, 0.f), red, parity).x), 1e-12f);
+    for (int j = 0; j < 3; ++j) {
+      const int t = t0 - 3 + j;
+      if (t >= 0) load4(x + ((int64_t)b * T + t) * C + c0, win[j]);
+      else
 #pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const int c = threadIdx.x + kRowThreads * k;
-      if (c < nch) {
-        if (NORM)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) z[k][i] *= inv;
-        store8(y + r * C + 8 * c, z[k]);
-      }
+        for (int i = 0; i < kConvV; ++i) win[j][i] = 0.f;
     }
   }
-}
+  // z of row t (whose input is xt), then slide the window
+  __device__ __forceinline__ void step(const float (&xt)[kConvV], float (&z)[kConvV]) {
+#pragma unroll
+    for (int i = 0; i < kConvV; ++i) {
+      z[i] = fmaf(w[i][3], xt[i], fmaf(w[i][2], win[2][i], fmaf(w[i][1], win[1][i], fmaf(w[i][0], win[0][i], bias[i]))));
+      win[0][i] = win[1][i];
+      win[1][i] = win[2][i];
+      win[2][i] = xt[i];
+    }
+  }
+};
 
-// backward, part 1: per (b, t) row, dz = d/dz of silu (and the row-wide L2 norm) at z = conv(x),
-// into fp32 dz
-template <int KC, bool NORM>
-__global__ void __launch_bounds__(kRowThreads) conv_silu_bwd_rows_kernel(int64_t rows, int T, int C,
-                                                                         const __nv_bfloat16 *x, const float *w,
-                                                                         const float *bias, const __nv_bfloat16 *dy,
-                                                                         float *dz, float scale) {
-  __shared__ float2 red[2][kRowThreads / 32];
-  const int nch = C >> 3;
+template <bool NORM>
+__global__ void __launch_bounds__(512) conv_silu_fwd_kernel(int B, int T, int C, const __nv_bfloat16 *x,
+                                                            const float *w, const float *bias,
+                                                            __nv_bfloat16 *y, float scale) {
+  __shared__ float red[2][16][kConvG];
+  const int nch = C / kConvV, nw = (blockDim.x + 31) >> 5, c = threadIdx.x, c0 = kConvV * c;
+  const bool act = c < nch;
+  const int nseg = (T + kConvRows - 1) / kConvRows;
+  const int b = blockIdx.x / nseg, t0 = (blockIdx.x % nseg) * kConvRows;
+  const int t1 = min(T, t0 + kConvRows);
+  ConvThread th;
+  if (act) th.init(b, t0, T, C, c0, x, w, bias);
   int parity = 0;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
-    const int t = (int)(r % T);
-    float z[KC][8], g[KC][8];
-    conv_row<KC>(r, t, C, x, w, bias, z);
-    float ss = 0.f, sg = 0.f;
+  for (int tg = t0; tg < t1; tg += kConvG, parity ^= 1) {
+    float z[kConvG][kConvV], ss[kConvG];
+    float xt[kConvG][kConvV];
 #pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const int c = threadIdx.x + kRowThreads * k;
-      if (c < nch) {
-        load8(dy + r * C + 8 * c, g[k]);
+    for (int g = 0; g < kConvG; ++g)  // all loads first
+      if (act && tg + g < t1) load4(x + ((int64_t)b * T + tg + g) * C + c0, xt[g]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float s = z[k][i] * sigm(z[k][i]);
-          ss += s * s;
-          sg += s * g[k][i];
+    for (int g = 0; g < kConvG; ++g) {
+      ss[g] = 0.f;
+      if (act && tg + g < t1) {
+        th.step(xt[g], z[g]);
+#pragma unroll
+        for (int i = 0; i < kConvV; ++i) {
+          z[g][i] *= sigm(z[g][i]);
+          ss[g] += z[g][i] * z[g][i];
         }
       }
     }
-    float inv = 1.f, proj = 0.f;
+    float inv[kConvG];
+#pragma unroll
+    for (int g = 0; g < kConvG; ++g) inv[g] = 1.f;
     if (NORM) {
-      const float2 s2 = block_sum2(make_float2(ss, sg), red, parity);
-      const float N = sqrtf(s2.x);
-      const bool clamp = !(N > 1e-12f);
-      inv = scale / (clamp ? 1e-12f : N);
-      proj = clamp ? 0.f : s2.y / s2.x;
+      float tot[kConvG];
+      block_sums<kConvG>(ss, tot, red, parity, nw);
+#pragma unroll
+      for (int g = 0; g < kConvG; ++g) inv[g] = scale / fmaxf(sqrtf(tot[g]), 1e-12f);
     }
 #pragma unroll
-    for (int k = 0; k < KC; ++k) {
-      const int c = threadIdx.x + kRowThreads * k;
-      if (c < nch) {
-        float o[8];
+    for (int g = 0; g < kConvG; ++g)
+      if (act && tg + g < t1) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float sgm = sigm(z[k][i]), s = z[k][i] * sgm;
-          o[i] = inv * (g[k][i] - s * proj) * sgm * (1.f + z[k][i] * (1.f - sgm));
+        for (int i = 0; i < kConvV; ++i) z[g][i] *= inv[g];
+        store4(y + ((int64_t)b * T + tg + g) * C + c0, z[g]);
+      }
+  }
+}
+
+// backward, part 1: per row, dz = d/dz of silu (and the row-wide L2 norm) at z = conv(x), into
+// fp32 dz; the same walk as the forward
+template <bool NORM>
+__global__ void __launch_bounds__(512) conv_silu_bwd_rows_kernel(int B, int T, int C, const __nv_bfloat16 *x,
+                                                                 const float *w, const float *bias,
+                                                                 const __nv_bfloat16 *dy, float *dz, float scale) {
+  __shared__ float red[2][16][kConvG];
+  __shared__ float red2[2][16][kConvG];
+  const int nch = C / kConvV, nw = (blockDim.x + 31) >> 5, c = threadIdx.x, c0 = kConvV * c;
+  const bool act = c < nch;
+  const int nseg = (T + kConvRows - 1) / kConvRows;
+  const int b = blockIdx.x / nseg, t0 = (blockIdx.x % nseg) * kConvRows;
+  const int t1 = min(T, t0 + kConvRows);
+  ConvThread th;
+  if (act) th.init(b, t0, T, C, c0, x, w, bias);
+  int parity = 0;
+  for (int tg = t0; tg < t1; tg += kConvG, parity ^= 1) {
+    float z[kConvG][kConvV], g4v[kConvG][kConvV], xt[kConvG][kConvV];
+    float ss[kConvG], sg[kConvG];
+#pragma unroll
+    for (int g = 0; g < kConvG; ++g)
+      if (act && tg + g < t1) {
+        load4(x + ((int64_t)b * T + tg + g) * C + c0, xt[g]);
+        load4(dy + ((int64_t)b * T + tg + g) * C + c0, g4v[g]);
+      }
+#pragma unroll
+    for (int g = 0; g < kConvG; ++g) {
+      ss[g] = sg[g] = 0.f;
+      if (act && tg + g < t1) {
+        th.step(xt[g], z[g]);
+#pragma unroll
+        for (int i = 0; i < kConvV; ++i) {
+          const float sv = z[g][i] * sigm(z[g][i]);
+          ss[g] += sv * sv;
+          sg[g] += sv * g4v[g][i];
         }
-        float4 *out = reinterpret_cast<float4 *>(dz + r * C + 8 * c);
-        out[0] = make_float4(o[0], o[1], o[2], o[3]);
-        out[1] = make_float4(o[4], o[5], o[6], o[7]);
       }
     }
+    float inv[kConvG], proj[kConvG];
+#pragma unroll
+    for (int g = 0; g < kConvG; ++g) {
+      inv[g] = 1.f;
+      proj[g] = 0.f;
+    }
+    if (NORM) {
+      float ta[kConvG], tb[kConvG];
+      block_sums<kConvG>(ss, ta, red, parity, nw);
+      block_sums<kConvG>(sg, tb, red2, parity, nw);
+#pragma unroll
+      for (int g = 0; g < kConvG; ++g) {
+        const float N = sqrtf(ta[g]);
+        const bool clamp = !(N > 1e-12f);
+        inv[g] = scale / (clamp ? 1e-12f : N);
+        proj[g] = clamp ? 0.f : tb[g] / ta[g];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kConvG; ++g)
+      if (act && tg + g < t1) {
+        float o[kConvV];
+#pragma unroll
+        for (int i = 0; i < kConvV; ++i) {
+          const float sgm = sigm(z[g][i]), sv = z[g][i] * sgm;
+          o[i] = inv[g] * (g4v[g][i] - sv * proj[g]) * sgm * (1.f + z[g][i] * (1.f - sgm));
+        }
+        *reinterpret_cast<float4 *>(dz + ((int64_t)b * T + tg + g) * C + c0) = make_float4(o[0], o[1], o[2], o[3]);
+      }
   }
 }
 
@@ -499,23 +567,15 @@ int kda_gated_rmsnorm_bwd(int64_t rows, int D, const void *o, const void *gate, 
 
 int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
                       void *y, int norm, float scale, void *stream) {
-  const int64_t rows = B * T;
   const int C = H * D;
-  if (H <= 0 || D <= 0 || !wide_row_ok(rows, C, {x, w, bias, y})) return KDA_ERR_INVALID_ARG;
+  if (H <= 0 || D <= 0 || C > kConvMaxC || !wide_row_ok(B * T, C, {x, w, bias, y})) return KDA_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  const int g = wide_grid(rows), kc = row_chunks(C);
+  const int threads = ((C / kConvV + 31) / 32) * 32;
+  const int grid = (int)(B * ((T + kConvRows - 1) / kConvRows));
   const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x;
   __nv_bfloat16 *yb = (__nv_bfloat16 *)y;
-#define KDA_CONV_FWD(KC)                                                                                       \
-  if (norm) conv_silu_fwd_kernel<KC, true><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale); \
-  else conv_silu_fwd_kernel<KC, false><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, yb, scale);
-  switch (kc) {
-    case 1: KDA_CONV_FWD(1) break;
-    case 2: KDA_CONV_FWD(2) break;
-    case 4: KDA_CONV_FWD(4) break;
-    default: KDA_CONV_FWD(8) break;
-  }
-#undef KDA_CONV_FWD
+  if (norm) conv_silu_fwd_kernel<true><<<grid, threads, 0, st>>>((int)B, (int)T, C, xb, w, bias, yb, scale);
+  else conv_silu_fwd_kernel<false><<<grid, threads, 0, st>>>((int)B, (int)T, C, xb, w, bias, yb, scale);
   kda::count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }
@@ -523,29 +583,22 @@ int kda_conv_silu_fwd(int64_t B, int64_t T, int H, int D, const void *x, const f
 int kda_conv_silu_bwd(int64_t B, int64_t T, int H, int D, const void *x, const float *w, const float *bias,
                       const void *dy, void *dx, float *dw, float *db, int norm, float scale, float *dz_ws,
                       void *stream) {
-  const int64_t rows = B * T;
   const int C = H * D;
-  if (H <= 0 || D <= 0 || !wide_row_ok(rows, C, {x, w, bias, dy, dx, dw, db, dz_ws})) return KDA_ERR_INVALID_ARG;
+  if (H <= 0 || D <= 0 || C > kConvMaxC || !wide_row_ok(B * T, C, {x, w, bias, dy, dx, dw, db, dz_ws}))
+    return KDA_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(dw, 0, sizeof(float) * C * 4, st) != cudaSuccess ||
       cudaMemsetAsync(db, 0, sizeof(float) * C, st) != cudaSuccess)
     return KDA_ERR_CUDA;
-  const int g = wide_grid(rows), kc = row_chunks(C);
+  const int threads = ((C / kConvV + 31) / 32) * 32;
+  const int grid = (int)(B * ((T + kConvRows - 1) / kConvRows));
   const __nv_bfloat16 *xb = (const __nv_bfloat16 *)x, *dyb = (const __nv_bfloat16 *)dy;
-#define KDA_CONV_BWD(KC)                                                                                          \
-  if (norm) conv_silu_bwd_rows_kernel<KC, true><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale); \
-  else conv_silu_bwd_rows_kernel<KC, false><<<g, kRowThreads, 0, st>>>(rows, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
-  switch (kc) {
-    case 1: KDA_CONV_BWD(1) break;
-    case 2: KDA_CONV_BWD(2) break;
-    case 4: KDA_CONV_BWD(4) break;
-    default: KDA_CONV_BWD(8) break;
-  }
-#undef KDA_CONV_BWD
+  if (norm) conv_silu_bwd_rows_kernel<true><<<grid, threads, 0, st>>>((int)B, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
+  else conv_silu_bwd_rows_kernel<false><<<grid, threads, 0, st>>>((int)B, (int)T, C, xb, w, bias, dyb, dz_ws, scale);
   kda::count_launch();
   const int seg = 64;
-  dim3 grid((C + 127) / 128, (int)((T + seg - 1) / seg), (int)B);
-  conv_bwd_cols_kernel<<<grid, 128, 0, st>>>((int)B, (int)T, C, seg, xb, w, dz_ws, (__nv_bfloat16 *)dx, dw, db);
+  dim3 grid2((C + 127) / 128, (int)((T + seg - 1) / seg), (int)B);
+  conv_bwd_cols_kernel<<<grid2, 128, 0, st>>>((int)B, (int)T, C, seg, xb, w, dz_ws, (__nv_bfloat16 *)dx, dw, db);
   kda::count_launch();
   return cudaPeekAtLastError() == cudaSuccess ? KDA_OK : KDA_ERR_CUDA;
 }

@@ -100,9 +100,9 @@ class ConvSiLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, b, H, D, norm, scale):
         x = x.contiguous()
-        if not x.is_cuda or x.dtype != torch.bfloat16 or x.shape[-1] != H * D or (H * D) % 8 or H * D > 8192:
+        if not x.is_cuda or x.dtype != torch.bfloat16 or x.shape[-1] != H * D or (H * D) % 8 or H * D > 2048:
             raise ValueError("conv_silu takes a bf16 CUDA tensor [B, T, H*D] with H*D a multiple of 8, "
-                             "at most 8192")
+                             "at most 2048")
         B, T = x.shape[0], x.shape[1]
         w32 = w.reshape(H * D, 4).to(torch.float32).contiguous()
         b32 = b.to(torch.float32).contiguous()
