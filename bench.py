@@ -308,26 +308,6 @@ def rank_shape(world, rank):
     return 1, hi - lo
 
 
-def bind_local_numa(dev):
-    """Pins this process to the host cores NVML lists as local to its GPU, so that the pinned
-    host buffers (first touch) sit on the GPU's own NUMA node.  Reads NVML only."""
-    try:
-        import pynvml
-        import torch
-        pynvml.nvmlInit()
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-        h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
-        n = os.cpu_count() or 1
-        words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
-        cpus = {64 * i + j for i, w in enumerate(words) for j in range(64) if (w >> j) & 1}
-        cpus &= os.sched_getaffinity(0)
-        if cpus:
-            os.sched_setaffinity(0, cpus)
-        return len(cpus)
-    except Exception:
-        return None
-
-
 def graph_time(fns, steps, warmup, flush, events_per_fn=False):
     """Captures each callable in ``fns`` in its own CUDA graph and replays them back to back per
     step, L2 flushed before each step; returns per-callable lists of CUDA-event milliseconds."""
@@ -413,7 +393,6 @@ def run_ours(args, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    numa_cpus = bind_local_numa(dev)
     L = _lib.lib()
     dt = torch.bfloat16
     Br, Hr = rank_shape(world, rank)
@@ -422,46 +401,8 @@ def run_ours(args, rank, world, local_rank):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
     calls = KdaCalls(L, inp, dev)
 
-    # ---- headline: fwd (saving the record) + bwd on this rank's share, CUDA graphs ----
-    c0 = L.kda_launch_counter()
-    calls.fwd()
-    calls.bwd()
-    launches_per_step = L.kda_launch_counter() - c0
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with Clocks(dev) as clk:
-        fwd_ms, bwd_ms = graph_time([calls.fwd, calls.bwd], args.steps, args.warmup, flush)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    launches = launches_per_step * args.steps
-    total_ms = max_over_ranks(sum(fwd_ms) + sum(bwd_ms), dev)
-    ms_per_step = total_ms / args.steps
-    tokens_step = B * T  # the whole problem, over all ranks
-    value = tokens_step * args.steps / (total_ms / 1e3)
-    fwd_avg = max_over_ranks(statistics.mean(fwd_ms), dev)
-    bwd_avg = max_over_ranks(statistics.mean(bwd_ms), dev)
-
-    # ---- config 1: inference forward (no saved record) on the same share ----
-    (inf_ms,) = graph_time([lambda: calls.fwd(save=False)], args.steps, args.warmup, flush)
-    inf_avg = max_over_ranks(statistics.mean(inf_ms), dev)
-
-    # ---- weak scaling (N > 1): every rank its own full B8 x H12 ----
-    weak = None
-    if world > 1:
-        winp = make_inputs_torch(B, T, H, D, seed=4321 + rank, device=dev, dtype=dt, state_std=0.1)
-        wc = KdaCalls(L, winp, dev)
-        wf, wb = graph_time([wc.fwd, wc.bwd], args.steps, args.warmup, flush)
-        wms = max_over_ranks((sum(wf) + sum(wb)) / args.steps, dev)
-        weak = {"value": round(B * T * world / (wms / 1e3), 1), "unit": UNIT, "ms_per_step": round(wms, 4),
-                "workload": "every rank its own B8 H12 T1568 (global batch 8 N)"}
-        del wc, winp
-
-    fused = fused_gates_leg(args, L, dev, inp, calls, flush)
-    streaming = streaming_d128_leg(args, L, dev, flush, rank, world)
-
-    # ---- e2e through the public API with host buffers (pinned), copies inside timing ----
+    # ---- e2e through the public API with host buffers (pinned), copies inside timing; first,
+    #      before any CUDA graph or other leg of this process ----
     # Every step copies this rank's inputs host->device, runs cuda_kda forward + autograd
     # backward and copies all outputs and gradients device->host.  Consecutive steps overlap the
     # way a data pipeline does: step i + 2's inputs go up (copy stream) and step i's results come
@@ -529,8 +470,49 @@ def run_ours(args, rank, world, local_rank):
     pipeline(args.steps, start=e0)
     e1.record(main)
     torch.cuda.synchronize()
-    e2e_value = tokens_step * args.steps / (max_over_ranks(e0.elapsed_time(e1), dev) / 1e3)
+    e2e_value = B * T * args.steps / (max_over_ranks(e0.elapsed_time(e1), dev) / 1e3)
     del dev_in, outs_host, host
+
+
+    # ---- headline: fwd (saving the record) + bwd on this rank's share, CUDA graphs ----
+    c0 = L.kda_launch_counter()
+    calls.fwd()
+    calls.bwd()
+    launches_per_step = L.kda_launch_counter() - c0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(dev) as clk:
+        fwd_ms, bwd_ms = graph_time([calls.fwd, calls.bwd], args.steps, args.warmup, flush)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = launches_per_step * args.steps
+    total_ms = max_over_ranks(sum(fwd_ms) + sum(bwd_ms), dev)
+    ms_per_step = total_ms / args.steps
+    tokens_step = B * T  # the whole problem, over all ranks
+    value = tokens_step * args.steps / (total_ms / 1e3)
+    fwd_avg = max_over_ranks(statistics.mean(fwd_ms), dev)
+    bwd_avg = max_over_ranks(statistics.mean(bwd_ms), dev)
+
+    # ---- config 1: inference forward (no saved record) on the same share ----
+    (inf_ms,) = graph_time([lambda: calls.fwd(save=False)], args.steps, args.warmup, flush)
+    inf_avg = max_over_ranks(statistics.mean(inf_ms), dev)
+
+    # ---- weak scaling (N > 1): every rank its own full B8 x H12 ----
+    weak = None
+    if world > 1:
+        winp = make_inputs_torch(B, T, H, D, seed=4321 + rank, device=dev, dtype=dt, state_std=0.1)
+        wc = KdaCalls(L, winp, dev)
+        wf, wb = graph_time([wc.fwd, wc.bwd], args.steps, args.warmup, flush)
+        wms = max_over_ranks((sum(wf) + sum(wb)) / args.steps, dev)
+        weak = {"value": round(B * T * world / (wms / 1e3), 1), "unit": UNIT, "ms_per_step": round(wms, 4),
+                "workload": "every rank its own B8 H12 T1568 (global batch 8 N)"}
+        del wc, winp
+
+
+    fused = fused_gates_leg(args, L, dev, inp, calls, flush)
+    streaming = streaming_d128_leg(args, L, dev, flush, rank, world)
 
     cfg3 = None
     if not args.skip_cfg3:
@@ -577,11 +559,10 @@ def run_ours(args, rank, world, local_rank):
         "streaming_d128": streaming,
         "cfg3": cfg3,
         "clocks": clocks,
-        "host_numa_cpus": numa_cpus,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
-                "path": "mlx_vit_b200.cuda_kda autograd fwd+bwd from pinned host buffers (on the "
-                        "GPU's NUMA node), all outputs and gradients copied back; consecutive "
+                "path": "mlx_vit_b200.cuda_kda autograd fwd+bwd from pinned host buffers, all "
+                        "outputs and gradients copied back; consecutive "
                         "steps' copies overlap compute (upload, compute, download on three "
                         "streams); per-rank bytes"},
     }
