@@ -33,6 +33,15 @@ namespace tcfwd {
 // set to a KDA_ERR_* code by a bounded wait that gave up (read by kda_device_status)
 static __device__ int g_fwd_status;
 
+// Optional event trace of the forward scan (builds with -DKDA_SCAN_TRACE only): SM clock at
+// fixed points of the first 64 chunks of (b, h) = 0, read back by kda_scan_trace().
+#ifdef KDA_SCAN_TRACE
+__device__ long long g_scan_trace[20][64];
+#define SCAN_TR(slot, c) do { if (bh == 0 && (c) < 64) g_scan_trace[slot][c] = clock64(); } while (0)
+#else
+#define SCAN_TR(slot, c) do { } while (0)
+#endif
+
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 // the block-pair factors e^{r_i - r_j} of a chunk that is not "big" stay above fp32's smallest
@@ -565,13 +574,14 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
 //     O = Qt S^T + O_intra,   Unew = U - W S^T             (Qt = Qd - P W, O_intra = P U)
 // Per chunk two MMAs read S^T: MMA1 = [Mneg; -W] S^T into accumulator D1 (rows 0-63 the state
 // product, rows 64-127 -W S^T) and MMA2 = [-W; Qt] S^T into D2 (rows 64-127 Qt S^T; rows 0-63
-// repeat -W S^T and are not read).  Both accumulators are double-buffered in TMEM (256 columns).
+// repeat -W S^T and are not read).  NB = 3 sets of both accumulators rotate in TMEM (512 columns
+// allocated), so the output roles may finish a chunk up to two chunks behind the state chain.
 // Warp roles (a warp reaches TMEM lanes 32 (warp % 4) ..):
 //   warps 0, 1, 4, 5  state rows d (lanes 0-63 of D1), warps 0-1 columns 0-31, warps 4-5
 //              columns 32-63: S <- D1 + e^{gamma_C} S + N, bf16 S^T tile for the next MMA;
 //              thread 0 then issues the next chunk's MMA1 itself (no hand-off on the chain);
-//   warps 2-3  Unew rows t (training only): D1 rows 64-127 + U;
-//   warps 6-7  O rows t: D2 rows 64-127 + O_intra;
+//   warps 2-3, 10-11  Unew rows t (training only): D1 rows 64-127 + U, columns 0-31 / 32-63;
+//   warps 6-7, 14-15  O rows t: D2 rows 64-127 + O_intra, columns 0-31 / 32-63;
 //              each of these two roles keeps a ring of NIO tiles: one thread bulk-loads the
 //              chunk's U / O_intra tile NIO - 1 chunks ahead, every thread adds its TMEM row in
 //              place, and the tile then leaves by a bulk / TMA store;
@@ -580,19 +590,20 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
 //              refilling a slot once the MMAs that read it are done.
 // Every wait is bounded; a role that gives up raises `abort`, which the others poll, and the
 // teardown drains copies, MMAs and stores before TMEM is freed.
-constexpr int NT2 = 288;
+constexpr int NT2 = 512;                       // warps 9, 12, 13 have no role
 constexpr int NREC = 4;                        // ring of chunk operand slots
 constexpr int R_MN = 0, R_W = 8192, R_QT = 16384, R_N = 24576, R_EG = 32768;
 constexpr int SLOT_BYTES = 32768 + 256;        // what one slot's copies bring
 constexpr int SLOT = 33 * 1024;                // slot stride (1024-byte aligned)
-constexpr int NST = 4;                         // bf16 S^T tiles (MMA B operand, saved-record staging)
+constexpr int NB = 3;                          // TMEM accumulator sets (D1, D2) in flight
+constexpr int NST = NB + 2;                    // bf16 S^T tiles (MMA B operand, saved-record staging)
 constexpr int NIO = 3;                         // U -> Unew and O_intra -> O tiles per role
 constexpr int OFF2_REC = 0;
 constexpr int OFF2_ST = OFF2_REC + NREC * SLOT;   // NST x 8 KB
 constexpr int OFF2_UN = OFF2_ST + NST * 8192;     // NIO x 8 KB
 constexpr int OFF2_O = OFF2_UN + NIO * 8192;      // NIO x 8 KB
-constexpr int OFF2_MBAR = OFF2_O + NIO * 8192;    // mrec[NREC] sfree[NREC] mA[2] mB[2] done[2] io[2][NIO] go2[2], TMEM slot, abort
-constexpr int NMBAR2 = 2 * NREC + 8 + 2 * NIO;
+constexpr int OFF2_MBAR = OFF2_O + NIO * 8192;    // mrec[NREC] sfree[NREC] mA[NB] mB[NB] done[NB] io[2][NIO] go2[NB], TMEM slot, abort
+constexpr int NMBAR2 = 2 * NREC + 4 * NB + 2 * NIO;
 constexpr int SMEM2 = OFF2_MBAR + 8 * NMBAR2 + 16;
 constexpr uint32_t kIdescScan = idesc_bf16(128, 64, 0, 1);  // A K-major, B MN-major
 
@@ -604,19 +615,6 @@ __device__ __forceinline__ void store_half_row_bf16(uint8_t *tile, int row, int 
         make_uint4(pack_bf16(x[8 * ch], x[8 * ch + 1]), pack_bf16(x[8 * ch + 2], x[8 * ch + 3]),
                    pack_bf16(x[8 * ch + 4], x[8 * ch + 5]), pack_bf16(x[8 * ch + 6], x[8 * ch + 7]));
 }
-// this thread's TMEM lane, 64 columns from taddr
-__device__ __forceinline__ void tmem_row64(uint32_t taddr, float *x) {
-  uint32_t v[32], w[32];
-  tmem_ld32(taddr, v);
-  tmem_ld32(taddr + 32, w);
-  tmem_wait_ld();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    x[i] = __uint_as_float(v[i]);
-    x[32 + i] = __uint_as_float(w[i]);
-  }
-}
-
 __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -627,8 +625,8 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     if (tid == 0) atomicExch(&g_fwd_status, KDA_ERR_MISALIGNED);
     return;
   }
-  const uint32_t mrec = s_base + OFF2_MBAR, sfree = mrec + 8 * NREC, mA = sfree + 8 * NREC, mB = mA + 16,
-                 done = mB + 16, mio = done + 16, go2 = mio + 16 * NIO;
+  const uint32_t mrec = s_base + OFF2_MBAR, sfree = mrec + 8 * NREC, mA = sfree + 8 * NREC, mB = mA + 8 * NB,
+                 done = mB + 8 * NB, mio = done + 8 * NB, go2 = mio + 16 * NIO;
   uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + OFF2_MBAR + 8 * NMBAR2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF2_MBAR + 8 * NMBAR2 + 4);
   const bool leader = tid == 256;
@@ -650,15 +648,13 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       mbar_init(mrec + 8 * i, 1);
       mbar_init(sfree + 8 * i, 1);
     }
-    mbar_init(mA, 1);
-    mbar_init(mA + 8, 1);
-    mbar_init(mB, 1);
-    mbar_init(mB + 8, 1);
-    mbar_init(done, 128);
-    mbar_init(done + 8, 128);
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(mA + 8 * i, 1);
+      mbar_init(mB + 8 * i, 1);
+      mbar_init(done + 8 * i, 256);
+      mbar_init(go2 + 8 * i, 1);
+    }
     for (int i = 0; i < 2 * NIO; ++i) mbar_init(mio + 8 * i, 1);
-    mbar_init(go2, 1);
-    mbar_init(go2 + 8, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -677,7 +673,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     store_half_row_bf16(sm + OFF2_ST, d, half, S);
   }
   if (warp == 8) {
-    tmem_alloc(smem_u32(tslot), 256);
+    tmem_alloc(smem_u32(tslot), 512);
     tmem_relinquish();
   }
   fence_proxy_async_smem();  // the S^T tile is read by the tensor cores
@@ -687,15 +683,21 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   const uint32_t tD = *tslot;
   const uint32_t lq = (uint32_t)(32 * (warp & 3)) << 16;  // this warp's TMEM lane quarter
   bool failed = false;
-  // MMA1 of chunk c (thread 0, on the chain): D1[c & 1] = [Mneg; -W] S^T(c); then thread 0 hands
-  // chunk c to the leader (go2), which issues MMA2: D2[c & 1] = [-W; Qt] S^T(c)
+  // MMA1 of chunk c (thread 0, on the chain): D1[c % NB] = [Mneg; -W] S^T(c); then thread 0 hands
+  // chunk c to the leader (go2), which issues MMA2: D2[c % NB] = [-W; Qt] S^T(c).  TMEM columns:
+  // D1[i] at 64 i, D2[i] at 64 (NB + i)
   auto issue_mma1 = [&](int c) {
-    const int bb = c & 1;
+    const int bb = c % NB;
     const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
     tc_fence_after();
+    SCAN_TR(2, c - 1);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
+    for (int k = 0; k < 4; ++k) {
+      tc_mma(tD + 64 * bb, desc_k(rec + R_MN, k), desc_mn(st, k), kIdescScan, k > 0);
+      if (k == 0) SCAN_TR(3, c - 1);
+    }
     tc_commit(mA + 8 * bb);
+    SCAN_TR(16, c - 1);
     mbar_arrive(go2 + 8 * bb);
   };
   if (leader) {
@@ -716,14 +718,15 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     };
     for (int c = 0; c < nc && c < NREC; ++c) issue(c);
     for (int c = 0; c < nc; ++c) {
-      const int bb = c & 1;
+      const int bb = c % NB;
       // thread 0 has written S^T(c) and issued MMA1(c) (after chunk c's operands landed)
-      bool ok = mbar_wait(go2 + 8 * bb, (c >> 1) & 1) && mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
+      bool ok = mbar_wait(go2 + 8 * bb, (c / NB) & 1) && mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
+      SCAN_TR(6, c);
       if (ok && !*abort_flag) {
         const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(tD + 128 + 64 * bb, desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
+        for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * (NB + bb), desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
         tc_commit(mB + 8 * bb);
         if (p.saved) {  // S^T(c), the chunk-entry state of the saved record
           bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedS0, st, 8192);
@@ -732,72 +735,85 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
         }
       }
       if (ok && c >= 1 && c - 1 + NREC < nc)  // chunk c - 1's slot: MMA2(c - 1) done, state reads done
-        ok = mbar_wait(mB + 8 * ((c - 1) & 1), ((c - 1) >> 1) & 1) &&
+        ok = mbar_wait(mB + 8 * ((c - 1) % NB), ((c - 1) / NB) & 1) &&
              mbar_wait(sfree + 8 * ((c - 1) % NREC), ((c - 1) / NREC) & 1);
       if (!ok || *abort_flag) {
         failed = true;
         *abort_flag = 1;
         break;
       }
+      SCAN_TR(7, c);
       if (c >= 1 && c - 1 + NREC < nc) issue(c - 1 + NREC);
     }
     if (*abort_flag)  // (bounded) the last copy issued into each slot lands before the CTA exits
       for (int c = issued > NREC ? issued - NREC : 0; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
   } else if (state_warp) {
     // ---- state rows: S <- D1 + e^{gamma_C} S + N, 32 columns per thread ----
-    if (tid == 0) {  // chunk 0's MMAs
-      if (!mbar_wait(mrec, 0)) *abort_flag = 1;
-      else issue_mma1(0);
+    // One thread per condition waits and the named-barrier vote passes the outcome on: thread 0
+    // polls MMA1(c) (the chain), thread 32 the barriers MMA1(c + 1) needs besides S^T(c + 1).
+    {
+      const bool ok0 = tid != 0 || mbar_wait(mrec, 0);  // chunk 0's operands
+      if (!bar_and(1, 128, ok0)) {
+        failed = true;
+        *abort_flag = 1;
+      } else if (tid == 0) {
+        issue_mma1(0);
+      }
     }
-    for (int c = 0; c < nc; ++c) {
-      const int bb = c & 1, s = c % NREC;
+    for (int c = 0; c < nc && !failed; ++c) {
+      const int bb = c % NB, s = c % NREC;
       const uint8_t *recm = sm + OFF2_REC + s * SLOT;
-      // one decision for the four warps (they meet at named barriers below)
-      if (!bar_and(1, 128, mbar_wait(mrec + 8 * s, (c / NREC) & 1) && mbar_wait_spin(mA + 8 * bb, (c >> 1) & 1) &&
-                              !*abort_flag)) {
+      // e^{gamma_C} S + N while MMA1(c) runs: chunk c's operands are in (vote of the step before)
+      {
+        const float e = reinterpret_cast<const float *>(recm + R_EG)[d];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const uint4 nw = *reinterpret_cast<const uint4 *>(recm + R_N + sw64(d, half + 8 * ch));
+          const uint32_t u[4] = {nw.x, nw.y, nw.z, nw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16(u[q]);
+            const int j = 8 * ch + 2 * q;
+            S[j] = fmaf(e, S[j], f.x);
+            S[j + 1] = fmaf(e, S[j + 1], f.y);
+          }
+        }
+      }
+      bool ok = true;
+      if (tid == 32 && c + 1 < nc) {
+        // D1 / D2[(c + 1) % NB] (chunk c + 1 - NB) are drained.  This also frees the tile of
+        // S^T(c + 1), which last held S^T(c + 1 - NST) = S^T(c - 1 - NB): the leader saw that
+        // state's saved-record store read its tile before it issued MMA2(c + 1 - NB), and
+        // done(c + 1 - NB) follows MMA2(c + 1 - NB).  And chunk c + 1's operands have landed.
+        if (c + 1 >= NB) ok = mbar_wait(done + 8 * ((c + 1) % NB), ((c + 1 - NB) / NB) & 1);
+        ok = ok && mbar_wait(mrec + 8 * ((c + 1) % NREC), ((c + 1) / NREC) & 1);
+      }
+      if (tid == 0) ok = mbar_wait_spin(mA + 8 * bb, (c / NB) & 1);
+      if (!bar_and(1, 128, ok && !*abort_flag)) {
         failed = true;
         *abort_flag = 1;
         break;
       }
+      if (tid == 0) SCAN_TR(0, c);
       tc_fence_after();
-      uint32_t v[32];
-      tmem_ld32(tD + 64 * bb + lq + half, v);
-      const float e = reinterpret_cast<const float *>(recm + R_EG)[d];
-      uint4 nw[4];
+      {
+        uint32_t v[32];
+        tmem_ld32(tD + 64 * bb + lq + half, v);
+        tmem_wait_ld();
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) nw[ch] = *reinterpret_cast<const uint4 *>(recm + R_N + sw64(d, half + 8 * ch));
-      tmem_wait_ld();
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        const uint32_t u[4] = {nw[ch].x, nw[ch].y, nw[ch].z, nw[ch].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = unpack_bf16(u[q]);
-          const int j = 8 * ch + 2 * q;
-          S[j] = fmaf(e, S[j], __uint_as_float(v[j]) + f.x);
-          S[j + 1] = fmaf(e, S[j + 1], __uint_as_float(v[j + 1]) + f.y);
-        }
+        for (int j = 0; j < 32; ++j) S[j] += __uint_as_float(v[j]);
       }
+      if (tid == 0) SCAN_TR(1, c);
       if (c + 1 < nc) {
-        // D1 / D2[(c + 1) & 1] (chunk c - 1) are drained.  This also frees the tile of S^T(c + 1),
-        // which last held S^T(c + 1 - NST): the leader saw that state's saved-record store read
-        // its tile before it issued MMA2(c - 1), and done(c - 1) follows MMA2(c - 1)
-        bool drained = true;
-        if (tid == 0 && c >= 1) drained = mbar_wait(done + 8 * ((c + 1) & 1), ((c - 1) >> 1) & 1);
-        bar_sync(1, 128);
         store_half_row_bf16(sm + OFF2_ST + ((c + 1) % NST) * 8192, d, half, S);
         fence_proxy_async_smem();
         tc_fence_before();
         bar_sync(1, 128);
         if (tid == 0) {
-          // chunk c + 1's operands have landed
-          const bool ok = drained && mbar_wait(mrec + 8 * ((c + 1) % NREC), ((c + 1) / NREC) & 1);
-          if (ok) {
-            issue_mma1(c + 1);
-            tc_commit(sfree + 8 * s);  // slot s (chunk c) is free once MMA1(c + 1) completes
-          } else {
-            *abort_flag = 1;
-          }
+          SCAN_TR(4, c);
+          issue_mma1(c + 1);
+          tc_commit(sfree + 8 * s);  // slot s (chunk c) is free once MMA1(c + 1) completes
+          SCAN_TR(5, c);
         }
       }
     }
@@ -805,15 +821,19 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
 #pragma unroll
       for (int j = 0; j < 32; ++j) p.stateT[(int64_t)bh * D * D + (half + j) * D + d] = S[j];
     }
-  } else if (warp < 8) {
-    // ---- warps 2-3: Unew rows (training); warps 6-7: O rows ----
-    const bool un = warp < 4;
-    const int t = 32 * (warp & 1) + lane, bar = un ? 2 : 3;
-    const bool lead = t == 0;
-    const uint32_t macc = un ? mA : mB, tcol = un ? 0 : 128, mb0 = mio + (un ? 0 : 8 * NIO);
+  } else if ((warp & 3) >= 2) {
+    // ---- warps 2-3, 10-11: Unew rows (training); warps 6-7, 14-15: O rows ----
+    const bool un = (warp & 4) == 0;
+    const int t = 32 * (warp & 1) + lane, bar = un ? 2 : 3, c0 = warp >= 8 ? 32 : 0;
+    const bool lead = t == 0 && c0 == 0;
+    const uint32_t macc = un ? mA : mB, tcol = un ? 0 : 64 * NB, mb0 = mio + (un ? 0 : 8 * NIO);
     const int src_off = un ? WS_U : WS_OI;
     const int ring = un ? OFF2_UN : OFF2_O;
+#ifdef SCAN_EXP_NO_IO
+    const bool active = false;
+#else
     const bool active = !un || p.saved;
+#endif
     int io_issued = 0;
     auto load_tile = [&](int c) {
       const int s = c % NIO;
@@ -824,9 +844,11 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     if (active && lead)
       for (int c = 0; c < nc && c < NIO - 1; ++c) load_tile(c);
     for (int c = 0; c < nc; ++c) {
-      const int bb = c & 1, s = c % NIO;
-      const bool ok = mbar_wait(macc + 8 * bb, (c >> 1) & 1) && (!active || mbar_wait(mb0 + 8 * s, (c / NIO) & 1));
-      if (!bar_and(bar, 64, ok && !*abort_flag)) {
+      const int bb = c % NB, s = c % NIO;
+      // the lead thread waits, the vote passes the outcome on
+      const bool ok = !lead || (mbar_wait(macc + 8 * bb, (c / NB) & 1) && (!active || mbar_wait(mb0 + 8 * s, (c / NIO) & 1)));
+      if (lead) SCAN_TR(un ? 8 : 10, c);
+      if (!bar_and(bar, 128, ok && !*abort_flag)) {
         failed = true;
         *abort_flag = 1;
         if (lead)  // (bounded) the last tile load issued into each slot lands before the CTA exits
@@ -836,25 +858,35 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       }
       tc_fence_after();
       if (active) {
-        float x[64];
-        tmem_row64(tD + tcol + 64 * bb + lq, x);
+        // + this thread's half row of U / O_intra, written back in place: its four 16-byte
+        // pieces are all read (while the TMEM load runs) before any is written
         uint8_t *tile = sm + ring + s * 8192;
+        uint32_t v[32];
+        tmem_ld32(tD + tcol + 64 * bb + lq + c0, v);
+        uint4 u[4];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {  // + this thread's row of U / O_intra, written back in place
-          const uint4 u = *reinterpret_cast<const uint4 *>(tile + sw64(t, 8 * ch));
-          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        for (int ch = 0; ch < 4; ++ch) u[ch] = *reinterpret_cast<const uint4 *>(tile + sw64(t, c0 + 8 * ch));
+        tmem_wait_ld();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const uint32_t uw[4] = {u[ch].x, u[ch].y, u[ch].z, u[ch].w};
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack_bf16(w[e]);
-            o[e] = pack_bf16(x[8 * ch + 2 * e] + f.x, x[8 * ch + 2 * e + 1] + f.y);
+            const int j = 8 * ch + 2 * e;
+            const float2 f = unpack_bf16(uw[e]);
+            o[e] = pack_bf16(__uint_as_float(v[j]) + f.x, __uint_as_float(v[j + 1]) + f.y);
           }
-          *reinterpret_cast<uint4 *>(tile + sw64(t, 8 * ch)) = make_uint4(o[0], o[1], o[2], o[3]);
+          u[ch] = make_uint4(o[0], o[1], o[2], o[3]);
         }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) *reinterpret_cast<uint4 *>(tile + sw64(t, c0 + 8 * ch)) = u[ch];
+        if (lead) SCAN_TR(un ? 12 : 14, c);
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(done + 8 * bb);
-        bar_sync(bar, 64);
+        if (lead) SCAN_TR(un ? 9 : 11, c);
+        bar_sync(bar, 128);
         if (lead) {
           const uint32_t src = s_base + ring + s * 8192;
           if (un)
@@ -867,6 +899,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
             bulk_wait_read<1>();
             load_tile(c + NIO - 1);
           }
+          SCAN_TR(un ? 13 : 15, c);
         }
       } else {
         tc_fence_before();
@@ -878,7 +911,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   if (failed && (leader || storer)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
   if (storer) bulk_wait_all();  // the stores this thread issued have completed
   if (tid == 0 && *abort_flag) {  // (bounded) no MMA may still write TMEM when it is freed
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NB; ++i) {
       mbar_wait(mA + 8 * i, 0);
       mbar_wait(mA + 8 * i, 1);
       mbar_wait(mB + 8 * i, 0);
@@ -888,7 +921,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) tmem_dealloc(tD, 256);
+  if (warp == 8) tmem_dealloc(tD, 512);
 }
 
 template <typename Tb>
@@ -938,3 +971,9 @@ int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st) {
 }
 
 }  // namespace kda
+
+#ifdef KDA_SCAN_TRACE
+extern "C" __attribute__((visibility("default"))) int kda_scan_trace(long long *out) {
+  return cudaMemcpyFromSymbol(out, kda::tcfwd::g_scan_trace, sizeof(long long) * 20 * 64) == cudaSuccess ? 0 : -1;
+}
+#endif
