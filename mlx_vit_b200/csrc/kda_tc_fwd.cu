@@ -585,9 +585,11 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
 //              each of these two roles keeps a ring of NIO tiles: one thread bulk-loads the
 //              chunk's U / O_intra tile NIO - 1 chunks ahead, every thread adds its TMEM row in
 //              place, and the tile then leaves by a bulk / TMA store;
-//   warp 8     one thread issues MMA2, stores S^T (the saved chunk-entry state) and keeps a ring of
-//              the chunk operands (Mneg, -W, Qt, N, e^{gamma_C}: bulk copies) NREC chunks deep,
-//              refilling a slot once the MMAs that read it are done.
+//   warp 8     one thread issues MMA2 as soon as thread 0 hands a chunk over (go2) and stores
+//              S^T (the saved chunk-entry state) from its tile;
+//   warp 9     one thread keeps the ring of chunk operands (Mneg, -W, Qt, N, e^{gamma_C}: bulk
+//              copies) NREC chunks deep, refilling a slot once the MMAs that read it are done.
+//
 // Every wait is bounded; a role that gives up raises `abort`, which the others poll, and the
 // teardown drains copies, MMAs and stores before TMEM is freed.
 constexpr int NT2 = 512;                       // warps 9, 12, 13 have no role
@@ -701,9 +703,33 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     mbar_arrive(go2 + 8 * bb);
   };
   if (leader) {
-    // ---- MMA2 of every chunk, and the operand ring: a slot is refilled once both MMAs of its
-    //      chunk are complete and the state warps have read it (thread 0 commits the next
-    //      chunk's MMA1 to sfree[slot]) ----
+    // ---- MMA2 of every chunk, issued as soon as thread 0 hands the chunk over (go2 follows
+    //      MMA1(c), which thread 0 issued after chunk c's operands were seen to land), so that
+    //      the tensor pipe runs it while the state rows are updated, not after the next MMA1 ----
+    for (int c = 0; c < nc; ++c) {
+      const int bb = c % NB;
+      const bool ok = mbar_wait_spin(go2 + 8 * bb, (c / NB) & 1);
+      SCAN_TR(6, c);
+      if (!ok || *abort_flag) {
+        failed = true;
+        *abort_flag = 1;
+        break;
+      }
+      const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * (NB + bb), desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
+      tc_commit(mB + 8 * bb);
+      if (p.saved) {  // S^T(c), the chunk-entry state of the saved record
+        bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedS0, st, 8192);
+        bulk_commit();
+        bulk_wait_read<1>();  // S^T(c - 1)'s store has read its tile (see the state warps)
+      }
+      SCAN_TR(7, c);
+    }
+  } else if (tid == 288) {
+    // ---- the operand ring: a slot is refilled once both MMAs of its chunk are complete and the
+    //      state warps have read it (thread 0 commits the next chunk's MMA1 to sfree[slot]) ----
     int issued = 0;
     auto issue = [&](int c) {
       const int s = c % NREC;
@@ -717,33 +743,14 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
       issued = c + 1;
     };
     for (int c = 0; c < nc && c < NREC; ++c) issue(c);
-    for (int c = 0; c < nc; ++c) {
-      const int bb = c % NB;
-      // thread 0 has written S^T(c) and issued MMA1(c) (after chunk c's operands landed)
-      bool ok = mbar_wait(go2 + 8 * bb, (c / NB) & 1) && mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
-      SCAN_TR(6, c);
-      if (ok && !*abort_flag) {
-        const uint32_t st = s_base + OFF2_ST + (c % NST) * 8192, rec = s_base + OFF2_REC + (c % NREC) * SLOT;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(tD + 64 * (NB + bb), desc_k(rec + R_W, k), desc_mn(st, k), kIdescScan, k > 0);
-        tc_commit(mB + 8 * bb);
-        if (p.saved) {  // S^T(c), the chunk-entry state of the saved record
-          bulk_s2g((uint8_t *)svb + (int64_t)c * kSavedChunk + kSavedS0, st, 8192);
-          bulk_commit();
-          bulk_wait_read<1>();  // S^T(c - 1)'s store has read its tile (see the state warps)
-        }
-      }
-      if (ok && c >= 1 && c - 1 + NREC < nc)  // chunk c - 1's slot: MMA2(c - 1) done, state reads done
-        ok = mbar_wait(mB + 8 * ((c - 1) % NB), ((c - 1) / NB) & 1) &&
-             mbar_wait(sfree + 8 * ((c - 1) % NREC), ((c - 1) / NREC) & 1);
+    for (int c = 0; c + NREC < nc; ++c) {
+      const bool ok = mbar_wait(mB + 8 * (c % NB), (c / NB) & 1) && mbar_wait(sfree + 8 * (c % NREC), (c / NREC) & 1);
       if (!ok || *abort_flag) {
         failed = true;
         *abort_flag = 1;
         break;
       }
-      SCAN_TR(7, c);
-      if (c >= 1 && c - 1 + NREC < nc) issue(c - 1 + NREC);
+      issue(c + NREC);
     }
     if (*abort_flag)  // (bounded) the last copy issued into each slot lands before the CTA exits
       for (int c = issued > NREC ? issued - NREC : 0; c < issued; ++c) mbar_wait(mrec + 8 * (c % NREC), (c / NREC) & 1);
@@ -908,7 +915,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     }
   }
   const bool storer = leader || tid == 64 || tid == 192;  // threads that issue bulk stores
-  if (failed && (leader || storer)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
+  if (failed && (tid == 288 || storer)) atomicExch(&g_fwd_status, KDA_ERR_TIMEOUT);
   if (storer) bulk_wait_all();  // the stores this thread issued have completed
   if (tid == 0 && *abort_flag) {  // (bounded) no MMA may still write TMEM when it is freed
     for (int i = 0; i < NB; ++i) {
