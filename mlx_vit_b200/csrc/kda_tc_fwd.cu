@@ -836,11 +836,7 @@ __global__ void __launch_bounds__(NT2, 1) kda_fwd_scan_kernel(Params p, const __
     const uint32_t macc = un ? mA : mB, tcol = un ? 0 : 64 * NB, mb0 = mio + (un ? 0 : 8 * NIO);
     const int src_off = un ? WS_U : WS_OI;
     const int ring = un ? OFF2_UN : OFF2_O;
-#ifdef SCAN_EXP_NO_IO
-    const bool active = false;
-#else
     const bool active = !un || p.saved;
-#endif
     int io_issued = 0;
     auto load_tile = [&](int c) {
       const int s = c % NIO;
