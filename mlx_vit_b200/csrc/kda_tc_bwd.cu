@@ -38,6 +38,15 @@ namespace tcbwd {
 // set to a KDA_ERR_* code by a bounded wait that gave up (read by kda_device_status)
 static __device__ int g_bwd_status;
 
+// Optional phase trace of the chunk kernel (builds with -DKDA_SCAN_TRACE only): SM clock after
+// each phase of the first 16 chunks that CTA 0 walks, read back by kda_bwd_trace().
+#ifdef KDA_SCAN_TRACE
+__device__ long long g_bwd_trace[12][16];
+#define BWD_TR(slot) do { if (tid == 0 && blockIdx.x == 0 && it < 16) g_bwd_trace[slot][it] = clock64(); } while (0)
+#else
+#define BWD_TR(slot) do { } while (0)
+#endif
+
 constexpr int C = 64, D = 64;
 constexpr float kSpanMax = 60.f;
 // the block-pair factors e^{r_i - r_j} of a chunk that is not "big" stay above fp32's smallest
@@ -288,6 +297,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     break;
   }
   const int nvalid = min(C, T - t0);
+  BWD_TR(0);
   if (tid < C)
     bet[tid] = !p.gated ? to_f(beta_next) : tid < nvalid ? p.beta_scale * sigmoid_f(to_f(beta_next)) : 0.f;
   if (p.gated) {  // g over GS; sigmoid and softplus of the gate input kept for the VJP
@@ -348,6 +358,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   if (tid == 0) bulk_wait_read_all();  // the previous chunk's output stores have read KD, QD, KF
   __syncthreads();
+  BWD_TR(1);
 
   // ---- P2: operand build: KD = k F, QD = q F, KF = k / F, KB = k e^{gamma_C - gamma}.
   //      A big chunk factors e^{gamma_t - gamma_s} (t in block i > j, the block of s) as
@@ -414,6 +425,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
 
   __syncthreads();
+  BWD_TR(2);
   // dGamma_C, state part: e^{gamma_C} sum_j S0[j,d] dS1[j,d]
   {
     const int d = tid & 63, jq = tid >> 6;
@@ -451,6 +463,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
             pack_bf16(du[nt][2 * hh], du[nt][2 * hh + 1]);
   }
   __syncthreads();
+  BWD_TR(3);
   {
     float y[2][4] = {};
 #pragma unroll
@@ -486,6 +499,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   __syncthreads();
   if (inext < nchunks) issue_loads(inext, 0);  // v, P and Tinv are dead from here on
+  BWD_TR(4);
 
   // ---- P6..P8: per warp rows 16 * mt.. and columns n0.. of dq, dk ----
   float DQ[2][4], DKp[2][4], DKm[2][4], Fv[2][4];
@@ -601,6 +615,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
   }
   __syncthreads();
   if (inext < nchunks) issue_loads(inext, 1);  // so are dO, g, S0, Unew^T, M and dS1
+  BWD_TR(5);
   // ---- P8: decayed products.  Block pairs go through the tensor cores with the factors of P2;
   //      a big chunk's diagonal block (mt, mt) is summed here with exact factors ----
   // block pairs; compiled once per case (`Big`: without the diagonal block, B_s for the columns)
@@ -678,34 +693,45 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
   };
   if (big) {
-    // this thread's own gamma, re-read from shared memory where used (register pressure)
-    auto gown = [&](int nt, int e) { return GB[gsw(16 * mt + g4 + 8 * (e >> 1), n0 + 8 * nt + 2 * c4 + (e & 1))]; };
-    // The DP / DK tiles are zero above the diagonal, so the sums run over whole row / column
-    // ranges; the clamp only keeps e^{gamma_t - gamma_s} finite where s > t.
+    // The DP / DK tiles are zero above the diagonal, so each sum runs only over the terms with
+    // s <= t: e^{gamma_t - gamma_s} <= 1 there (gamma is a running sum of g <= 0).
     auto bf = [&](int tile, int r, int c) {
       return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
     };
     const int r0 = 16 * mt + g4, r1 = r0 + 8;  // this thread's two rows
-    for (int s = 16 * mt; s <= r1; ++s) {  // dq, dk rows: sum over s <= t
-      const float dp[2] = {bf(O_DP, r0, s), bf(O_DP, r1, s)}, dk[2] = {bf(O_DK, r0, s), bf(O_DK, r1, s)};
+    float gw[2][4];                              // this thread's own gamma (log2 units)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) gw[nt][e] = GB[gsw(e < 2 ? r0 : r1, n0 + 8 * nt + 2 * c4 + (e & 1))];
+    // dq, dk rows: sum over s <= t; rows r0 and r1 for s <= r0, row r1 alone for r0 < s <= r1
+    auto rows_term = [&](int s, auto both_tag) {
+      constexpr bool Both = decltype(both_tag)::value;
+      const float dp1 = bf(O_DP, r1, s), dk1 = bf(O_DK, r1, s);
+      const float dp0 = Both ? bf(O_DP, r0, s) : 0.f, dk0 = Both ? bf(O_DK, r0, s) : 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const int d = n0 + 8 * nt + 2 * c4;
         const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s, d));
         const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s, d)));
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+        for (int hh = Both ? 0 : 1; hh < 2; ++hh)
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
             const int e = 2 * hh + x;
-            const float w = (x ? ks.y : ks.x) * exp2f(fminf(gown(nt, e) - (x ? gs.y : gs.x), 0.f));
-            DQ[nt][e] = fmaf(dp[hh], w, DQ[nt][e]);
-            DKp[nt][e] = fmaf(dk[hh], w, DKp[nt][e]);
+            const float w = (x ? ks.y : ks.x) * exp2f(gw[nt][e] - (x ? gs.y : gs.x));
+            DQ[nt][e] = fmaf(hh ? dp1 : dp0, w, DQ[nt][e]);
+            DKp[nt][e] = fmaf(hh ? dk1 : dk0, w, DKp[nt][e]);
           }
       }
-    }
-    for (int t2 = r0; t2 < 16 * mt + 16; ++t2) {  // dk columns: sum over t >= s
-      const float dp[2] = {bf(O_DP, t2, r0), bf(O_DP, t2, r1)}, dk[2] = {bf(O_DK, t2, r0), bf(O_DK, t2, r1)};
+    };
+    for (int s = 16 * mt; s <= r0; ++s) rows_term(s, std::true_type{});
+    for (int s = r0 + 1; s <= r1; ++s) rows_term(s, std::false_type{});
+    // dk columns: sum over t >= s; column r0 alone for r0 <= t < r1, columns r0 and r1 for t >= r1
+    auto cols_term = [&](int t2, auto both_tag) {
+      constexpr bool Both = decltype(both_tag)::value;
+      const float dp0 = bf(O_DP, t2, r0), dk0 = bf(O_DK, t2, r0);
+      const float dp1 = Both ? bf(O_DP, t2, r1) : 0.f, dk1 = Both ? bf(O_DK, t2, r1) : 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const int d = n0 + 8 * nt + 2 * c4;
@@ -713,15 +739,18 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
         const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t2, d)));
         const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t2, d)));
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
+        for (int hh = 0; hh < (Both ? 2 : 1); ++hh)
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
             const int e = 2 * hh + x;
-            const float w = exp2f(fminf((x ? gt.y : gt.x) - gown(nt, e), 0.f));
-            DKm[nt][e] = fmaf(dk[hh] * (x ? kt.y : kt.x) + dp[hh] * (x ? qt.y : qt.x), w, DKm[nt][e]);
+            const float w = exp2f((x ? gt.y : gt.x) - gw[nt][e]);
+            DKm[nt][e] = fmaf((hh ? dk1 : dk0) * (x ? kt.y : kt.x) + (hh ? dp1 : dp0) * (x ? qt.y : qt.x), w,
+                              DKm[nt][e]);
           }
       }
-    }
+    };
+    for (int t2 = r0; t2 < r1; ++t2) cols_term(t2, std::false_type{});
+    for (int t2 = r1; t2 < 16 * mt + 16; ++t2) cols_term(t2, std::true_type{});
     p8_pairs(std::true_type{});
   } else {
     p8_pairs(std::false_type{});
@@ -740,6 +769,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       dgm[nt][e + 1] = qv.y * DQ[nt][e + 1] + kv.y * (DKp[nt][e + 1] - DKm[nt][e + 1]);
     }
   __syncthreads();  // every warp is done with q, k and the P8 operand tiles
+  BWD_TR(6);
   if (inext < nchunks) issue_loads(inext, 2);
   // staging: dq (bf16) in KD, dk (bf16) in QD, dgamma (fp32, gsw layout) over KF and KB
   float *DG = reinterpret_cast<float *>(sm + O_KF);
@@ -829,6 +859,7 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
       atomicAdd(p.dA_log + h, sa);
     }
   }
+  BWD_TR(7);
   }  // chunk loop
   if (tid == 0) bulk_wait_all();  // shared memory stays valid until the stores have read it
 }
@@ -934,4 +965,8 @@ extern "C" int kda_bwd_noalloc(const KdaDesc *d, const void *q, const void *k, c
                  scratch, need ? (size_t)KDA_NOALLOC_SCRATCH_BYTES : 0, stream);
 }
 
-
+#ifdef KDA_SCAN_TRACE
+extern "C" __attribute__((visibility("default"))) int kda_bwd_trace(long long *out) {
+  return cudaMemcpyFromSymbol(out, kda::tcbwd::g_bwd_trace, sizeof(long long) * 12 * 16) == cudaSuccess ? 0 : -1;
+}
+#endif
