@@ -69,6 +69,15 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D += A(16x8, row) * B(8x8, col), bf16 in, fp32 accumulate; A in two registers (rows g, g + 8),
+// B in one (k = 2c, 2c + 1 of column g), with g = lane / 4, c = lane % 4
+__device__ __forceinline__ void mma1688(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
 // Lane address helpers for ldmatrix/stmatrix x4 on 64-column swizzled tiles.
 //  A fragment of the 16x16 block at (r0, k0):
 __device__ __forceinline__ uint32_t a_frag_addr(uint32_t base, int r0, int k0, int lane) {
@@ -88,6 +97,17 @@ __device__ __forceinline__ uint32_t bkn_frag_addr(uint32_t base, int k0, int n0,
 //   - equally the A fragment of X^T for rows j0..j0+15 and k = t0..t0+15.
 __device__ __forceinline__ uint32_t ct_frag_addr(uint32_t base, int t0, int j0, int lane) {
   return base + sw64(t0 + (lane & 7) + ((lane >> 4) << 3), j0 + (((lane >> 3) & 1) << 3));
+}
+// ldmatrix x2 on 64-column swizzled tiles (m16n8k8 operands):
+//  - plain: the A fragment of the 16 x 8 block at (r0, k0) of a tile stored [m][k];
+//  - with .trans, from rows r0..r0+7 and columns c0..c0+15 of a tile stored [k][x]: the A
+//    fragment of its transpose (rows c0..c0+15, k = r0..r0+7), or the B fragments of the two n8
+//    tiles c0 and c0 + 8 (k = r0..r0+7)
+__device__ __forceinline__ uint32_t a8_frag_addr(uint32_t base, int r0, int k0, int lane) {
+  return base + sw64(r0 + (lane & 15), k0);
+}
+__device__ __forceinline__ uint32_t t8_frag_addr(uint32_t base, int r0, int c0, int lane) {
+  return base + sw64(r0 + (lane & 7), c0 + (((lane >> 3) & 1) << 3));
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {

@@ -693,64 +693,152 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     }
   };
   if (big) {
-    // The DP / DK tiles are zero above the diagonal, so each sum runs only over the terms with
-    // s <= t: e^{gamma_t - gamma_s} <= 1 there (gamma is a running sum of g <= 0).
+    // A big chunk's diagonal blocks, split into 8-row halves.  The block of t in the upper half
+    // and s in the lower half goes through the tensor cores as A'_t G B'_s, every factor <= 1:
+    // A'_t = e^{gamma_t - gamma_8}, G = e^{gamma_8 - gamma_7}, B'_s = e^{gamma_7 - gamma_s} (rows
+    // 7 and 8 of the block).  The two 8 x 8 triangles on the diagonal are summed exactly, over
+    // the terms with s <= t only, where e^{gamma_t - gamma_s} <= 1 (gamma is a running sum of
+    // g <= 0; the DP / DK tiles are zero above the diagonal).
+    {  // X = k B' (lower-half rows), k A' (upper-half rows) in the dead dR tile; Y = q A' (upper-half
+       // rows) in the dead Kb tile
+      const int t = tid >> 3, d0 = (tid & 7) * 8, up = (t >> 3) & 1, rr = (t & ~15) + 7 + up;
+      const uint32_t off = sw64(t, d0);
+      const uint4 kq = *reinterpret_cast<const uint4 *>(sm + O_KS + off);
+      const uint4 qq = *reinterpret_cast<const uint4 *>(sm + O_QS + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+      uint32_t ox[4], oy[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d0 + 2 * e;
+        const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t, d));
+        const float2 gr = *reinterpret_cast<const float2 *>(GB + gsw(rr, d));
+        const float f0 = exp2f(up ? gt.x - gr.x : gr.x - gt.x), f1 = exp2f(up ? gt.y - gr.y : gr.y - gt.y);
+        const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
+        ox[e] = pack_bf16(kf.x * f0, kf.y * f1);
+        oy[e] = pack_bf16(qf.x * f0, qf.y * f1);
+      }
+      *reinterpret_cast<uint4 *>(sm + O_DR + off) = make_uint4(ox[0], ox[1], ox[2], ox[3]);
+      if (up) *reinterpret_cast<uint4 *>(sm + O_KB + off) = make_uint4(oy[0], oy[1], oy[2], oy[3]);
+    }
+    __syncthreads();
+    BWD_TR(8);
     auto bf = [&](int tile, int r, int c) {
       return __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(sm + tile + sw64(r, c)));
     };
-    const int r0 = 16 * mt + g4, r1 = r0 + 8;  // this thread's two rows
+    const int r0 = 16 * mt + g4, r1 = r0 + 8;  // this thread's two rows: lower and upper half
     float gw[2][4];                              // this thread's own gamma (log2 units)
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) gw[nt][e] = GB[gsw(e < 2 ? r0 : r1, n0 + 8 * nt + 2 * c4 + (e & 1))];
-    // dq, dk rows: sum over s <= t; rows r0 and r1 for s <= r0, row r1 alone for r0 < s <= r1
-    auto rows_term = [&](int s, auto both_tag) {
-      constexpr bool Both = decltype(both_tag)::value;
-      const float dp1 = bf(O_DP, r1, s), dk1 = bf(O_DK, r1, s);
-      const float dp0 = Both ? bf(O_DP, r0, s) : 0.f, dk0 = Both ? bf(O_DK, r0, s) : 0.f;
+    {  // rows t = r1 over s in the lower half: dq += A'G (dP X), dk_row += A'G (dKK X)
+      float T1[2][4] = {}, T2[2][4] = {};
+      uint32_t aP[2], aK[2], bX[2];
+      ldsm_x2(a8_frag_addr(s_base + O_DP, 16 * mt, 16 * mt, lane), aP);
+      ldsm_x2(a8_frag_addr(s_base + O_DK, 16 * mt, 16 * mt, lane), aK);
+      ldsm_x2_t(t8_frag_addr(s_base + O_DR, 16 * mt, n0, lane), bX);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const int d = n0 + 8 * nt + 2 * c4;
-        const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s, d));
-        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s, d)));
-#pragma unroll
-        for (int hh = Both ? 0 : 1; hh < 2; ++hh)
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            const int e = 2 * hh + x;
-            const float w = (x ? ks.y : ks.x) * exp2f(gw[nt][e] - (x ? gs.y : gs.x));
-            DQ[nt][e] = fmaf(hh ? dp1 : dp0, w, DQ[nt][e]);
-            DKp[nt][e] = fmaf(hh ? dk1 : dk0, w, DKp[nt][e]);
-          }
+        mma1688(T1[nt], aP[0], aP[1], bX[nt]);
+        mma1688(T2[nt], aK[0], aK[1], bX[nt]);
       }
-    };
-    for (int s = 16 * mt; s <= r0; ++s) rows_term(s, std::true_type{});
-    for (int s = r0 + 1; s <= r1; ++s) rows_term(s, std::false_type{});
-    // dk columns: sum over t >= s; column r0 alone for r0 <= t < r1, columns r0 and r1 for t >= r1
-    auto cols_term = [&](int t2, auto both_tag) {
-      constexpr bool Both = decltype(both_tag)::value;
-      const float dp0 = bf(O_DP, t2, r0), dk0 = bf(O_DK, t2, r0);
-      const float dp1 = Both ? bf(O_DP, t2, r1) : 0.f, dk1 = Both ? bf(O_DK, t2, r1) : 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float ag = exp2f(gw[nt][2 + x] - GB[gsw(16 * mt + 7, n0 + 8 * nt + 2 * c4 + x)]);
+          DQ[nt][2 + x] = fmaf(ag, T1[nt][2 + x], DQ[nt][2 + x]);
+          DKp[nt][2 + x] = fmaf(ag, T2[nt][2 + x], DKp[nt][2 + x]);
+        }
+    }
+    {  // columns s = r0 over t in the upper half: dk_col += G B' (dKK^T X + dP^T Y)
+      float T3[2][4] = {};
+      uint32_t aK[2], aP[2], bX[2], bY[2];
+      ldsm_x2_t(t8_frag_addr(s_base + O_DK, 16 * mt + 8, 16 * mt, lane), aK);
+      ldsm_x2_t(t8_frag_addr(s_base + O_DP, 16 * mt + 8, 16 * mt, lane), aP);
+      ldsm_x2_t(t8_frag_addr(s_base + O_DR, 16 * mt + 8, n0, lane), bX);
+      ldsm_x2_t(t8_frag_addr(s_base + O_KB, 16 * mt + 8, n0, lane), bY);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const int d = n0 + 8 * nt + 2 * c4;
-        const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t2, d));
-        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t2, d)));
-        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t2, d)));
+        mma1688(T3[nt], aK[0], aK[1], bX[nt]);
+        mma1688(T3[nt], aP[0], aP[1], bY[nt]);
+      }
 #pragma unroll
-        for (int hh = 0; hh < (Both ? 2 : 1); ++hh)
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          const float bg = exp2f(GB[gsw(16 * mt + 8, n0 + 8 * nt + 2 * c4 + x)] - gw[nt][x]);
+          DKm[nt][x] = fmaf(bg, T3[nt][x], DKm[nt][x]);
+        }
+    }
+    BWD_TR(9);
+    // The triangles, exactly, balanced over the lanes: lane row g (g = g4) takes lower-half row
+    // 16 mt + g (g + 1 terms) and upper-half row tu = 16 mt + 15 - g (8 - g terms), nine steps on
+    // every lane; the upper row's sums belong to lane row 7 - g, which holds tu's fragments, and
+    // move there by one shuffle (lane ^ 28).
+    const int tu = 16 * mt + 15 - g4;
+    {  // dq, dk rows over s <= t in t's half
+      float TQ[2][2] = {}, TK[2][2] = {};
+#pragma unroll
+      for (int j = 0; j < 9; ++j) {
+        const bool lo = j <= g4;
+        const int t = lo ? r0 : tu, s = lo ? 16 * mt + j : 16 * mt + 7 + j - g4;
+        const float dp = bf(O_DP, t, s), dk = bf(O_DK, t, s);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int d = n0 + 8 * nt + 2 * c4;
+          const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t, d));
+          const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(s, d));
+          const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(s, d)));
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            const int e = 2 * hh + x;
-            const float w = exp2f((x ? gt.y : gt.x) - gw[nt][e]);
-            DKm[nt][e] = fmaf((hh ? dk1 : dk0) * (x ? kt.y : kt.x) + (hh ? dp1 : dp0) * (x ? qt.y : qt.x), w,
-                              DKm[nt][e]);
+            const float w = (x ? ks.y : ks.x) * exp2f((x ? gt.y : gt.x) - (x ? gs.y : gs.x));
+            const float wl = lo ? w : 0.f, wh = lo ? 0.f : w;
+            DQ[nt][x] = fmaf(dp, wl, DQ[nt][x]);
+            DKp[nt][x] = fmaf(dk, wl, DKp[nt][x]);
+            TQ[nt][x] = fmaf(dp, wh, TQ[nt][x]);
+            TK[nt][x] = fmaf(dk, wh, TK[nt][x]);
           }
+        }
       }
-    };
-    for (int t2 = r0; t2 < r1; ++t2) cols_term(t2, std::false_type{});
-    for (int t2 = r1; t2 < 16 * mt + 16; ++t2) cols_term(t2, std::true_type{});
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          DQ[nt][2 + x] += __shfl_xor_sync(0xffffffffu, TQ[nt][x], 28);
+          DKp[nt][2 + x] += __shfl_xor_sync(0xffffffffu, TK[nt][x], 28);
+        }
+    }
+    BWD_TR(10);
+    {  // dk columns over t >= s in s's half: column 16 mt + g (8 - g terms), column tu (g + 1 terms)
+      float TM[2][2] = {};
+#pragma unroll
+      for (int j = 0; j < 9; ++j) {
+        const bool lo = j < 8 - g4;
+        const int sc = lo ? r0 : tu, t = lo ? r0 + j : tu + j - (8 - g4);
+        const float dp = bf(O_DP, t, sc), dk = bf(O_DK, t, sc);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int d = n0 + 8 * nt + 2 * c4;
+          const float2 gt = *reinterpret_cast<const float2 *>(GB + gsw(t, d));
+          const float2 gs = *reinterpret_cast<const float2 *>(GB + gsw(sc, d));
+          const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_KS + sw64(t, d)));
+          const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + O_QS + sw64(t, d)));
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const float v = (dk * (x ? kt.y : kt.x) + dp * (x ? qt.y : qt.x)) *
+                            exp2f((x ? gt.y : gt.x) - (x ? gs.y : gs.x));
+            DKm[nt][x] += lo ? v : 0.f;
+            TM[nt][x] += lo ? 0.f : v;
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) DKm[nt][2 + x] += __shfl_xor_sync(0xffffffffu, TM[nt][x], 28);
+    }
+    BWD_TR(11);
     p8_pairs(std::true_type{});
   } else {
     p8_pairs(std::false_type{});
