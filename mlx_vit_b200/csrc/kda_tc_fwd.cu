@@ -38,8 +38,11 @@ static __device__ int g_fwd_status;
 #ifdef KDA_SCAN_TRACE
 __device__ long long g_scan_trace[20][64];
 #define SCAN_TR(slot, c) do { if (bh == 0 && (c) < 64) g_scan_trace[slot][c] = clock64(); } while (0)
+__device__ long long g_chunk_trace[12][64];
+#define CHUNK_TR(slot) do { if (threadIdx.x == 0 && (int)blockIdx.x < 64) g_chunk_trace[slot][blockIdx.x] = clock64(); } while (0)
 #else
 #define SCAN_TR(slot, c) do { } while (0)
+#define CHUNK_TR(slot) do { } while (0)
 #endif
 
 constexpr int C = 64, D = 64;
@@ -190,6 +193,7 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     gate_to_g(sm + R_GS, GS, p.A_log, p.dt_bias, h, nvalid, tid + NT1, true);
   }
   __syncthreads();
+  CHUNK_TR(0);
 
   // ---- (1a) gamma = cumsum(g): 4 segments of 16 rows per channel ----
   {
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     if (lane == 0) flag[warp] = any;
   }
   __syncthreads();
+  CHUNK_TR(1);
   const bool big = flag[0] | flag[1];
   // per-block vectors, item (slot, d): slot i < 4 -> block i's entries, slot 4 -> gamma_C
   for (int u = tid; u < 320; u += NT1) {
@@ -246,45 +251,118 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     }
   }
   __syncthreads();
+  CHUNK_TR(2);
 
-  // exact diagonal blocks of M and P for a "big" chunk (per-element decay factors, from the raw
-  // q / k tiles, so before the operand build reuses them): the 136 pairs s <= t of each block,
-  // each summed over d by four adjacent lanes (16 channels each); the pair's lane for channels
-  // 0-15 also zeroes the mirror entry above the diagonal
+  // diagonal blocks of M and P for a "big" chunk, from the raw q / k tiles (so before the operand
+  // build reuses them), each 16-row block split into 8-row halves:
+  //  - t in the upper half, s in the lower half: e^{gamma_t - gamma_s} = A_t B_s with A_t =
+  //    e^{gamma_t - gamma_8} and B_s = e^{gamma_8 - gamma_s} (row 8 of the block), both <= 1, so
+  //    this quadrant is a tensor-core product of X = k A (upper rows) / k B (lower rows) and
+  //    Y = q A (upper rows), built in the Qd / -W tiles that the operand build fills later;
+  //  - t in the lower half, s in the upper half: zero (above the diagonal);
+  //  - the two 8 x 8 triangles on the diagonal: exact, per-element factors (s <= t, so <= 1).
   if (big) {
-    for (int item = tid; item < 4 * 136 * 4; item += NT1) {
-      const int qd = item & 3, pr = item >> 2, i = pr / 136, pi = pr - i * 136;
-      int tl = (int)((sqrtf(8.f * pi + 1.f) - 1.f) * 0.5f);
-      tl += (tl + 1) * (tl + 2) / 2 <= pi;
-      tl -= tl * (tl + 1) / 2 > pi;
-      const int sl = pi - tl * (tl + 1) / 2, t = 16 * i + tl, s = 16 * i + sl;
-      float mk = 0.f, mq = 0.f;
-#pragma unroll 4
-      for (int d = 16 * qd; d < 16 * qd + 16; d += 2) {
-        const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(t, d)));
-        const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_QS + sw64(t, d)));
-        const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(s, d)));
+    uint8_t *XT = hom + HO_QD, *YT = hom + HO_W;
+    for (int u = tid; u < 512; u += NT1) {
+      const int t = u >> 3, d0 = (u & 7) * 8, up = (t >> 3) & 1, rr = (t & ~15) + 8;
+      const uint32_t off = sw64(t, d0);
+      const uint4 kq = *reinterpret_cast<const uint4 *>(sm + R_KS + off);
+      const uint4 qq = *reinterpret_cast<const uint4 *>(sm + R_QS + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+      uint32_t ox[4], oy[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = d0 + 2 * e;
         const float2 gt = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
-        const float2 gs = *reinterpret_cast<const float2 *>(GS + gsw(s, d));
-        const float e0 = __expf(gt.x - gs.x), e1 = __expf(gt.y - gs.y);
-        mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
-        mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
+        const float2 gr = *reinterpret_cast<const float2 *>(GS + gsw(rr, d));
+        const float f0 = __expf(up ? gt.x - gr.x : gr.x - gt.x), f1 = __expf(up ? gt.y - gr.y : gr.y - gt.y);
+        const float2 kf = unpack_bf16(kw[e]), qf = unpack_bf16(qw[e]);
+        ox[e] = pack_bf16(kf.x * f0, kf.y * f1);
+        oy[e] = pack_bf16(qf.x * f0, qf.y * f1);
       }
-      mk += __shfl_xor_sync(0xffffffffu, mk, 1);
-      mq += __shfl_xor_sync(0xffffffffu, mq, 1);
-      mk += __shfl_xor_sync(0xffffffffu, mk, 2);
-      mq += __shfl_xor_sync(0xffffffffu, mq, 2);
-      if (qd == 0) {
-        AD[i * 256 + tl * 16 + sl] = s < t ? bet[t] * mk : 0.f;
+      *reinterpret_cast<uint4 *>(XT + off) = make_uint4(ox[0], ox[1], ox[2], ox[3]);
+      if (up) *reinterpret_cast<uint4 *>(YT + off) = make_uint4(oy[0], oy[1], oy[2], oy[3]);
+    }
+    __syncthreads();
+    CHUNK_TR(9);
+    {  // warp (block i, M or P): the quadrant t upper / s lower, and the zero quadrant above it
+      const int i = warp >> 1, isP = warp & 1;
+      float acc[4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t af[4], bf[2];
+        ldsm_x4(a_frag_addr(ho + (isP ? HO_W : HO_QD), 16 * i, 16 * kk, lane), af);
+        ldsm_x2(t8_frag_addr(ho + HO_QD, 16 * i, 16 * kk, lane), bf);  // X rows s, k = d
+        mma16816(acc, af, bf[0], bf[1]);
+      }
+      const int tl = 8 + g4, t = 16 * i + tl, sl = 2 * c4;  // rows g4 + 8 of the fragment
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const float v = acc[2 + x];
+        if (isP) {
+          *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, 16 * i + sl + x)) = __float2bfloat16_rn(v);
+          *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(16 * i + sl + x, t)) = __float2bfloat16_rn(0.f);
+        } else {
+          AD[i * 256 + tl * 16 + sl + x] = bet[t] * v;
+          AD[i * 256 + (sl + x) * 16 + tl] = 0.f;
+          *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(t, 16 * i + sl + x)) = __float2bfloat16_rn(v);
+          *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(16 * i + sl + x, t)) = __float2bfloat16_rn(0.f);
+        }
+      }
+    }
+    CHUNK_TR(10);
+    {  // warp w: the triangle of half w & 1 of block w >> 1 (36 pairs t >= s).  Lane l sums pair
+       // l over all 64 channels; a column read then touches one address per row, each row in
+       // its own bank (or the same address: broadcast).  The last four pairs (row 7, columns
+       // 4-7) take eight lanes each, one eighth of the channels per lane.
+      const int i = warp >> 1, hb = 16 * i + 8 * (warp & 1);
+      auto store = [&](int t, int s, float mk, float mq, bool mirror) {
+        const int tb = t - 16 * i, sb = s - 16 * i;  // positions in the 16 x 16 block
+        AD[i * 256 + tb * 16 + sb] = s < t ? bet[t] * mk : 0.f;
         *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(t, s)) = __float2bfloat16_rn(s < t ? mk : 0.f);
         *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(t, s)) = __float2bfloat16_rn(mq);
-      } else if (qd == 1 && sl < tl) {  // the mirror (sl, tl) above the diagonal
-        AD[i * 256 + sl * 16 + tl] = 0.f;
-        *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(s, t)) = __float2bfloat16_rn(0.f);
-        *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(s, t)) = __float2bfloat16_rn(0.f);
+        if (mirror && s < t) {  // the mirror (s, t) above the diagonal
+          AD[i * 256 + sb * 16 + tb] = 0.f;
+          *reinterpret_cast<__nv_bfloat16 *>(sm + R_MK + sw64(s, t)) = __float2bfloat16_rn(0.f);
+          *reinterpret_cast<__nv_bfloat16 *>(hom + HO_P + sw64(s, t)) = __float2bfloat16_rn(0.f);
+        }
+      };
+      auto dot = [&](int t, int s, int d0, int nd, float &mk, float &mq) {
+#pragma unroll 8
+        for (int d = d0; d < d0 + nd; d += 2) {
+          const float2 kt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(t, d)));
+          const float2 qt = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_QS + sw64(t, d)));
+          const float2 ks = unpack_bf16(*reinterpret_cast<const uint32_t *>(sm + R_KS + sw64(s, d)));
+          const float2 gt = *reinterpret_cast<const float2 *>(GS + gsw(t, d));
+          const float2 gs = *reinterpret_cast<const float2 *>(GS + gsw(s, d));
+          const float e0 = __expf(gt.x - gs.x), e1 = __expf(gt.y - gs.y);
+          mk = fmaf(kt.x * ks.x, e0, fmaf(kt.y * ks.y, e1, mk));
+          mq = fmaf(qt.x * ks.x, e0, fmaf(qt.y * ks.y, e1, mq));
+        }
+      };
+      {  // pairs 0-31: row tl, column sl with lane = tl (tl + 1) / 2 + sl
+        int tl = (int)((sqrtf(8.f * lane + 1.f) - 1.f) * 0.5f);
+        tl += (tl + 1) * (tl + 2) / 2 <= lane;
+        tl -= tl * (tl + 1) / 2 > lane;
+        const int sl = lane - tl * (tl + 1) / 2;
+        float mk = 0.f, mq = 0.f;
+        dot(hb + tl, hb + sl, 0, 64, mk, mq);
+        store(hb + tl, hb + sl, mk, mq, true);
+      }
+      {  // pairs 32-35: row 7, columns 4 + (lane >> 3)
+        const int e8 = lane & 7, t = hb + 7, s = hb + 4 + (lane >> 3);
+        float mk = 0.f, mq = 0.f;
+        dot(t, s, 8 * e8, 8, mk, mq);
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          mk += __shfl_xor_sync(0xffffffffu, mk, o);
+          mq += __shfl_xor_sync(0xffffffffu, mq, o);
+        }
+        if (e8 == 0) store(t, s, mk, mq, true);
       }
     }
     __syncthreads();
+    CHUNK_TR(3);
   }
 
   // ---- (1b) operand build: 512 units of (row t, 8 consecutive channels), two per thread; all
@@ -362,6 +440,7 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     }
   }
   __syncthreads();
+  CHUNK_TR(4);
 
   // ---- (2) M = Kdec Kinc^T and P = Qdec Kinc^T per (block row i, block column j <= i), and
   //      (3) T_ii = (I + A_ii)^{-1}.  Warps 0-3 take the diagonal M block i = warp and invert it
@@ -447,11 +526,13 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     for (int q = warp - 4; q < 12; q += 4) mp_task(q);
   }
   __syncthreads();
+  CHUNK_TR(5);
 
   // ---- (4) Tinv = (I+A)^{-1} (into the Kdec tile): block forward substitution on the identity,
   //      8 columns per warp (the rows above a column's diagonal block are zero and skipped) ----
   solve_columns(sm, s_base, warp * 8, warp >> 1, warp, lane);
   __syncthreads();
+  CHUNK_TR(6);
   // ---- (5) W = Tinv beta Kd (stored negated) and U = Tinv beta V as one block-triangular GEMM;
   //      warp w takes 16 of the 128 columns of [W | U] for all four row blocks ----
   {
@@ -481,6 +562,7 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
     }
   }
   __syncthreads();
+  CHUNK_TR(7);
   // ---- (6) the state-independent products the scan and the backward need, 16 tasks of 16 rows
   //      x 64 columns, two per warp:
   //        [Mneg | N]       = Kb^T [-W | U]          (tasks 0-7, rows d)
@@ -536,6 +618,7 @@ __global__ void __launch_bounds__(NT1, 2) kda_fwd_chunks_kernel(Params p, const 
   }
   fence_proxy_async_smem();  // make this thread's smem writes visible to the bulk copies
   __syncthreads();
+  CHUNK_TR(8);
   // ---- the scan's record (ws) and, for training, the backward's record (saved): bulk copies
   //      of the swizzled tiles as they lie in shared memory ----
   if (tid == 0) {
@@ -976,6 +1059,9 @@ int tc_fwd(const Params &p, int dtype_beta, cudaStream_t st) {
 }  // namespace kda
 
 #ifdef KDA_SCAN_TRACE
+extern "C" __attribute__((visibility("default"))) int kda_chunk_trace(long long *out) {
+  return cudaMemcpyFromSymbol(out, kda::tcfwd::g_chunk_trace, sizeof(long long) * 12 * 64) == cudaSuccess ? 0 : -1;
+}
 extern "C" __attribute__((visibility("default"))) int kda_scan_trace(long long *out) {
   return cudaMemcpyFromSymbol(out, kda::tcfwd::g_scan_trace, sizeof(long long) * 20 * 64) == cudaSuccess ? 0 : -1;
 }
