@@ -130,6 +130,20 @@ def test_strong_decay_stays_finite(cuda):
         assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))
 
 
+@pytest.mark.parametrize("T", [5, 77, 141])
+def test_strong_decay_ragged_tails(cuda, T):
+    """Strong decays (every chunk "big": diagonal blocks split into 8-row halves, the lower-left
+    half block on the tensor cores, the triangles exact) with the last chunk ending inside the
+    first or the second half of a 16-row block, and a single short chunk."""
+    inp = make_inputs(2, T, 2, 64, seed=T + 3, state_std=0.1)
+    inp["g"] = (inp["g"] * 30.0).astype(np.float32)  # about -20 per step: big even at T = 5
+    ref = O.fwd_bwd(rounded_inputs(inp, torch.bfloat16), dtype=np.float64)
+    got = run_fwd_bwd(to_dev(inp, cuda, torch.bfloat16), 64)
+    for k in OUT_KEYS:
+        assert np.isfinite(got[k]).all(), k
+        assert rel_err(got[k], ref[k]) <= TOL_BF16, (k, rel_err(got[k], ref[k]))
+
+
 def test_realistic_gate_decays_mixed_per_head(cuda):
     """Per-head decay scales like the reference's gate init (A = e^{A_log} in [1, 16], so
     g = -A softplus(.) reaches -10 per step and gamma spans of -80 or more within a chunk):
