@@ -17,7 +17,8 @@ run, on the GPU box or by the test-suite).  It
 
 Inputs are not stored: the tests rebuild them from the seed and compare the checksum.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
+Usage:  python tests/golden/make_golden.py /path/to/reference
+        (or with the reference checkout's directory in KDA_REFERENCE_DIR)
 """
 from __future__ import annotations
 
@@ -103,7 +104,9 @@ def run_case(ref, B, T, H, D, seed, state_std):
 
 
 def main():
-    ref_dir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_dir = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KDA_REFERENCE_DIR")
+    if not ref_dir:
+        sys.exit("usage: make_golden.py /path/to/reference (the checkout holding nope_gdn_mlx.py)")
     mlx_emul.install(torch.float64)
     spec = importlib.util.spec_from_file_location("nope_gdn_mlx", os.path.join(ref_dir, "nope_gdn_mlx.py"))
     ref = importlib.util.module_from_spec(spec)
