@@ -214,6 +214,18 @@ constexpr int O_MBAR = O_VEC + (V_FLAG + 4) * 4;                    // three mba
 constexpr int CK_SMEM = O_MBAR + 24;
 constexpr int CK_SMEM_GP = (CK_SMEM + 15) & ~15;                  // staged gate parameters
 
+// out[r] = in[(r - s) mod 8] for a run-time s in [0, 8): three conditional rotations, so that the
+// arrays stay in registers
+__device__ __forceinline__ void rot8(const float (&in)[8], float (&out)[8], int s) {
+  float a[8], b[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) a[r] = (s & 1) ? in[(r + 7) & 7] : in[r];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) b[r] = (s & 2) ? a[(r + 6) & 7] : a[r];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) out[r] = (s & 4) ? b[(r + 4) & 7] : b[r];
+}
+
 template <typename Tb>
 __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, const __grid_constant__ TmaMaps tm) {
   extern __shared__ __align__(1024) uint8_t sm[];
@@ -305,33 +317,44 @@ __global__ void __launch_bounds__(CK_NT, 1) kda_bwd_chunks_kernel(Params p, cons
     __syncthreads();
   }
   if (inext < nchunks && tid < C) beta_next = load_beta(inext);
-  // ---- P1: gamma = cumsum(g) (8 segments of 8 rows per channel), guard, per-block vectors ----
+  // ---- P1: gamma = cumsum(g) per channel without a CTA barrier: warp w owns channels 4 w ..
+  //      4 w + 3, lane (segment sg = lane / 4 of 8 rows, channel 4 w + lane % 4) adds up its
+  //      segment in registers, and the segments' offsets come from a shuffle scan.  Lane sg
+  //      visits its rows rotated by sg, so that the 8 lanes of a channel read and write 8 different
+  //      swizzle phases (no bank conflicts).  The big-chunk guard comes from the same registers ----
+  int bigloc;
   {
-    const int d = tid & 63, seg = tid >> 6;
-    float acc = 0.f;
+    const int sg = lane >> 2, d = 4 * warp + (lane & 3);
+    float v[8], w[8], q[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) acc += GS[gsw(seg * 8 + r, d)];
-    part[seg * 64 + d] = acc;
-    __syncthreads();
-    float off = 0.f;
-    for (int s2 = 0; s2 < seg; ++s2) off += part[s2 * 64 + d];
+    for (int k = 0; k < 8; ++k) v[k] = GS[gsw(8 * sg + ((k + sg) & 7), d)];  // row 8 sg + (k + sg) % 8
+    rot8(v, w, sg);  // w[r]: row 8 sg + r
+    float tot = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) tot += w[r];
+    float inc = tot;
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      const float x = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += x;
+    }
+    float run = inc - tot;  // the segments before this one
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      off += GS[gsw(seg * 8 + r, d)];
-      GS[gsw(seg * 8 + r, d)] = off;
+      run += w[r];
+      w[r] = run;
     }
-    __syncthreads();
-  }
-  int bigloc = 0;
-  if (tid < 64) {
-    float span = 0.f;
+    rot8(w, q, (8 - sg) & 7);  // back to the visiting order
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      span = fmaxf(span, GS[gsw(i * 16, tid)] - GS[gsw(i * 16 + 8, tid)]);
-      span = fmaxf(span, GS[gsw(i * 16 + 8, tid)] - GS[gsw(i * 16 + 15, tid)]);
-    }
-    if (!(GS[gsw(8, tid)] - GS[gsw(56, tid)] <= kMidGapMax)) span = 2.f * kSpanMax;
-    bigloc = !(span <= kSpanMax);
+    for (int k = 0; k < 8; ++k) GS[gsw(8 * sg + ((k + sg) & 7), d)] = q[k];
+    // guard: gamma may move at most kSpanMax across either half of a 16-row block (rows 0-8 and
+    // 8-15 of block i: lanes of the odd segment 2 i + 1 see both), and at most kMidGapMax between
+    // rows 8 and 56 (the block-pair factors), or the chunk is "big"
+    const float g_prev = __shfl_up_sync(0xffffffffu, w[0], 4);  // first row of the segment before
+    const float g8 = __shfl_sync(0xffffffffu, w[0], 4 + (lane & 3));
+    const float g56 = __shfl_sync(0xffffffffu, w[0], 28 + (lane & 3));
+    const float span = (sg & 1) ? fmaxf(g_prev - w[0], w[0] - w[7]) : 0.f;
+    bigloc = !(span <= kSpanMax) || !(g8 - g56 <= kMidGapMax);
   }
   // a "big" chunk (decay too strong for the factored form) keeps gamma itself and takes exact
   // per-element decay factors in P2, P6 and P8; everything else is the same
